@@ -1,0 +1,161 @@
+/*
+ * pagedkv.h — C ABI of the B200 (sm_100a) paged KV-cache decode path.
+ *
+ * Three operations make up the path:
+ *   1. batched GQA decode attention that reads K/V through a block table,
+ *   2. the per-step KV append into the [num_blocks, block_size, kv_heads,
+ *      head_dim] pool through a slot mapping,
+ *   3. the copy-on-write block copy behind the prefix cache.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes
+ * and a CUDA stream handle (cudaStream_t passed as void*). Nothing here
+ * allocates device memory except where stated; nothing synchronises the host
+ * except pagedkv_read_error_flags(). All launches go to the given stream.
+ *
+ * Return value: PAGEDKV_OK (0) or one of the PAGEDKV_ERR_* codes below; the
+ * calling thread's last message is available from pagedkv_last_error().
+ *
+ * Pool layout (shared by all entry points, identical to the reference's
+ * PhysicalBlockPool, engine/memory/block_allocator.py:68-101): one K and one V
+ * tensor per layer, each contiguous with shape
+ *   [num_blocks, block_size, num_kv_heads, head_dim]
+ * so token slot s = block_id * block_size + offset starts at element
+ *   s * num_kv_heads * head_dim.
+ * Byte offsets are computed in 64 bits; a pool tensor may exceed 2^31 bytes.
+ */
+#ifndef PAGEDKV_H_
+#define PAGEDKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define PAGEDKV_OK                    0
+#define PAGEDKV_ERR_INVALID_ARGUMENT  1  /* shape / pointer / alignment check failed */
+#define PAGEDKV_ERR_UNSUPPORTED       2  /* head_dim or dtype outside the built kernels */
+#define PAGEDKV_ERR_CUDA              3  /* a CUDA runtime call failed */
+#define PAGEDKV_ERR_WORKSPACE         4  /* workspace missing or too small */
+
+/* ---- element types ------------------------------------------------------ */
+#define PAGEDKV_DTYPE_F16   0
+#define PAGEDKV_DTYPE_BF16  1
+
+/* ---- device error word bits (set by kernels, read by pagedkv_read_error_flags) */
+#define PAGEDKV_EFLAG_BLOCK_ID_RANGE  0x1u  /* a block-table entry >= num_blocks or < 0 */
+#define PAGEDKV_EFLAG_SLOT_RANGE      0x2u  /* a slot >= num_blocks * block_size */
+#define PAGEDKV_EFLAG_SEQ_LEN_RANGE   0x4u  /* seq_len > max_blocks_per_seq * block_size */
+#define PAGEDKV_EFLAG_COPY_RANGE      0x8u  /* a copy_blocks src/dst outside [0, num_blocks) */
+#define PAGEDKV_EFLAG_PIPE_TIMEOUT    0x10u /* a bounded pipeline wait gave up */
+
+/* Library version string, e.g. "pagedkv-b200 0.1.0 sm_100a". */
+const char *pagedkv_version(void);
+
+/* Message for the last non-zero status returned on the calling thread. */
+const char *pagedkv_last_error(void);
+
+/*
+ * Decode attention, batched over sequences (one new query token each).
+ *
+ * Replaces the launch of _paged_attention_decode_batched_kernel inside
+ * paged_attention_decode_batched (engine/kernels/paged_attention.py:634-698,
+ * launch at :675-697) and, with num_seqs == 1 and seq_lens == NULL, the v1 and
+ * v2 single-sequence launches (paged_attention.py:254-305 and :419-470).
+ *
+ *   out[s, h, :] = softmax(scale * q[s, h, :] . K[s, :, h / G, :]) @ V[s, :, h / G, :]
+ *
+ * over the first seq_len(s) tokens of sequence s, whose token t lives in pool
+ * block block_tables[s * block_tables_stride + t / block_size] at offset
+ * t % block_size. G = num_q_heads / num_kv_heads. Accumulation is fp32; out
+ * is stored in the pool dtype. A sequence with seq_len 0 yields zeros.
+ *
+ * q/out: [num_seqs, num_q_heads, head_dim], last dim contiguous, strides in
+ * elements. seq_lens: int32 device array, or NULL to use uniform_seq_len for
+ * every sequence. block_tables: int32 [num_seqs, >= max_blocks_per_seq].
+ * Entries beyond a sequence's last used block are never read.
+ *
+ * workspace: device scratch of at least
+ * pagedkv_decode_attention_workspace_size(...) bytes (may be NULL when that
+ * size is 0); it is fully overwritten before it is read.
+ */
+int pagedkv_decode_attention(
+    void *out, int64_t out_stride_seq, int64_t out_stride_head,
+    const void *q, int64_t q_stride_seq, int64_t q_stride_head,
+    const void *k_cache, const void *v_cache,
+    const int32_t *block_tables, int64_t block_tables_stride,
+    const int32_t *seq_lens, int32_t uniform_seq_len,
+    int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
+    int32_t head_dim, int64_t num_blocks, int32_t block_size,
+    int32_t max_blocks_per_seq, float scale, int32_t dtype,
+    void *workspace, size_t workspace_bytes, void *stream);
+
+/* Bytes of workspace pagedkv_decode_attention needs for this shape on the
+ * current device (0 when the launch needs none). */
+size_t pagedkv_decode_attention_workspace_size(
+    int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
+    int32_t head_dim, int32_t block_size, int32_t max_blocks_per_seq,
+    int32_t dtype);
+
+/*
+ * KV append: write one layer's new K and V rows into the pool.
+ *
+ * Replaces the per-sequence index_put loop of paged_decode_attention_forward
+ * (engine/kernels/paged_attention_integration.py:150-160, single-sequence form
+ * at :120-132): for token i with slot = slot_mapping[i] >= 0,
+ *   k_cache[slot / block_size, slot % block_size, :, :] = k_new[i, :, :]
+ * and the same for V, as a bit-exact copy. slot < 0 skips the token (padding).
+ * A slot >= num_blocks * block_size is skipped and sets
+ * PAGEDKV_EFLAG_SLOT_RANGE. k_new/v_new: [num_tokens, num_kv_heads, head_dim],
+ * last dim contiguous, strides in elements. One launch covers K and V.
+ */
+int pagedkv_kv_append(
+    void *k_cache, void *v_cache,
+    const void *k_new, int64_t k_new_stride_tok, int64_t k_new_stride_head,
+    const void *v_new, int64_t v_new_stride_tok, int64_t v_new_stride_head,
+    const int64_t *slot_mapping, int32_t num_tokens, int32_t num_kv_heads,
+    int32_t head_dim, int64_t num_blocks, int32_t block_size, int32_t dtype,
+    void *stream);
+
+/*
+ * Copy-on-write block copy over every layer's K and V pool.
+ *
+ * The reference has no data copy for CoW: BlockAllocator.fork only bumps a
+ * refcount (engine/memory/block_allocator.py:264-270) and the decode runner
+ * asserts it never writes a shared block (paged_attention_integration.py:
+ * 587-592). This entry point is the copy that assert stands in for: for every
+ * pair p and layer l,
+ *   k_cache[l][block_mapping[2p + 1]] = k_cache[l][block_mapping[2p]]
+ * and the same for V, bit-exact. k_cache_ptrs / v_cache_ptrs are DEVICE arrays
+ * of num_layers pool base pointers; block_mapping is a device int64 [num_pairs, 2]
+ * (src, dst) array. Destinations must be distinct and must not appear as a
+ * source in the same call. block_bytes = block_size * num_kv_heads * head_dim
+ * * element size. One launch covers all layers, K and V.
+ */
+int pagedkv_copy_blocks(
+    void *const *k_cache_ptrs, void *const *v_cache_ptrs, int32_t num_layers,
+    const int64_t *block_mapping, int32_t num_pairs, int64_t block_bytes,
+    int64_t num_blocks, void *stream);
+
+/*
+ * Read (and optionally clear) the device error word of the current device.
+ * Synchronises `stream`. Kernels never trap on bad indices: they skip the
+ * access and set a PAGEDKV_EFLAG_* bit, which this call reports.
+ */
+int pagedkv_read_error_flags(uint32_t *flags_out, int32_t clear, void *stream);
+
+/*
+ * Number of kernel launches the last pagedkv_decode_attention call on this
+ * thread issued (1 or 2: the split-K combine is a second launch), and the
+ * name of the decode kernel family it chose ("tc" = tcgen05/TMA, "simt").
+ */
+int32_t pagedkv_last_decode_launches(void);
+const char *pagedkv_last_decode_kernel(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGEDKV_H_ */

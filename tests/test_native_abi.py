@@ -1,0 +1,78 @@
+"""CPU: the C-ABI library loads and exports what include/pagedkv.h declares,
+and rejects bad arguments before touching a device."""
+import ctypes
+import re
+
+import pytest
+
+from pagedkv import _native
+
+
+def _header_functions() -> list[str]:
+    text = _native.HEADER_PATH.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(pagedkv_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_header_symbol():
+    lib = _native.lib()
+    declared = _header_functions()
+    assert declared, "no declarations parsed from include/pagedkv.h"
+    missing = [name for name in declared if not hasattr(lib, name)]
+    assert not missing, f"symbols declared in include/pagedkv.h but not exported: {missing}"
+    # the ctypes binding covers exactly the header
+    assert sorted(_native.declared_symbols()) == declared
+
+
+def test_version_string():
+    v = _native.lib().pagedkv_version().decode()
+    assert v.startswith("pagedkv-b200") and "sm_100a" in v
+
+
+def _decode(lib, **kw):
+    args = dict(
+        out=None, os=0, oh=0, q=None, qs=0, qh=0, k=None, v=None, bt=None, bts=0, lens=None, ulen=0,
+        n=1, hq=14, hkv=2, d=64, nb=16, bs=16, mb=1, scale=0.125, dtype=0, ws=None, wsb=0, stream=None,
+    )
+    args.update(kw)
+    return lib.pagedkv_decode_attention(*args.values())
+
+
+def test_decode_rejects_bad_arguments_without_a_device():
+    lib = _native.lib()
+    assert _decode(lib, n=0) == _native.PAGEDKV_OK  # empty batch is a no-op
+    assert _decode(lib, hq=13) == _native.PAGEDKV_ERR_INVALID_ARGUMENT
+    assert "multiple of num_kv_heads" in lib.pagedkv_last_error().decode()
+    assert _decode(lib, d=80) == _native.PAGEDKV_ERR_UNSUPPORTED
+    assert _decode(lib, dtype=7) == _native.PAGEDKV_ERR_UNSUPPORTED
+    assert _decode(lib, bs=0) == _native.PAGEDKV_ERR_INVALID_ARGUMENT
+    assert _decode(lib) == _native.PAGEDKV_ERR_INVALID_ARGUMENT  # null pointers
+    assert _decode(lib, n=-1) == _native.PAGEDKV_ERR_INVALID_ARGUMENT
+
+
+def test_append_and_copy_reject_bad_arguments_without_a_device():
+    lib = _native.lib()
+    assert lib.pagedkv_kv_append(None, None, None, 0, 0, None, 0, 0, None, 0, 2, 64, 16, 16, 0, None) == 0
+    assert lib.pagedkv_kv_append(None, None, None, 0, 0, None, 0, 0, None, 3, 2, 64, 16, 16, 0, None) == (
+        _native.PAGEDKV_ERR_INVALID_ARGUMENT
+    )
+    assert lib.pagedkv_kv_append(None, None, None, 0, 0, None, 0, 0, None, 3, 2, 64, 16, 16, 5, None) == (
+        _native.PAGEDKV_ERR_UNSUPPORTED
+    )
+    assert lib.pagedkv_copy_blocks(None, None, 1, None, 0, 4096, 8, None) == 0
+    assert lib.pagedkv_copy_blocks(None, None, 1, None, 1, 4095, 8, None) == _native.PAGEDKV_ERR_INVALID_ARGUMENT
+    assert lib.pagedkv_copy_blocks(None, None, 1, None, 1, 4096, 8, None) == _native.PAGEDKV_ERR_INVALID_ARGUMENT
+    assert lib.pagedkv_read_error_flags(None, 0, None) == _native.PAGEDKV_ERR_INVALID_ARGUMENT
+
+
+def test_error_flag_descriptions():
+    assert _native.describe_error_flags(0) == "none"
+    text = _native.describe_error_flags(_native.EFLAG_BLOCK_ID_RANGE | _native.EFLAG_SLOT_RANGE)
+    assert "block-table" in text and "slot" in text
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_native, "_lib", None)
+    monkeypatch.setattr(_native, "LIB_PATH", tmp_path / "nope.so")
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        _native.lib()

@@ -1,0 +1,89 @@
+// Shared device helpers for the pagedkv sm_100a kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/pagedkv.h"
+
+namespace pagedkv {
+
+// Kernels never trap on a bad index: they skip the access and OR a
+// PAGEDKV_EFLAG_* bit into the device error word whose address the ABI layer
+// passes in (see pagedkv_read_error_flags).
+__device__ __forceinline__ void set_error(unsigned int *err, unsigned int bit) {
+  atomicOr(err, bit);
+}
+
+// 16-byte streaming load through the read-only path. The KV pool is read once
+// per decode call, so it is marked evict-first in L1.
+__device__ __forceinline__ uint4 ldg_stream16(const void *p) {
+  uint4 r;
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint4 ldg16(const void *p) {
+  return __ldg(reinterpret_cast<const uint4 *>(p));
+}
+
+__device__ __forceinline__ void stg16(void *p, uint4 v) {
+  *reinterpret_cast<uint4 *>(p) = v;
+}
+
+// Element type traits: unpack 8 packed 16-bit values into fp32 and pack back.
+template <typename T> struct Elem;
+
+template <> struct Elem<__half> {
+  static constexpr int kDtype = PAGEDKV_DTYPE_F16;
+  __device__ __forceinline__ static void unpack8(const uint4 &r, float (&f)[8]) {
+    const __half2 *h = reinterpret_cast<const __half2 *>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 v = __half22float2(h[i]);
+      f[2 * i] = v.x;
+      f[2 * i + 1] = v.y;
+    }
+  }
+  __device__ __forceinline__ static uint4 pack8(const float (&f)[8]) {
+    uint4 r;
+    __half2 *h = reinterpret_cast<__half2 *>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    return r;
+  }
+  __device__ __forceinline__ static float to_float(__half x) { return __half2float(x); }
+  __device__ __forceinline__ static __half from_float(float x) { return __float2half_rn(x); }
+};
+
+template <> struct Elem<__nv_bfloat16> {
+  static constexpr int kDtype = PAGEDKV_DTYPE_BF16;
+  __device__ __forceinline__ static void unpack8(const uint4 &r, float (&f)[8]) {
+    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 v = __bfloat1622float2(h[i]);
+      f[2 * i] = v.x;
+      f[2 * i + 1] = v.y;
+    }
+  }
+  __device__ __forceinline__ static uint4 pack8(const float (&f)[8]) {
+    uint4 r;
+    __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    return r;
+  }
+  __device__ __forceinline__ static float to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
+  __device__ __forceinline__ static __nv_bfloat16 from_float(float x) { return __float2bfloat16_rn(x); }
+};
+
+// log2(e): scores are kept in the base-2 domain so exp() becomes one exp2f.
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kNegInf = -__builtin_huge_valf();
+
+}  // namespace pagedkv

@@ -1,0 +1,26 @@
+// Interface of the tcgen05 + TMA decode-attention kernel (decode_tc.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "launch.h"
+
+namespace pagedkv {
+
+// True when the tensor-core kernel covers this shape (GQA group >= 4 and a
+// head_dim / block_size it was built for).
+bool tc_eligible(int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size);
+
+// Scratch the tensor-core path needs (split-K partials), in bytes.
+size_t tc_workspace_bytes(int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
+                          int32_t head_dim, int32_t max_tokens, int32_t num_sms);
+
+// Launch; returns a PAGEDKV_* status and writes the number of launches.
+int tc_launch(DecodeParams &p, int dtype, void *workspace, size_t workspace_bytes,
+              int32_t num_sms, cudaStream_t stream, int *launches, std::string *error);
+
+}  // namespace pagedkv

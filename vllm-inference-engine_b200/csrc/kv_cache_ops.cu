@@ -1,0 +1,148 @@
+// KV append and copy-on-write block copy (sm_100a).
+//
+// Both are pure byte movement bound by HBM bandwidth: every thread moves one
+// 16-byte chunk (or a strided run of them), with 64-bit offsets so pools larger
+// than 2^31 bytes per layer are addressed correctly.
+#include "common.cuh"
+#include "launch.h"
+
+namespace pagedkv {
+
+// One thread per 16-byte chunk of one token's [num_kv_heads, head_dim] row,
+// for K and V together. chunks_per_row = num_kv_heads * head_dim / 8.
+// Restates engine/kernels/paged_attention_integration.py:150-160: the reference
+// computes (phys, off) = (table[(len-1)/BS], (len-1)%BS) per sequence on the host
+// and assigns pool[l][phys, off] = k; here the slot phys*BS+off comes in
+// precomputed and every token of the batch is written by one launch.
+__global__ void __launch_bounds__(256)
+kv_append_vec_kernel(char *__restrict__ k_cache, char *__restrict__ v_cache,
+                     const char *__restrict__ k_new, int64_t ks_tok, int64_t ks_head,
+                     const char *__restrict__ v_new, int64_t vs_tok, int64_t vs_head,
+                     const int64_t *__restrict__ slots, int32_t num_tokens,
+                     int32_t num_kv_heads, int32_t head_dim, int64_t num_slots, unsigned int *err) {
+  const int chunks_per_head = head_dim >> 3;
+  const int chunks_per_row = num_kv_heads * chunks_per_head;
+  const int64_t total = (int64_t)num_tokens * chunks_per_row;
+  const int64_t row_bytes = (int64_t)num_kv_heads * head_dim * 2;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int tok = (int)(idx / chunks_per_row);
+    const int rem = (int)(idx - (int64_t)tok * chunks_per_row);
+    const int head = rem / chunks_per_head;
+    const int c = rem - head * chunks_per_head;
+    const int64_t slot = __ldg(slots + tok);
+    if (slot < 0) continue;
+    if (slot >= num_slots) {
+      set_error(err, PAGEDKV_EFLAG_SLOT_RANGE);
+      continue;
+    }
+    const int64_t dst = slot * row_bytes + ((int64_t)head * head_dim + c * 8) * 2;
+    const uint4 kv = ldg16(k_new + ((int64_t)tok * ks_tok + (int64_t)head * ks_head + c * 8) * 2);
+    const uint4 vv = ldg16(v_new + ((int64_t)tok * vs_tok + (int64_t)head * vs_head + c * 8) * 2);
+    stg16(k_cache + dst, kv);
+    stg16(v_cache + dst, vv);
+  }
+}
+
+// Fallback for inputs whose rows are not 16-byte aligned: one 2-byte element
+// per thread.
+__global__ void __launch_bounds__(256)
+kv_append_scalar_kernel(uint16_t *__restrict__ k_cache, uint16_t *__restrict__ v_cache,
+                        const uint16_t *__restrict__ k_new, int64_t ks_tok, int64_t ks_head,
+                        const uint16_t *__restrict__ v_new, int64_t vs_tok, int64_t vs_head,
+                        const int64_t *__restrict__ slots, int32_t num_tokens,
+                        int32_t num_kv_heads, int32_t head_dim, int64_t num_slots,
+                        unsigned int *err) {
+  const int per_row = num_kv_heads * head_dim;
+  const int64_t total = (int64_t)num_tokens * per_row;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int tok = (int)(idx / per_row);
+    const int rem = (int)(idx - (int64_t)tok * per_row);
+    const int head = rem / head_dim;
+    const int d = rem - head * head_dim;
+    const int64_t slot = slots[tok];
+    if (slot < 0) continue;
+    if (slot >= num_slots) {
+      set_error(err, PAGEDKV_EFLAG_SLOT_RANGE);
+      continue;
+    }
+    const int64_t dst = slot * per_row + rem;
+    k_cache[dst] = k_new[(int64_t)tok * ks_tok + (int64_t)head * ks_head + d];
+    v_cache[dst] = v_new[(int64_t)tok * vs_tok + (int64_t)head * vs_head + d];
+  }
+}
+
+// One CTA per (pair, layer, K|V): copies block_bytes from block src to block
+// dst of that layer's pool with 16-byte loads/stores, four in flight per thread.
+__global__ void __launch_bounds__(256)
+copy_blocks_kernel(char *const *__restrict__ k_ptrs, char *const *__restrict__ v_ptrs,
+                   const int64_t *__restrict__ mapping, int64_t block_bytes,
+                   int64_t num_blocks, unsigned int *err) {
+  const int pair = blockIdx.x;
+  const int layer = blockIdx.y >> 1;
+  const bool is_v = blockIdx.y & 1;
+  const int64_t src = __ldg(mapping + 2 * pair);
+  const int64_t dst = __ldg(mapping + 2 * pair + 1);
+  if (src < 0 || src >= num_blocks || dst < 0 || dst >= num_blocks) {
+    if (threadIdx.x == 0) set_error(err, PAGEDKV_EFLAG_COPY_RANGE);
+    return;
+  }
+  char *base = is_v ? v_ptrs[layer] : k_ptrs[layer];
+  const char *s = base + src * block_bytes;
+  char *d = base + dst * block_bytes;
+  const int64_t n16 = block_bytes >> 4;
+  const int64_t step = (int64_t)blockDim.x * 4;
+  for (int64_t i = threadIdx.x; i < n16; i += step) {
+    uint4 r[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t j = i + (int64_t)u * blockDim.x;
+      if (j < n16) r[u] = ldg_stream16(s + j * 16);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t j = i + (int64_t)u * blockDim.x;
+      if (j < n16) stg16(d + j * 16, r[u]);
+    }
+  }
+}
+
+cudaError_t launch_kv_append(void *k_cache, void *v_cache, const void *k_new, int64_t ks_tok,
+                             int64_t ks_head, const void *v_new, int64_t vs_tok,
+                             int64_t vs_head, const int64_t *slots, int32_t num_tokens,
+                             int32_t num_kv_heads, int32_t head_dim, int64_t num_slots,
+                             bool vectorized, unsigned int *err, cudaStream_t stream) {
+  if (num_tokens == 0) return cudaSuccess;
+  const int threads = 256;
+  if (vectorized) {
+    const int64_t total = (int64_t)num_tokens * num_kv_heads * (head_dim / 8);
+    const int64_t blocks = (total + threads - 1) / threads;
+    kv_append_vec_kernel<<<(unsigned)(blocks < 65535 * 8 ? blocks : 65535 * 8), threads, 0,
+                           stream>>>(
+        (char *)k_cache, (char *)v_cache, (const char *)k_new, ks_tok, ks_head,
+        (const char *)v_new, vs_tok, vs_head, slots, num_tokens, num_kv_heads, head_dim,
+        num_slots, err);
+  } else {
+    const int64_t total = (int64_t)num_tokens * num_kv_heads * head_dim;
+    const int64_t blocks = (total + threads - 1) / threads;
+    kv_append_scalar_kernel<<<(unsigned)(blocks < 65535 * 8 ? blocks : 65535 * 8), threads, 0,
+                              stream>>>(
+        (uint16_t *)k_cache, (uint16_t *)v_cache, (const uint16_t *)k_new, ks_tok, ks_head,
+        (const uint16_t *)v_new, vs_tok, vs_head, slots, num_tokens, num_kv_heads, head_dim,
+        num_slots, err);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_copy_blocks(void *const *k_ptrs, void *const *v_ptrs, int32_t num_layers,
+                               const int64_t *mapping, int32_t num_pairs, int64_t block_bytes,
+                               int64_t num_blocks, unsigned int *err, cudaStream_t stream) {
+  if (num_pairs == 0 || num_layers == 0) return cudaSuccess;
+  dim3 grid((unsigned)num_pairs, (unsigned)(num_layers * 2));
+  copy_blocks_kernel<<<grid, 256, 0, stream>>>((char *const *)k_ptrs, (char *const *)v_ptrs,
+                                               mapping, block_bytes, num_blocks, err);
+  return cudaGetLastError();
+}
+
+}  // namespace pagedkv

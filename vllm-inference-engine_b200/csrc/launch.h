@@ -1,0 +1,53 @@
+// Host-side launch declarations shared by the pagedkv translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pagedkv {
+
+// Everything one decode-attention launch needs, resolved by the ABI layer.
+struct DecodeParams {
+  void *out;
+  int64_t o_ss, o_sh;           // out strides (elements): seq, head
+  const void *q;
+  int64_t q_ss, q_sh;           // q strides (elements): seq, head
+  const void *k;
+  const void *v;
+  const int32_t *bt;            // block tables
+  int64_t bt_s;                 // block table row stride (elements)
+  const int32_t *lens;          // seq_lens or nullptr
+  int32_t uniform_len;          // used when lens == nullptr
+  int32_t num_seqs, hq, hkv, group, head_dim, block_size, max_blocks;
+  int64_t num_blocks;
+  float scale_log2;             // scale * log2(e)
+  int32_t split_tokens;         // tokens per split-K chunk
+  int32_t num_splits;           // chunks per sequence (1 = no combine pass)
+  float *ws_acc;                // [num_seqs, hq, num_splits, head_dim] partial sums
+  float2 *ws_ml;                // [num_seqs, hq, num_splits] (running max, denominator)
+  unsigned int *err;            // device error word
+};
+
+// Split-K decision shared by the workspace-size query and the launcher.
+struct SplitPlan {
+  int32_t split_tokens;
+  int32_t num_splits;
+};
+
+SplitPlan plan_simt_splits(int32_t num_seqs, int32_t num_kv_heads, int32_t group,
+                           int32_t max_tokens, int32_t num_sms);
+
+cudaError_t launch_decode_simt(const DecodeParams &p, int dtype, cudaStream_t stream);
+cudaError_t launch_decode_combine(const DecodeParams &p, int dtype, cudaStream_t stream);
+
+cudaError_t launch_kv_append(void *k_cache, void *v_cache, const void *k_new, int64_t ks_tok,
+                             int64_t ks_head, const void *v_new, int64_t vs_tok,
+                             int64_t vs_head, const int64_t *slots, int32_t num_tokens,
+                             int32_t num_kv_heads, int32_t head_dim, int64_t num_slots,
+                             bool vectorized, unsigned int *err, cudaStream_t stream);
+
+cudaError_t launch_copy_blocks(void *const *k_ptrs, void *const *v_ptrs, int32_t num_layers,
+                               const int64_t *mapping, int32_t num_pairs, int64_t block_bytes,
+                               int64_t num_blocks, unsigned int *err, cudaStream_t stream);
+
+}  // namespace pagedkv

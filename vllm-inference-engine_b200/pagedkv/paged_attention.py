@@ -1,0 +1,400 @@
+"""B200 paged decode attention with the reference's Python interface.
+
+Drop-in for the kernel entry points of the reference module
+``engine/kernels/paged_attention.py``:
+
+* ``paged_attention_decode_batched`` (reference :634-698)
+* ``paged_attention_decode_v1`` (reference :254-305) and
+  ``paged_attention_decode_v2`` (reference :419-470)
+* ``paged_attention_decode`` (reference stub :86-99, list-of-lists tables)
+* ``pad_block_tables`` (reference :473-505)
+
+plus the two pool-write operations of the same path:
+
+* ``kv_append`` — the decode append of paged_attention_integration.py:150-160,
+  one launch per layer through a slot mapping;
+* ``copy_blocks`` — the copy-on-write block copy over all layers.
+
+Same argument names, shapes and meaning; the same ``AssertionError`` for the
+preconditions the reference asserts. Every call launches the sm_100a kernels of
+``libpagedkv_b200.so`` on the current torch CUDA stream. There is no Triton,
+no CPU path and no fallback: a CPU tensor or a missing library raises.
+
+Beyond the reference: bf16 pools are accepted as well as fp16, and q/out may
+be strided views (last dimension contiguous).
+"""
+from __future__ import annotations
+
+import os
+from typing import Any, Sequence
+
+import torch
+
+from . import _native
+
+_DEBUG = os.environ.get("PAGEDKV_DEBUG", "0") not in ("", "0")
+
+_DTYPES = {torch.float16: _native.DTYPE_F16, torch.bfloat16: _native.DTYPE_BF16}
+
+# Split-K scratch, one cached buffer per device, grown on demand.
+_workspaces: dict[int, torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
+    if nbytes == 0:
+        return None
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _workspaces.get(idx)
+    if buf is None or buf.numel() < nbytes:
+        size = max(nbytes, 1 << 20)
+        buf = torch.empty(size, dtype=torch.uint8, device=device)
+        _workspaces[idx] = buf
+    return buf
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _aligned(t: torch.Tensor) -> bool:
+    return t.data_ptr() % 16 == 0
+
+
+def _qo_ok(t: torch.Tensor) -> bool:
+    return t.stride(-1) == 1 and _aligned(t) and t.stride(0) % 8 == 0 and t.stride(1) % 8 == 0
+
+
+def _device_guard(device: torch.device):
+    if device.index is not None and torch.cuda.current_device() != device.index:
+        return torch.cuda.device(device)
+    return None
+
+
+def _debug_check(device: torch.device, what: str) -> None:
+    if _DEBUG:
+        flags = read_error_flags(device, clear=True)
+        if flags:
+            raise RuntimeError(f"{what}: device error flags 0x{flags:x} ({_native.describe_error_flags(flags)})")
+
+
+def read_error_flags(device: torch.device | str | int | None = None, clear: bool = True) -> int:
+    """Return (and by default clear) the device error word the kernels set when
+    they skip an out-of-range block id, slot or length. Synchronises the stream."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if dev.type == "cuda" and dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    out = _native.ctypes.c_uint32(0)
+    guard = _device_guard(dev)
+    if guard is not None:
+        with guard:
+            rc = _native.lib().pagedkv_read_error_flags(_native.ctypes.byref(out), int(clear), _stream_handle(dev))
+    else:
+        rc = _native.lib().pagedkv_read_error_flags(_native.ctypes.byref(out), int(clear), _stream_handle(dev))
+    _native.check(rc, "pagedkv_read_error_flags")
+    return int(out.value)
+
+
+def _decode_into(
+    out: torch.Tensor,
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor | None,
+    uniform_seq_len: int,
+    scale: float,
+) -> None:
+    """Launch decode attention writing into ``out`` ([N, Hq, D])."""
+    assert k_cache.is_contiguous() and v_cache.is_contiguous(), "KV pool tensors must be contiguous"
+    assert v_cache.shape == k_cache.shape, "k_cache and v_cache must have the same shape"
+    num_seqs, num_q_heads, head_dim = q.shape
+    num_blocks, block_size, num_kv_heads, _ = k_cache.shape
+    if num_seqs == 0:
+        return
+    if block_tables.stride(-1) != 1:
+        block_tables = block_tables.contiguous()
+    if seq_lens is not None and not seq_lens.is_contiguous():
+        seq_lens = seq_lens.contiguous()
+    qq = q if _qo_ok(q) else q.contiguous()
+    oo = out if _qo_ok(out) else torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    dtype = _DTYPES[q.dtype]
+    max_blocks = block_tables.shape[1]
+    lib = _native.lib()
+    dev = q.device
+    guard = _device_guard(dev)
+    ctx = guard if guard is not None else _NullCtx()
+    with ctx:
+        nbytes = lib.pagedkv_decode_attention_workspace_size(
+            num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks, dtype
+        )
+        ws = _workspace(dev, nbytes)
+        rc = lib.pagedkv_decode_attention(
+            oo.data_ptr(), oo.stride(0), oo.stride(1),
+            qq.data_ptr(), qq.stride(0), qq.stride(1),
+            k_cache.data_ptr(), v_cache.data_ptr(),
+            block_tables.data_ptr(), block_tables.stride(0),
+            seq_lens.data_ptr() if seq_lens is not None else None, int(uniform_seq_len),
+            num_seqs, num_q_heads, num_kv_heads, head_dim,
+            num_blocks, block_size, max_blocks,
+            float(scale), dtype,
+            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+            _stream_handle(dev),
+        )
+    _native.check(rc, "pagedkv_decode_attention")
+    if oo is not out:
+        out.copy_(oo)
+    _debug_check(dev, "paged decode attention")
+
+
+class _NullCtx:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
+
+
+def paged_attention_decode_batched(
+    q: torch.Tensor,            # [num_seqs, num_q_heads, head_dim] (fp16/bf16, cuda)
+    k_cache: torch.Tensor,      # [num_blocks, block_size, num_kv_heads, head_dim]
+    v_cache: torch.Tensor,      # [num_blocks, block_size, num_kv_heads, head_dim]
+    block_tables: torch.Tensor,  # [num_seqs, max_blocks_per_seq] (int32, cuda)
+    seq_lens: torch.Tensor,     # [num_seqs] (int32, cuda)
+    scale: float,
+) -> torch.Tensor:
+    """Batched decode attention over paged K/V (reference paged_attention.py:634-698).
+
+    Same preconditions as the reference (asserted identically), output
+    ``torch.empty_like(q)`` filled by the sm_100a kernel.
+    """
+    assert q.is_cuda and k_cache.is_cuda and v_cache.is_cuda
+    assert block_tables.is_cuda and seq_lens.is_cuda
+    assert q.dtype in _DTYPES and k_cache.dtype == q.dtype and v_cache.dtype == q.dtype
+    assert block_tables.dtype == torch.int32 and seq_lens.dtype == torch.int32
+
+    num_seqs, num_q_heads, head_dim = q.shape
+    num_blocks, block_size, num_kv_heads, head_dim_k = k_cache.shape
+    assert head_dim == head_dim_k, f"Head dimensions must match: {head_dim} vs {head_dim_k}"
+    assert num_q_heads % num_kv_heads == 0, (
+        f"num_q_heads ({num_q_heads}) must be divisible by num_kv_heads ({num_kv_heads})"
+    )
+    assert block_tables.shape[0] == num_seqs
+    assert seq_lens.shape[0] == num_seqs
+
+    out = torch.empty_like(q)
+    _decode_into(out, q, k_cache, v_cache, block_tables, seq_lens, 0, scale)
+    return out
+
+
+def _single_sequence(q, k_cache, v_cache, block_table, seq_len, scale) -> torch.Tensor:
+    assert q.is_cuda and k_cache.is_cuda and v_cache.is_cuda and block_table.is_cuda
+    assert q.dtype in _DTYPES and k_cache.dtype == q.dtype and v_cache.dtype == q.dtype
+    assert block_table.dtype == torch.int32
+
+    num_q_heads, head_dim = q.shape
+    num_blocks, block_size, num_kv_heads, head_dim_k = k_cache.shape
+    assert head_dim == head_dim_k, f"Head dimensions must match: {head_dim} vs {head_dim_k}"
+    assert num_q_heads % num_kv_heads == 0, (
+        f"num_q_heads ({num_q_heads}) must be divisible by num_kv_heads ({num_kv_heads})"
+    )
+    seq_len = int(seq_len)
+    num_blocks_for_seq = (seq_len + block_size - 1) // block_size
+    assert block_table.shape[0] >= num_blocks_for_seq, (
+        f"block_table size ({block_table.shape[0]}) smaller than needed ({num_blocks_for_seq})"
+    )
+    out = torch.empty_like(q)
+    table = block_table.reshape(1, -1)
+    if table.shape[1] == 0:
+        table = torch.zeros((1, 1), dtype=torch.int32, device=q.device)
+    _decode_into(out.unsqueeze(0), q.unsqueeze(0), k_cache, v_cache, table, None, seq_len, scale)
+    return out
+
+
+def paged_attention_decode_v1(
+    q: torch.Tensor,            # [num_q_heads, head_dim]
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_table: torch.Tensor,  # 1D int32 cuda tensor of physical block IDs
+    seq_len: int,
+    scale: float,
+) -> torch.Tensor:
+    """Single-sequence decode attention (reference paged_attention.py:254-305).
+
+    The reference's v1 makes three passes over K; this build serves v1 and v2
+    with the same one-pass kernel (identical mathematics), so v1 == v2 here.
+    """
+    return _single_sequence(q, k_cache, v_cache, block_table, seq_len, scale)
+
+
+def paged_attention_decode_v2(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_len: int,
+    scale: float,
+) -> torch.Tensor:
+    """Single-sequence online-softmax decode attention (reference :419-470)."""
+    return _single_sequence(q, k_cache, v_cache, block_table, seq_len, scale)
+
+
+def _raw_lists(block_tables: Sequence[Any]) -> list[list[int]]:
+    raw: list[list[int]] = []
+    for bt in block_tables:
+        if hasattr(bt, "physical_block_ids"):
+            raw.append(list(bt.physical_block_ids))
+        elif isinstance(bt, (list, tuple)):
+            raw.append(list(bt))
+        else:
+            raise TypeError(f"Unsupported block table type: {type(bt)}")
+    return raw
+
+
+def pad_block_tables(
+    block_tables: Sequence[Any],
+    device: torch.device | str = "cuda",
+) -> torch.Tensor:
+    """List of lists (or objects with ``.physical_block_ids``) -> zero-padded
+    int32 tensor [num_seqs, max(1, max_len)] on ``device`` (reference :473-505).
+
+    Same result as the reference; built on the host and moved with a single
+    copy instead of one device copy per row.
+    """
+    num_seqs = len(block_tables)
+    if num_seqs == 0:
+        return torch.empty((0, 0), dtype=torch.int32, device=device)
+    raw = _raw_lists(block_tables)
+    max_len = max(1, max((len(r) for r in raw), default=0))
+    host = torch.zeros((num_seqs, max_len), dtype=torch.int32)
+    for i, row in enumerate(raw):
+        if row:
+            host[i, : len(row)] = torch.tensor(row, dtype=torch.int32)
+    dev = torch.device(device)
+    if dev.type == "cuda":
+        return host.pin_memory().to(dev, non_blocking=True)
+    return host.to(dev)
+
+
+def paged_attention_decode(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: list[list[int]],
+    seq_lens: list[int],
+    scale: float,
+) -> torch.Tensor:
+    """The reference's list-based entry (paged_attention.py:86-99), which there
+    falls back to the PyTorch reference; here it runs the batched kernel."""
+    tables = pad_block_tables(block_tables, device=q.device)
+    lens = torch.tensor(list(seq_lens), dtype=torch.int32).to(q.device)
+    return paged_attention_decode_batched(q, k_cache, v_cache, tables, lens, scale)
+
+
+def kv_append(
+    k_new: torch.Tensor,        # [num_tokens, num_kv_heads, head_dim]
+    v_new: torch.Tensor,        # [num_tokens, num_kv_heads, head_dim]
+    k_cache: torch.Tensor,      # [num_blocks, block_size, num_kv_heads, head_dim]
+    v_cache: torch.Tensor,
+    slot_mapping: torch.Tensor,  # [num_tokens] int64; slot = block_id * block_size + offset
+) -> None:
+    """Write one layer's new K/V rows into the pool in place, bit-exact.
+
+    Equivalent to ``k_cache[slot // BS, slot % BS] = k_new[i]`` (and V) for
+    every token with ``slot >= 0`` — the assignment the reference performs per
+    sequence at paged_attention_integration.py:150-160 — in one launch.
+    """
+    assert k_new.is_cuda and v_new.is_cuda and k_cache.is_cuda and v_cache.is_cuda and slot_mapping.is_cuda
+    assert k_cache.dtype in _DTYPES and v_cache.dtype == k_cache.dtype
+    assert k_new.dtype == k_cache.dtype and v_new.dtype == k_cache.dtype, "new K/V must match the pool dtype"
+    assert slot_mapping.dtype == torch.int64, "slot_mapping must be int64"
+    assert k_cache.is_contiguous() and v_cache.is_contiguous(), "KV pool tensors must be contiguous"
+    assert v_cache.shape == k_cache.shape
+    num_blocks, block_size, num_kv_heads, head_dim = k_cache.shape
+    k3 = k_new.reshape(-1, num_kv_heads, head_dim)
+    v3 = v_new.reshape(-1, num_kv_heads, head_dim)
+    num_tokens = k3.shape[0]
+    assert v3.shape[0] == num_tokens and slot_mapping.numel() == num_tokens, (
+        f"k_new/v_new/slot_mapping disagree on the token count ({num_tokens}, {v3.shape[0]}, {slot_mapping.numel()})"
+    )
+    if num_tokens == 0:
+        return
+    if k3.stride(-1) != 1:
+        k3 = k3.contiguous()
+    if v3.stride(-1) != 1:
+        v3 = v3.contiguous()
+    slots = slot_mapping.reshape(-1)
+    if not slots.is_contiguous():
+        slots = slots.contiguous()
+    dev = k_cache.device
+    guard = _device_guard(dev)
+    with guard if guard is not None else _NullCtx():
+        rc = _native.lib().pagedkv_kv_append(
+            k_cache.data_ptr(), v_cache.data_ptr(),
+            k3.data_ptr(), k3.stride(0), k3.stride(1),
+            v3.data_ptr(), v3.stride(0), v3.stride(1),
+            slots.data_ptr(), num_tokens, num_kv_heads, head_dim,
+            num_blocks, block_size, _DTYPES[k_cache.dtype],
+            _stream_handle(dev),
+        )
+    _native.check(rc, "pagedkv_kv_append")
+    _debug_check(dev, "kv_append")
+
+
+# Device arrays of per-layer pool base pointers, keyed by the pointer tuple.
+_ptr_tables: dict[tuple, tuple[torch.Tensor, torch.Tensor]] = {}
+
+
+def _pointer_tables(k_caches: Sequence[torch.Tensor], v_caches: Sequence[torch.Tensor]):
+    key = tuple(t.data_ptr() for t in k_caches) + tuple(t.data_ptr() for t in v_caches)
+    hit = _ptr_tables.get(key)
+    if hit is None:
+        dev = k_caches[0].device
+        kp = torch.tensor([t.data_ptr() for t in k_caches], dtype=torch.int64).to(dev)
+        vp = torch.tensor([t.data_ptr() for t in v_caches], dtype=torch.int64).to(dev)
+        if len(_ptr_tables) > 64:
+            _ptr_tables.clear()
+        hit = (kp, vp)
+        _ptr_tables[key] = hit
+    return hit
+
+
+def copy_blocks(
+    k_caches: Sequence[torch.Tensor],
+    v_caches: Sequence[torch.Tensor],
+    block_mapping: torch.Tensor,  # [num_pairs, 2] int64 (src, dst)
+) -> None:
+    """Copy-on-write block copy: for each (src, dst) pair and every layer,
+    ``k_caches[l][dst] = k_caches[l][src]`` and the same for V, in one launch.
+
+    The reference shares blocks by refcount only (block_allocator.py:264-270)
+    and asserts it never writes a shared block (integration.py:587-592); this
+    is the data copy that lets a writer take a private copy instead.
+    Destinations must be distinct and must not be sources in the same call.
+    """
+    assert len(k_caches) == len(v_caches) and len(k_caches) > 0
+    ref = k_caches[0]
+    assert ref.is_cuda and block_mapping.is_cuda
+    assert block_mapping.dtype == torch.int64 and block_mapping.dim() == 2 and block_mapping.shape[1] == 2
+    for t in list(k_caches) + list(v_caches):
+        assert t.shape == ref.shape and t.dtype == ref.dtype and t.is_contiguous() and t.device == ref.device
+    num_pairs = block_mapping.shape[0]
+    if num_pairs == 0:
+        return
+    mapping = block_mapping if block_mapping.is_contiguous() else block_mapping.contiguous()
+    kp, vp = _pointer_tables(k_caches, v_caches)
+    block_bytes = ref[0].numel() * ref.element_size()
+    dev = ref.device
+    guard = _device_guard(dev)
+    with guard if guard is not None else _NullCtx():
+        rc = _native.lib().pagedkv_copy_blocks(
+            kp.data_ptr(), vp.data_ptr(), len(k_caches), mapping.data_ptr(), num_pairs,
+            block_bytes, ref.shape[0], _stream_handle(dev),
+        )
+    _native.check(rc, "pagedkv_copy_blocks")
+    _debug_check(dev, "copy_blocks")
+
+
+def last_decode_launch_info() -> tuple[int, str]:
+    """(kernel launches, kernel family) of the last decode call on this thread."""
+    lib = _native.lib()
+    return int(lib.pagedkv_last_decode_launches()), lib.pagedkv_last_decode_kernel().decode()
