@@ -1,6 +1,6 @@
 // Paged GQA decode attention on the 5th-generation tensor cores (sm_100a):
 // TMA tile loads of K/V blocks through the block table, tcgen05.mma with TMEM
-// accumulators, one persistent CTA per SM.
+// accumulators, one persistent CTA per SM, stream-K work split.
 //
 // Math (restates engine/kernels/paged_attention.py:508-631, the batched
 // online-softmax kernel; same result as the oracle :30-83):
@@ -22,22 +22,28 @@
 //     Accumulator in TMEM, one token row per TMEM lane.
 //   * Softmax warps (128 threads, one token row each) read S, mask tokens past
 //     the end, take the tile max with redux.sync, write P (fp16/bf16) to shared
-//     memory as the B operand of the second MMA.
+//     memory as the (MN-major) B operand of the second MMA.
 //   * O^T = V^T P^T on the tensor core: M = 128 (kv head, dim) rows read from
 //     the SAME swizzled V tile as an MN-major operand, N = query columns,
 //     K = 128 tokens. Fresh TMEM accumulator per tile; the softmax warps fold
 //     it into fp32 registers with the online-softmax rescale.
-//   * Work items = (sequence, head group, context chunk); a sequence spanning
-//     several chunks writes unnormalised partials and the last CTA to finish
-//     it (arrival counter) combines them — no second launch.
-//   * Warp roles: warp 0 TMA producer (also stages Q), warp 1 MMA issuer and
-//     TMEM owner, warps 2-5 softmax / correction / epilogue.
+//   * Work split (stream-K): the (sequence, head group) segments are laid end
+//     to end as one sequence of 128-token tiles; CTA b takes tiles
+//     [b*T/grid, (b+1)*T/grid). A segment cut by a CTA boundary is finished by
+//     the last of its CTAs to arrive (arrival counter), which folds the <= 2
+//     partial results each CTA leaves — no second launch, equal work per SM.
+//   * Warp roles: warp 0 K-tile TMA producer (also stages Q), warp 6 V-tile
+//     TMA producer, warp 1 MMA issuer and TMEM owner, warps 2-5 softmax /
+//     correction / epilogue. K and V have separate smem rings: a K tile is
+//     freed once the S MMA has read it, so K prefetch runs deeper than V.
 //   * Every mbarrier wait is bounded (2 s): on timeout the kernel sets
 //     PAGEDKV_EFLAG_PIPE_TIMEOUT, unwinds every role, drains its own TMA loads
 //     and MMAs, frees TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -50,101 +56,191 @@ using namespace sm100;
 
 namespace {
 
-constexpr int kTile = 128;                 // tokens per tile (MMA M of S^T)
-constexpr int kHalfBytes = kTile * 128;    // one 64-element half of a tile: 16 KB
+constexpr int kTile = 128;                     // tokens per tile (MMA M of S^T)
+constexpr int kHalfBytes = kTile * 128;        // one 64-element half of a tile: 16 KB
 constexpr int kOperandBytes = 2 * kHalfBytes;  // [128 x 128] K or V tile: 32 KB
-constexpr int kThreads = 192;              // 6 warps
+constexpr int kThreads = 224;                  // 7 warps
 constexpr uint64_t kTimeoutNs = 2000000000ull;
+
+// Optional wait-time trace (build with -DPAGEDKV_TRACE; off in the product
+// build): per CTA and warp role, nanoseconds spent in each pipeline wait.
+#ifdef PAGEDKV_TRACE
+constexpr int kTraceSlots = 8;
+constexpr int kTraceCtas = 160;
+__device__ unsigned long long g_trace[kTraceCtas][4][kTraceSlots];
+#define PKV_TW(slot, expr)             \
+  ([&]() {                              \
+    const uint64_t _t0 = globaltimer_ns(); \
+    const auto _r = (expr);             \
+    tw[slot] += globaltimer_ns() - _t0; \
+    return _r;                          \
+  }())
+#define PKV_TV(slot, stmt)              \
+  do {                                  \
+    const uint64_t _t0 = globaltimer_ns(); \
+    stmt;                               \
+    tw[slot] += globaltimer_ns() - _t0; \
+  } while (0)
+#define PKV_TADD(slot, v) (tw[slot] += (v))
+#else
+#define PKV_TW(slot, expr) (expr)
+#define PKV_TV(slot, stmt) stmt
+#define PKV_TADD(slot, v) ((void)0)
+#endif
 
 struct TcParams {
   DecodeParams p;
-  int32_t head_groups;   // ceil(hkv / H)
-  int32_t total_items;   // num_seqs * head_groups * num_splits
-  int32_t oob_row;       // num_blocks * block_size: first row past the pool
-  int32_t *counters;     // [num_seqs * head_groups] arrival counters, or null
+  int32_t head_groups;  // ceil(hkv / H)
+  int32_t oob_row;      // num_blocks * block_size: first row past the pool
+  float *part_acc;      // [2 * grid][H * G][head_dim] partial sums of cut segments
+  float2 *part_ml;      // [2 * grid][H * G] (running max, denominator)
+  int32_t *counters;    // [num_seqs * head_groups] arrival counters (zeroed per launch)
 };
 
-struct Item {
-  int seq, hg, c, len, t0, t1, ntiles, nck;
-};
-
-__device__ __forceinline__ Item item_info(const TcParams &tp, int item) {
-  const DecodeParams &p = tp.p;
-  Item it;
-  const int per_seq = tp.head_groups * p.num_splits;
-  it.seq = item / per_seq;
-  const int rem = item - it.seq * per_seq;
-  it.hg = rem / p.num_splits;
-  it.c = rem - it.hg * p.num_splits;
-  int len = p.lens ? __ldg(p.lens + it.seq) : p.uniform_len;
+__device__ __forceinline__ int seq_len_clamped(const DecodeParams &p, int seq) {
+  int len = p.lens ? __ldg(p.lens + seq) : p.uniform_len;
   const int cap = p.max_blocks * p.block_size;
   len = len > cap ? cap : len;
-  len = len < 0 ? 0 : len;
-  it.len = len;
-  it.t0 = it.c * p.split_tokens;
-  it.t1 = min(len, it.t0 + p.split_tokens);
-  it.ntiles = it.t1 > it.t0 ? (it.t1 - it.t0 + kTile - 1) / kTile : 0;
-  it.nck = (len + p.split_tokens - 1) / p.split_tokens;
-  return it;
+  return len < 0 ? 0 : len;
 }
 
-template <int N, int STAGES>
-struct SmemLayout {
-  static constexpr int kQBytes = 2 * N * 128;  // B operand [N x 128], two K-halves
-  static constexpr int kPBytes = 2 * N * 128;  // B operand [N x 128 tokens], two K-halves
-  static constexpr int kOffK = 0;
-  static constexpr int kOffV = kOffK + STAGES * kOperandBytes;
-  static constexpr int kOffQ = kOffV + STAGES * kOperandBytes;
-  static constexpr int kOffP = kOffQ + 2 * kQBytes;
-  static constexpr int kOffRedMax = kOffP + 2 * kPBytes;         // float [2][4][N]
-  static constexpr int kOffRedL = kOffRedMax + 2 * 4 * N * 4;    // float [4][N]
-  static constexpr int kOffBars = kOffRedL + 4 * N * 4;          // uint64 barriers
-  // kfull, vfull, empty [STAGES]; s_full, s_empty, p_full, p_empty, o_full,
-  // o_empty, q_full, q_empty [2]; mma_done [1]
-  static constexpr int kNumBars = 3 * STAGES + 8 * 2 + 1;
-  static constexpr int kOffMisc = kOffBars + kNumBars * 8;       // tmem base, abort, flag
-  static constexpr int kBytes = kOffMisc + 16;
-  static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
+__device__ __forceinline__ int tiles_of(int len) { return (len + kTile - 1) / kTile; }
+
+// First tile of CTA b and the CTA owning global tile t, for T tiles over G CTAs.
+__device__ __forceinline__ int64_t range_lo(int64_t b, int64_t T, int64_t G) { return b * T / G; }
+__device__ __forceinline__ int64_t owner_of(int64_t t, int64_t T, int64_t G) {
+  return ((t + 1) * G + T - 1) / T - 1;
+}
+
+// One contiguous run of tiles of a (sequence, head group) segment.
+struct Piece {
+  int seq, hg, len;
+  int t0, t1;         // token range [t0, t1)
+  int ntiles;         // tiles in this piece
+  int seg_tiles;      // tiles in the whole segment
+  int64_t seg_start;  // global index of the segment's first tile
+  bool first;         // first piece of this CTA
 };
 
-template <typename T, int H, int GP, int N, int STAGES>
+// Walks this CTA's tile range segment by segment. Every role runs its own copy
+// and sees the same pieces in the same order.
+struct Walker {
+  int64_t cur, hi;
+  int seq, hg, off;
+  bool started;
+
+  __device__ bool next(const TcParams &tp, Piece &pc) {
+    const DecodeParams &p = tp.p;
+    if (cur >= hi || seq >= p.num_seqs) return false;
+    int len = seq_len_clamped(p, seq);
+    int nt = tiles_of(len);
+    while (nt == 0) {  // zero-length sequences own no tiles
+      if (++seq >= p.num_seqs) return false;
+      hg = 0;
+      off = 0;
+      len = seq_len_clamped(p, seq);
+      nt = tiles_of(len);
+    }
+    const int64_t avail = hi - cur;
+    const int take = (int)((int64_t)(nt - off) < avail ? (int64_t)(nt - off) : avail);
+    pc.seq = seq;
+    pc.hg = hg;
+    pc.len = len;
+    pc.t0 = off * kTile;
+    pc.t1 = min(len, (off + take) * kTile);
+    pc.ntiles = take;
+    pc.seg_tiles = nt;
+    pc.seg_start = cur - off;
+    pc.first = !started;
+    started = true;
+    cur += take;
+    off += take;
+    if (off == nt) {
+      off = 0;
+      if (++hg == tp.head_groups) {
+        hg = 0;
+        ++seq;
+      }
+    }
+    return true;
+  }
+};
+
+template <int N, int SK, int SV>
+struct SmemLayout {
+  static constexpr int kQBytes = 2 * N * 128;  // B operand [N x 128], two K-halves
+  static constexpr int kPBytes = N * 256;      // B operand P^T, MN-major SW32: N/16 atoms x 4 KB
+  static constexpr int kOffK = 0;                               // K ring: SK tiles
+  static constexpr int kOffV = kOffK + SK * kOperandBytes;      // V ring: SV tiles
+  static constexpr int kOffQ = kOffV + SV * kOperandBytes;
+  static constexpr int kOffP = kOffQ + 2 * kQBytes;
+  static constexpr int kOffRedMax = kOffP + 2 * kPBytes;        // float [2][4][N]; prologue scratch
+  static constexpr int kOffRedL = kOffRedMax + 2 * 4 * N * 4;   // float [4][N]
+  static constexpr int kOffBars = kOffRedL + 4 * N * 4;         // uint64 barriers
+  // kfull, kempty [SK]; vfull, vempty [SV]; s_full, s_empty, p_full, p_empty,
+  // o_full, o_empty, q_full, q_empty [2]; mma_done [1]
+  static constexpr int kNumBars = 2 * SK + 2 * SV + 8 * 2 + 1;
+  static constexpr int kOffMisc = kOffBars + kNumBars * 8;  // see MiscSmem
+  static constexpr int kBytes = kOffMisc + 80;
+  static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
+  static_assert(2 * 4 * N * 4 >= 8 * 8, "prologue scan scratch fits the max-reduction buffer");
+};
+
+struct MiscSmem {
+  uint32_t tmem;
+  int abort;
+  int combine[2];
+  int seq0, hg0, off0, pad;
+  long long lo, hi, total, grid;
+};
+
+template <typename T, int H, int GP, int N, int SK, int SV>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
                  const __grid_constant__ CUtensorMap tmap_v, const TcParams tp) {
-  using L = SmemLayout<N, STAGES>;
+  using L = SmemLayout<N, SK, SV>;
   using E = Elem<T>;
-  constexpr int D = 128 / H;                   // head_dim
-  constexpr uint32_t kCols = 4 * N;            // TMEM: S[2] then O[2]
+  constexpr int D = 128 / H;         // head_dim
+  constexpr uint32_t kCols = 4 * N;  // TMEM: S[2] then O[2]
   constexpr uint32_t kFmt = E::kDtype == PAGEDKV_DTYPE_BF16 ? 1u : 0u;
   constexpr uint32_t kIdescS = idesc_f16(kFmt, N, false, false);
-  constexpr uint32_t kIdescO = idesc_f16(kFmt, N, true, false);
+  constexpr uint32_t kIdescO = idesc_f16(kFmt, N, true, true);
   static_assert(H * GP <= N && N % 16 == 0 && N <= 32, "column layout");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bars = sbase + L::kOffBars;
+  // K and V have separate rings: a K tile is released as soon as the S MMA
+  // has read it, a V tile only after the O MMA, so K prefetch runs deeper.
   auto kfull = [&](int s) { return bars + 8u * s; };
-  auto vfull = [&](int s) { return bars + 8u * (STAGES + s); };
-  auto empty = [&](int s) { return bars + 8u * (2 * STAGES + s); };
-  auto bar2 = [&](int which, int b) { return bars + 8u * (3 * STAGES + 2 * which + b); };
+  auto kempty = [&](int s) { return bars + 8u * (SK + s); };
+  auto vfull = [&](int s) { return bars + 8u * (2 * SK + s); };
+  auto vempty = [&](int s) { return bars + 8u * (2 * SK + SV + s); };
+  auto bar2 = [&](int which, int b) { return bars + 8u * (2 * SK + 2 * SV + 2 * which + b); };
   // which: 0 s_full, 1 s_empty, 2 p_full, 3 p_empty, 4 o_full, 5 o_empty, 6 q_full, 7 q_empty
-  const uint32_t mma_done = bars + 8u * (3 * STAGES + 16);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kOffMisc);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::kOffMisc + 4);
-  volatile int *combine_flag = reinterpret_cast<volatile int *>(smem + L::kOffMisc + 8);
+  const uint32_t mma_done = bars + 8u * (2 * SK + 2 * SV + 16);
+  MiscSmem *misc = reinterpret_cast<MiscSmem *>(smem + L::kOffMisc);
+  volatile int *abort_flag = &misc->abort;
   float *red_max = reinterpret_cast<float *>(smem + L::kOffRedMax);
   float *red_l = reinterpret_cast<float *>(smem + L::kOffRedL);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const DecodeParams &p = tp.p;
+#ifdef PAGEDKV_TRACE
+  uint64_t tw[kTraceSlots] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const uint64_t t_kernel0 = globaltimer_ns();
+#endif
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(kfull(s), 1);
+    for (int s = 0; s < SK; ++s) {
+      mbar_init(kfull(s), 1);   // producer arrive.expect_tx + TMA bytes
+      mbar_init(kempty(s), 1);  // MMA commit after S
+    }
+    for (int s = 0; s < SV; ++s) {
       mbar_init(vfull(s), 1);
-      mbar_init(empty(s), 1);
+      mbar_init(vempty(s), 1);  // MMA commit after O
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar2(0, b), 1);    // s_full: MMA commit
@@ -157,25 +253,87 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       mbar_init(bar2(7, b), 1);    // q_empty: MMA commit
     }
     mbar_init(mma_done, 1);
-    *abort_flag = 0;
-    *combine_flag = 0;
+    misc->abort = 0;
+    misc->combine[0] = misc->combine[1] = 0;
     fence_mbarrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), kCols);
+    tmem_alloc(smem_u32(&misc->tmem), kCols);
     tmem_relinquish();
+  }
+
+  // ---- prologue: total tile count and the start of this CTA's range ----------
+  {
+    long long *scan = reinterpret_cast<long long *>(smem + L::kOffRedMax);  // [6] warp sums
+    const int ns = p.num_seqs;
+    const int per = (ns + kThreads - 1) / kThreads;
+    const int s_begin = min(ns, (int)threadIdx.x * per);
+    const int s_end = min(ns, s_begin + per);
+    long long local = 0;
+    for (int s = s_begin; s < s_end; ++s) local += tiles_of(seq_len_clamped(p, s));
+    long long incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) scan[warp] = incl;
+    __syncthreads();
+    long long warp_off = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) {
+      const long long v = scan[w];
+      warp_off += w < warp ? v : 0;
+      total += v;
+    }
+    const long long excl = warp_off + incl - local;  // tiles of sequences before s_begin
+    const long long HG = tp.head_groups;
+    const long long Tt = HG * total;
+    // Effective grid: never more CTAs than tiles, so every participating CTA
+    // owns at least one tile and the owners of a segment are consecutive.
+    const long long Ge = Tt < (long long)gridDim.x ? Tt : (long long)gridDim.x;
+    const long long lo = (long long)blockIdx.x < Ge ? range_lo(blockIdx.x, Tt, Ge) : Tt;
+    const long long hi = (long long)blockIdx.x < Ge ? range_lo(blockIdx.x + 1, Tt, Ge) : Tt;
+    if (threadIdx.x == 0) {
+      misc->lo = lo;
+      misc->hi = hi;
+      misc->total = Tt;
+      misc->grid = Ge;
+      misc->seq0 = ns;  // empty range unless a thread below claims lo
+      misc->hg0 = 0;
+      misc->off0 = 0;
+    }
+    __syncthreads();
+    if (lo < Tt && HG * excl <= lo && lo < HG * (excl + local)) {
+      long long acc_t = HG * excl;
+      for (int s = s_begin; s < s_end; ++s) {
+        const int nt = tiles_of(seq_len_clamped(p, s));
+        if (lo < acc_t + HG * nt) {
+          const long long rel = lo - acc_t;
+          misc->seq0 = s;
+          misc->hg0 = (int)(rel / nt);
+          misc->off0 = (int)(rel % nt);
+          break;
+        }
+        acc_t += HG * nt;
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = misc->tmem;
+  const int64_t T_total = misc->total;
+  const int64_t G = misc->grid;
+  Walker walk{misc->lo, misc->hi, misc->seq0, misc->hg0, misc->off0, false};
 
-  if (warp == 0) {
-    // ---------------------------------------------------------------- producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tmap_k);
-      tma_prefetch_desc(&tmap_v);
-    }
+  if (warp == 0 || warp == 6) {
+    // ------------------------------------------------ producers: warp 0 K (+ Q), warp 6 V
+    const bool is_k = warp == 0;
+    const CUtensorMap *tmap = is_k ? &tmap_k : &tmap_v;
+    const int nst = is_k ? SK : SV;
+    const uint32_t ring = sbase + (is_k ? L::kOffK : L::kOffV);
+    if (lane == 0) tma_prefetch_desc(tmap);
     const uint64_t policy = l2_policy_evict_first();
     const int blocks_per_tile = kTile / p.block_size;
     int stage = 0;
@@ -183,46 +341,45 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     uint32_t qi = 0;
     int issued = 0;
     bool ok = true;
-    for (int item = blockIdx.x; ok && item < tp.total_items; item += gridDim.x) {
-      const Item it = item_info(tp, item);
-      if (it.ntiles == 0) continue;
-      // Stage Q for this item: block-diagonal B operand [N rows x 128], K-major SW128.
-      const uint32_t qb = qi & 1u;
-      if (!mbar_wait(bar2(7, qb), ((qi >> 1) & 1u) ^ 1u, abort_flag, kTimeoutNs)) { ok = false; break; }
-      const uint32_t qbuf = sbase + L::kOffQ + qb * L::kQBytes;
-      for (int idx = lane; idx < 16 * N; idx += 32) {
-        const int xh = idx / (8 * N);
-        const int rem = idx - xh * 8 * N;
-        const int n = rem >> 3, ch = rem & 7;
-        const int hl = n / GP, g = n - hl * GP;
-        const int kv = it.hg * H + hl;
-        uint4 val = make_uint4(0u, 0u, 0u, 0u);
-        if (hl < H && g < p.group && kv < p.hkv && (H == 1 || xh == hl)) {
-          const int d = (H == 1 ? xh * 64 : 0) + ch * 8;
-          val = ldg16(reinterpret_cast<const T *>(p.q) + (int64_t)it.seq * p.q_ss +
-                      (int64_t)(kv * p.group + g) * p.q_sh + d);
+    Piece pc;
+    while (ok && walk.next(tp, pc)) {
+      if (is_k) {
+        // Stage Q for this piece: block-diagonal B operand [N rows x 128], K-major SW128.
+        const uint32_t qb = qi & 1u;
+        if (!PKV_TW(0, mbar_wait(bar2(7, qb), ((qi >> 1) & 1u) ^ 1u, abort_flag, kTimeoutNs))) { ok = false; break; }
+        const uint32_t qbuf = sbase + L::kOffQ + qb * L::kQBytes;
+        for (int idx = lane; idx < 16 * N; idx += 32) {
+          const int xh = idx / (8 * N);
+          const int rem = idx - xh * 8 * N;
+          const int n = rem >> 3, ch = rem & 7;
+          const int hl = n / GP, g = n - hl * GP;
+          const int kv = pc.hg * H + hl;
+          uint4 val = make_uint4(0u, 0u, 0u, 0u);
+          if (hl < H && g < p.group && kv < p.hkv && (H == 1 || xh == hl)) {
+            const int d = (H == 1 ? xh * 64 : 0) + ch * 8;
+            val = ldg16(reinterpret_cast<const T *>(p.q) + (int64_t)pc.seq * p.q_ss +
+                        (int64_t)(kv * p.group + g) * p.q_sh + d);
+          }
+          const uint32_t addr = qbuf + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
+          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(val.x), "r"(val.y),
+                       "r"(val.z), "r"(val.w)
+                       : "memory");
         }
-        const uint32_t addr = qbuf + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
-        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(val.x), "r"(val.y),
-                     "r"(val.z), "r"(val.w)
-                     : "memory");
+        fence_proxy_async_smem();
+        mbar_arrive(bar2(6, qb));
+        ++qi;
       }
-      fence_proxy_async_smem();
-      mbar_arrive(bar2(6, qb));
-      ++qi;
-      const int need_blocks = (it.t1 + p.block_size - 1) / p.block_size;
-      const int32_t *bt = p.bt + (int64_t)it.seq * p.bt_s;
-      const int x0 = it.hg * 128;
-      for (int j = 0; j < it.ntiles; ++j) {
-        if (!mbar_wait(empty(stage), sphase ^ 1u, abort_flag, kTimeoutNs)) { ok = false; break; }
-        if (lane == 0) {
-          mbar_arrive_expect_tx(kfull(stage), kOperandBytes);
-          mbar_arrive_expect_tx(vfull(stage), kOperandBytes);
-        }
+      const int need_blocks = (pc.t1 + p.block_size - 1) / p.block_size;
+      const int32_t *bt = p.bt + (int64_t)pc.seq * p.bt_s;
+      const int x0 = pc.hg * 128;
+      for (int j = 0; j < pc.ntiles; ++j) {
+        const uint32_t full = is_k ? kfull(stage) : vfull(stage);
+        const uint32_t emp = is_k ? kempty(stage) : vempty(stage);
+        if (!PKV_TW(1, mbar_wait(emp, sphase ^ 1u, abort_flag, kTimeoutNs))) { ok = false; break; }
+        if (lane == 0) mbar_arrive_expect_tx(full, kOperandBytes);
         __syncwarp();
-        const int lb0 = (it.t0 + j * kTile) / p.block_size;
-        const uint32_t kdst = sbase + L::kOffK + stage * kOperandBytes;
-        const uint32_t vdst = sbase + L::kOffV + stage * kOperandBytes;
+        const int lb0 = (pc.t0 + j * kTile) / p.block_size;
+        const uint32_t dst = ring + stage * kOperandBytes;
         for (int bi = lane; bi < blocks_per_tile; bi += 32) {
           const int lb = lb0 + bi;
           int32_t y = tp.oob_row;  // out of range: TMA fills zeros, reads nothing
@@ -230,46 +387,42 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
             const int blk = __ldg(bt + lb);
             if (blk >= 0 && (int64_t)blk < p.num_blocks) {
               y = blk * p.block_size;
-            } else {
+            } else if (is_k) {
               set_error(p.err, PAGEDKV_EFLAG_BLOCK_ID_RANGE);
             }
           }
           const uint32_t off = bi * p.block_size * 128;
-#pragma unroll
-          for (int xh = 0; xh < 2; ++xh) {
-            tma_load_2d(kdst + xh * kHalfBytes + off, &tmap_k, x0 + xh * 64, y, kfull(stage), policy);
-            tma_load_2d(vdst + xh * kHalfBytes + off, &tmap_v, x0 + xh * 64, y, vfull(stage), policy);
-          }
+          tma_load_2d(dst + off, tmap, x0, y, full, policy);
+          tma_load_2d(dst + kHalfBytes + off, tmap, x0 + 64, y, full, policy);
         }
         ++issued;
-        if (++stage == STAGES) {
+        if (++stage == nst) {
           stage = 0;
           sphase ^= 1u;
         }
       }
     }
-    // Drain: the last min(issued, STAGES) tiles' loads must have landed before
-    // this CTA's shared memory is released (immediate on the normal path).
-    for (int k = 0; k < STAGES && k < issued; ++k) {
+    // Drain: the last min(issued, ring size) tiles' loads must have landed
+    // before this CTA's shared memory is released (immediate on the normal path).
+    for (int k = 0; k < nst && k < issued; ++k) {
       if (--stage < 0) {
-        stage = STAGES - 1;
+        stage = nst - 1;
         sphase ^= 1u;
       }
       volatile int never = 0;
-      mbar_wait(kfull(stage), sphase, &never, kTimeoutNs / 4);
-      mbar_wait(vfull(stage), sphase, &never, kTimeoutNs / 4);
+      mbar_wait(is_k ? kfull(stage) : vfull(stage), sphase, &never, kTimeoutNs / 4);
     }
   } else if (warp == 1) {
     // --------------------------------------------------------------- MMA issuer
-    int stage = 0;
-    uint32_t sphase = 0;
+    int kst = 0, vst = 0;  // K / V ring positions of the current tile
+    uint32_t kph = 0, vph = 0;
     uint32_t gt = 0;  // global tile counter (S/P/O double buffers)
     uint32_t qi = 0;
     bool ok = true;
     auto issue_s = [&](int st, uint32_t ph, uint32_t g, uint32_t qbuf) -> bool {
       const uint32_t b = g & 1u;
-      if (!mbar_wait(kfull(st), ph, abort_flag, kTimeoutNs)) return false;
-      if (!mbar_wait(bar2(1, b), ((g >> 1) & 1u) ^ 1u, abort_flag, kTimeoutNs)) return false;
+      if (!PKV_TW(1, mbar_wait(kfull(st), ph, abort_flag, kTimeoutNs))) return false;
+      if (!PKV_TW(2, mbar_wait(bar2(1, b), ((g >> 1) & 1u) ^ 1u, abort_flag, kTimeoutNs))) return false;
       tc_fence_after();
       if (lane == 0) {
         const uint32_t ka = sbase + L::kOffK + st * kOperandBytes;
@@ -279,37 +432,38 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           const uint64_t bd = smem_desc_sw128(qbuf + (kk >> 2) * (N * 128) + (kk & 3) * 32, 16, 1024);
           mma_f16_ss(tmem + b * N, ad, bd, kIdescS, kk > 0 ? 1u : 0u);
         }
-        mma_commit(bar2(0, b));
+        mma_commit(bar2(0, b));  // s_full
+        mma_commit(kempty(st));  // K tile read: free it for the next load
       }
       __syncwarp();
       return true;
     };
-    for (int item = blockIdx.x; ok && item < tp.total_items; item += gridDim.x) {
-      const Item it = item_info(tp, item);
-      if (it.ntiles == 0) continue;
+    Piece pc;
+    while (ok && walk.next(tp, pc)) {
       const uint32_t qb = qi & 1u;
-      if (!mbar_wait(bar2(6, qb), (qi >> 1) & 1u, abort_flag, kTimeoutNs)) { ok = false; break; }
+      if (!PKV_TW(0, mbar_wait(bar2(6, qb), (qi >> 1) & 1u, abort_flag, kTimeoutNs))) { ok = false; break; }
       const uint32_t qbuf = sbase + L::kOffQ + qb * L::kQBytes;
-      if (!issue_s(stage, sphase, gt, qbuf)) { ok = false; break; }
-      for (int j = 0; j < it.ntiles; ++j) {
+      if (!issue_s(kst, kph, gt, qbuf)) { ok = false; break; }
+      for (int j = 0; j < pc.ntiles; ++j) {
         const uint32_t b = gt & 1u;
         const uint32_t bph = (gt >> 1) & 1u;
-        int nstage = stage + 1;
-        uint32_t nphase = sphase;
-        if (nstage == STAGES) {
-          nstage = 0;
-          nphase ^= 1u;
+        int nkst = kst + 1;
+        uint32_t nkph = kph;
+        if (nkst == SK) {
+          nkst = 0;
+          nkph ^= 1u;
         }
-        if (j + 1 < it.ntiles) {
-          if (!issue_s(nstage, nphase, gt + 1, qbuf)) { ok = false; break; }
+        if (j + 1 < pc.ntiles) {
+          if (!issue_s(nkst, nkph, gt + 1, qbuf)) { ok = false; break; }
         }
-        if (!mbar_wait(vfull(stage), sphase, abort_flag, kTimeoutNs)) { ok = false; break; }
-        const uint32_t va = sbase + L::kOffV + stage * kOperandBytes;
+        if (!PKV_TW(3, mbar_wait(vfull(vst), vph, abort_flag, kTimeoutNs))) { ok = false; break; }
+        const uint32_t va = sbase + L::kOffV + vst * kOperandBytes;
         // Rows of the last block past the sequence end hold stale pool data:
         // zero them so 0 * (non-finite stale value) never reaches the sum.
-        if (j == it.ntiles - 1 && it.t1 == it.len && (it.len % p.block_size) != 0) {
-          const int r0 = it.len - (it.t0 + j * kTile);  // first stale row in the tile
-          const int r1 = ((it.len + p.block_size - 1) / p.block_size) * p.block_size - (it.t0 + j * kTile);
+        const int tile_t0 = pc.t0 + j * kTile;
+        if (pc.t1 == pc.len && tile_t0 + kTile >= pc.len && (pc.len % p.block_size) != 0) {
+          const int r0 = pc.len - tile_t0;  // first stale row in the tile
+          const int r1 = ((pc.len + p.block_size - 1) / p.block_size) * p.block_size - tile_t0;
           const int chunks = (r1 - r0) * 8 * 2;
           for (int idx = lane; idx < chunks; idx += 32) {
             const int xh = idx / ((r1 - r0) * 8);
@@ -320,8 +474,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           fence_proxy_async_smem();
           __syncwarp();
         }
-        if (!mbar_wait(bar2(2, b), bph, abort_flag, kTimeoutNs)) { ok = false; break; }
-        if (!mbar_wait(bar2(5, b), bph ^ 1u, abort_flag, kTimeoutNs)) { ok = false; break; }
+        if (!PKV_TW(4, mbar_wait(bar2(2, b), bph, abort_flag, kTimeoutNs))) { ok = false; break; }
+        if (!PKV_TW(5, mbar_wait(bar2(5, b), bph ^ 1u, abort_flag, kTimeoutNs))) { ok = false; break; }
         tc_fence_after();
         if (lane == 0) {
           const uint32_t pbuf = sbase + L::kOffP + b * L::kPBytes;
@@ -329,18 +483,23 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           for (int kk = 0; kk < 8; ++kk) {
             // A = V^T: MN-major SW128, 64-element atoms 16 KB apart (LBO), 8-token groups 1 KB apart (SBO)
             const uint64_t ad = smem_desc_sw128(va + kk * 2048, kHalfBytes, 1024);
-            const uint64_t bd = smem_desc_sw128(pbuf + (kk >> 2) * (N * 128) + (kk & 3) * 32, 16, 1024);
+            // B = P^T: MN-major SW32, 16-column atoms 4 KB apart (LBO), 8-token groups 256 B apart (SBO)
+            const uint64_t bd = smem_desc(pbuf + kk * 512, 4096, 256, kLayoutSwizzle32);
             mma_f16_ss(tmem + 2 * N + b * N, ad, bd, kIdescO, kk > 0 ? 1u : 0u);
           }
-          mma_commit(bar2(4, b));   // o_full
-          mma_commit(empty(stage));  // K/V stage free
-          mma_commit(bar2(3, b));   // p_empty
-          if (j == it.ntiles - 1) mma_commit(bar2(7, qb));  // q_empty
+          mma_commit(bar2(4, b));  // o_full
+          mma_commit(vempty(vst));  // V tile read
+          mma_commit(bar2(3, b));  // p_empty
+          if (j == pc.ntiles - 1) mma_commit(bar2(7, qb));  // q_empty
         }
         __syncwarp();
         ++gt;
-        stage = nstage;
-        sphase = nphase;
+        kst = nkst;
+        kph = nkph;
+        if (++vst == SV) {
+          vst = 0;
+          vph ^= 1u;
+        }
       }
       ++qi;
     }
@@ -351,20 +510,34 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     mbar_wait(mma_done, 0, &never, kTimeoutNs / 4);
   } else {
     // ------------------------------------------------- softmax / correction / epilogue
-    const int q4 = warp & 3;            // TMEM lane quarter of this warp
-    const int row = q4 * 32 + lane;     // TMEM lane: token row (S) / (kv head, dim) row (O)
+    const int q4 = warp & 3;         // TMEM lane quarter of this warp
+    const int row = q4 * 32 + lane;  // TMEM lane: token row (S) / (kv head, dim) row (O)
     const int hl = H == 2 ? (row >> 6) : 0;
     const int dim = H == 2 ? (row & 63) : row;
     const uint32_t tl = tmem + ((uint32_t)(q4 * 32) << 16);
+    const int HQS = H * p.group;  // query heads per segment
     uint32_t gt = 0;
     int red_buf = 0;
-    for (int item = blockIdx.x; item < tp.total_items; item += gridDim.x) {
-      const Item it = item_info(tp, item);
-      if (it.ntiles == 0 && !(it.len == 0 && it.c == 0)) continue;
-      if (it.c == 0 && row == 0 && it.hg == 0) {
-        int raw = p.lens ? __ldg(p.lens + it.seq) : p.uniform_len;
-        if (raw > p.max_blocks * p.block_size) set_error(p.err, PAGEDKV_EFLAG_SEQ_LEN_RANGE);
+
+    // Sequences of length 0 own no tiles: CTA (seq % grid) writes their zeros.
+    for (int s = blockIdx.x; s < p.num_seqs; s += gridDim.x) {
+      const int raw = p.lens ? __ldg(p.lens + s) : p.uniform_len;
+      if (raw > p.max_blocks * p.block_size && row == 0) set_error(p.err, PAGEDKV_EFLAG_SEQ_LEN_RANGE);
+      if (seq_len_clamped(p, s) == 0) {
+        T *out = reinterpret_cast<T *>(p.out) + (int64_t)s * p.o_ss;
+        for (int idx = row; idx < p.hq * D; idx += 128)
+          out[(int64_t)(idx / D) * p.o_sh + idx % D] = E::from_float(0.f);
       }
+    }
+
+    // Up to two pieces of this CTA are cut segments; their fence / arrival /
+    // combine is deferred to the end so it never stalls the tile pipeline.
+    int n_pend = 0;
+    int64_t pend_start[2] = {0, 0};
+    int pend_tiles[2] = {0, 0}, pend_seq[2] = {0, 0}, pend_hg[2] = {0, 0};
+
+    Piece pc;
+    while (walk.next(tp, pc)) {
       float m_run[N], l_part[N], alpha_prev[N], acc[GP];
 #pragma unroll
       for (int n = 0; n < N; ++n) {
@@ -381,7 +554,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       // PIPE_TIMEOUT bit.
       auto correction = [&](uint32_t g_tile) {
         const uint32_t b = g_tile & 1u;
-        mbar_wait(bar2(4, b), (g_tile >> 1) & 1u, abort_flag, kTimeoutNs);
+        PKV_TW(3, mbar_wait(bar2(4, b), (g_tile >> 1) & 1u, abort_flag, kTimeoutNs));
         tc_fence_after();
         float o[GP];
         tmem_ld<GP>(tl + 2 * N + b * N + hl * GP, o);
@@ -395,10 +568,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         }
       };
 
-      for (int j = 0; j < it.ntiles; ++j) {
+      for (int j = 0; j < pc.ntiles; ++j) {
         const uint32_t b = gt & 1u;
         const uint32_t bph = (gt >> 1) & 1u;
-        mbar_wait(bar2(0, b), bph, abort_flag, kTimeoutNs);
+        PKV_TW(0, mbar_wait(bar2(0, b), bph, abort_flag, kTimeoutNs));
+        PKV_TADD(5, 1);
         tc_fence_after();
         float s[N];
         tmem_ld<N>(tl + b * N, s);
@@ -406,20 +580,35 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         tc_fence_before();
         mbar_arrive(bar2(1, b));
 
-        const bool valid = it.t0 + j * kTile + row < it.t1;
+        const bool valid = pc.t0 + j * kTile + row < pc.t1;
         float *rm = red_max + red_buf * 4 * N;
+        float wm[N];
 #pragma unroll
         for (int n = 0; n < N; ++n) {
           s[n] = valid ? s[n] * p.scale_log2 : kNegInf;
-          const float wm = warp_max(s[n]);
-          if (lane == 0) rm[q4 * N + n] = wm;
+          wm[n] = warp_max(s[n]);
+        }
+        if (lane == 0) {
+#pragma unroll
+          for (int n = 0; n < N; n += 4)
+            *reinterpret_cast<float4 *>(rm + q4 * N + n) = make_float4(wm[n], wm[n + 1], wm[n + 2], wm[n + 3]);
         }
         named_bar(1, 128);
+#pragma unroll
+        for (int n = 0; n < N; n += 4) {
+          const float4 a0 = *reinterpret_cast<const float4 *>(rm + n);
+          const float4 a1 = *reinterpret_cast<const float4 *>(rm + N + n);
+          const float4 a2 = *reinterpret_cast<const float4 *>(rm + 2 * N + n);
+          const float4 a3 = *reinterpret_cast<const float4 *>(rm + 3 * N + n);
+          wm[n] = fmaxf(fmaxf(a0.x, a1.x), fmaxf(a2.x, a3.x));
+          wm[n + 1] = fmaxf(fmaxf(a0.y, a1.y), fmaxf(a2.y, a3.y));
+          wm[n + 2] = fmaxf(fmaxf(a0.z, a1.z), fmaxf(a2.z, a3.z));
+          wm[n + 3] = fmaxf(fmaxf(a0.w, a1.w), fmaxf(a2.w, a3.w));
+        }
         float alpha[N];
 #pragma unroll
         for (int n = 0; n < N; ++n) {
-          const float mt = fmaxf(fmaxf(rm[n], rm[N + n]), fmaxf(rm[2 * N + n], rm[3 * N + n]));
-          const float mn = fmaxf(m_run[n], mt);
+          const float mn = fmaxf(m_run[n], wm[n]);
           alpha[n] = mn == kNegInf ? 1.f : exp2f(m_run[n] - mn);
           // The denominator sums P as rounded for the MMA, so the normalisation
           // matches the numerator exactly.
@@ -429,16 +618,25 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           m_run[n] = mn;
         }
         red_buf ^= 1;
-        mbar_wait(bar2(3, b), bph ^ 1u, abort_flag, kTimeoutNs);
-        // P^T as the B operand [N x 128 tokens], K-major SW128: token `row` of column n.
-        const uint32_t pbuf = sbase + L::kOffP + b * L::kPBytes + (row >> 6) * (N * 128);
-        const int tr = row & 63;
+        PKV_TW(2, mbar_wait(bar2(3, b), bph ^ 1u, abort_flag, kTimeoutNs));
+        // P^T as the B operand [128 tokens x N], MN-major with 32-byte swizzle:
+        // token `row` owns 32 contiguous bytes (16 columns) in each 16-column
+        // atom, its two 16-byte halves swapped on rows 4-7 of every 8.
+        const uint32_t prow = sbase + L::kOffP + b * L::kPBytes + (row >> 3) * 256 + (row & 7) * 32;
+        const uint32_t sw = (row >> 2) & 1;
 #pragma unroll
-        for (int n = 0; n < N; ++n) {
-          const uint32_t addr = pbuf + (n >> 3) * 1024 + (n & 7) * 128 + ((((tr >> 3) ^ (n & 7))) << 4) + (tr & 7) * 2;
-          const T hv = E::from_float(s[n]);
-          asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(*reinterpret_cast<const uint16_t *>(&hv))
-                       : "memory");
+        for (int a = 0; a < N / 16; ++a) {
+#pragma unroll
+          for (int h8 = 0; h8 < 2; ++h8) {
+            float v8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v8[i] = s[a * 16 + h8 * 8 + i];
+            const uint4 pk = E::pack8(v8);
+            const uint32_t addr = prow + a * 4096 + ((h8 ^ sw) << 4);
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(pk.x), "r"(pk.y), "r"(pk.z),
+                         "r"(pk.w)
+                         : "memory");
+          }
         }
         fence_proxy_async_smem();
         mbar_arrive(bar2(2, b));
@@ -447,9 +645,13 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         for (int n = 0; n < N; ++n) alpha_prev[n] = alpha[n];
         ++gt;
       }
-      if (it.ntiles > 0) correction(gt - 1);
+      if (pc.ntiles > 0) correction(gt - 1);
+#ifdef PAGEDKV_TRACE
+      const uint64_t t_epi0 = globaltimer_ns();
+      tw[6] += 1;
+#endif
 
-      // ---- epilogue: denominators across the 128 rows
+      // ---- per-piece epilogue: denominators across the 128 rows
 #pragma unroll
       for (int n = 0; n < N; ++n) {
         float v = l_part[n];
@@ -461,20 +663,20 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       float l_sel[GP], m_sel[GP];
 #pragma unroll
       for (int g = 0; g < GP; ++g) {
-        const int n0 = g, n1 = GP + g;
+        const int n0 = g, n1 = (GP + g) % N;
         const float l0 = red_l[n0] + red_l[N + n0] + red_l[2 * N + n0] + red_l[3 * N + n0];
         float l1 = 0.f;
-        if (H == 2) l1 = red_l[n1 % N] + red_l[N + n1 % N] + red_l[2 * N + n1 % N] + red_l[3 * N + n1 % N];
+        if (H == 2) l1 = red_l[n1] + red_l[N + n1] + red_l[2 * N + n1] + red_l[3 * N + n1];
         l_sel[g] = (H == 2 && hl == 1) ? l1 : l0;
-        m_sel[g] = (H == 2 && hl == 1) ? m_run[(GP + g) % N] : m_run[g];
+        m_sel[g] = (H == 2 && hl == 1) ? m_run[n1] : m_run[g];
       }
-      named_bar(1, 128);  // red_l is rewritten by the next item
+      named_bar(1, 128);  // red_l is rewritten by the next piece
 
-      const int kv = it.hg * H + hl;
+      const int kv = pc.hg * H + hl;
       const bool have = kv < p.hkv;
-      if (it.nck <= 1) {
+      if (pc.ntiles == pc.seg_tiles) {
         if (have) {
-          T *out = reinterpret_cast<T *>(p.out) + (int64_t)it.seq * p.o_ss + dim;
+          T *out = reinterpret_cast<T *>(p.out) + (int64_t)pc.seq * p.o_ss + dim;
 #pragma unroll
           for (int g = 0; g < GP; ++g) {
             if (g < p.group) {
@@ -484,50 +686,118 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           }
         }
       } else {
+        const int64_t slot = 2 * (int64_t)blockIdx.x + (pc.first ? 0 : 1);
         if (have) {
 #pragma unroll
           for (int g = 0; g < GP; ++g) {
             if (g < p.group) {
-              const int64_t slot = ((int64_t)it.seq * p.hq + kv * p.group + g) * p.num_splits + it.c;
-              p.ws_acc[slot * D + dim] = acc[g];
-              if (dim == 0) p.ws_ml[slot] = make_float2(m_sel[g], l_sel[g]);
+              const int64_t hh = slot * HQS + hl * p.group + g;
+              tp.part_acc[hh * D + dim] = acc[g];
+              if (dim == 0) tp.part_ml[hh] = make_float2(m_sel[g], l_sel[g]);
             }
           }
         }
-        __threadfence();
-        named_bar(1, 128);
-        if (row == 0) {
-          const int prev = atomicAdd(tp.counters + (int64_t)it.seq * tp.head_groups + it.hg, 1);
-          *combine_flag = prev == it.nck - 1 ? 1 : 0;
+        if (n_pend < 2) {
+          pend_start[n_pend] = pc.seg_start;
+          pend_tiles[n_pend] = pc.seg_tiles;
+          pend_seq[n_pend] = pc.seq;
+          pend_hg[n_pend] = pc.hg;
         }
-        named_bar(1, 128);
-        if (*combine_flag) {
-          __threadfence();
-          if (have) {
-            T *out = reinterpret_cast<T *>(p.out) + (int64_t)it.seq * p.o_ss + dim;
-            for (int g = 0; g < p.group && g < GP; ++g) {
-              const int64_t slot0 = ((int64_t)it.seq * p.hq + kv * p.group + g) * p.num_splits;
-              float mm = kNegInf;
-              for (int cc = 0; cc < it.nck; ++cc) mm = fmaxf(mm, __ldcg(&p.ws_ml[slot0 + cc].x));
-              float ll = 0.f, a = 0.f;
-              if (mm != kNegInf) {
-                for (int cc = 0; cc < it.nck; ++cc) {
-                  const float2 ml = __ldcg(&p.ws_ml[slot0 + cc]);
-                  const float f = exp2f(ml.x - mm);
-                  ll = fmaf(f, ml.y, ll);
-                  a = fmaf(f, __ldcg(&p.ws_acc[(slot0 + cc) * D + dim]), a);
-                }
-              }
-              out[(int64_t)(kv * p.group + g) * p.o_sh] = E::from_float(ll > 0.f ? a / ll : 0.f);
-            }
-          }
-        }
-        named_bar(1, 128);  // combine_flag is rewritten by the next item
+        ++n_pend;
       }
+#ifdef PAGEDKV_TRACE
+      tw[4] += globaltimer_ns() - t_epi0;
+#endif
+    }
+
+    // ---- cut segments: publish this CTA's partials, the last arrival combines
+    if (n_pend > 0) {
+#ifdef PAGEDKV_TRACE
+      const uint64_t t_fin0 = globaltimer_ns();
+#endif
+      named_bar(1, 128);  // every partial store of this CTA issued
+      if (row == 0) {
+        __threadfence();  // release them (cumulative over the barrier) before arriving
+        bool any = false;
+        for (int k = 0; k < n_pend && k < 2; ++k) {
+          const int64_t seg = (int64_t)pend_seq[k] * tp.head_groups + pend_hg[k];
+          const int pieces = (int)(owner_of(pend_start[k] + pend_tiles[k] - 1, T_total, G) -
+                                   owner_of(pend_start[k], T_total, G) + 1);
+          const int prev = atomicAdd(tp.counters + seg, 1);
+          misc->combine[k] = prev == pieces - 1 ? 1 : 0;
+          any |= misc->combine[k] != 0;
+        }
+        if (any) __threadfence();  // acquire the other CTAs' partials
+      }
+      named_bar(1, 128);
+#ifdef PAGEDKV_TRACE
+      tw[1] += globaltimer_ns() - t_fin0;
+#endif
+      for (int k = 0; k < n_pend && k < 2; ++k) {
+        if (!misc->combine[k]) continue;
+        const int kv = pend_hg[k] * H + hl;
+        if (kv >= p.hkv) continue;
+        const int64_t b0 = owner_of(pend_start[k], T_total, G);
+        const int64_t b1 = owner_of(pend_start[k] + pend_tiles[k] - 1, T_total, G);
+        // CTA b0 reached this segment after another piece unless its range starts here.
+        const bool b0_second = range_lo(b0, T_total, G) < pend_start[k];
+        // Piece-outer: every head's (m, l) and partial sum of one piece are
+        // loaded together, so each piece costs one round trip to L2.
+        float mm[GP], ll[GP], a[GP], res[GP];
+#pragma unroll
+        for (int g = 0; g < GP; ++g) {
+          mm[g] = kNegInf;
+          ll[g] = 0.f;
+          a[g] = 0.f;
+        }
+        for (int64_t bb = b0; bb <= b1; ++bb) {
+          const int64_t slot = 2 * bb + ((bb == b0 && b0_second) ? 1 : 0);
+          const int64_t hh0 = slot * HQS + hl * p.group;
+          float2 ml[GP];
+          float av[GP];
+#pragma unroll
+          for (int g = 0; g < GP; ++g) {
+            ml[g] = make_float2(kNegInf, 0.f);
+            av[g] = 0.f;
+            if (g < p.group) {
+              ml[g] = __ldcg(&tp.part_ml[hh0 + g]);
+              av[g] = __ldcg(&tp.part_acc[(hh0 + g) * D + dim]);
+            }
+          }
+#pragma unroll
+          for (int g = 0; g < GP; ++g) {
+            const float mb = fmaxf(mm[g], ml[g].x);
+            const float sc = mm[g] == kNegInf ? 0.f : exp2f(mm[g] - mb);
+            const float f = ml[g].x == kNegInf ? 0.f : exp2f(ml[g].x - mb);
+            ll[g] = fmaf(f, ml[g].y, ll[g] * sc);
+            a[g] = fmaf(f, av[g], a[g] * sc);
+            mm[g] = mb;
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < GP; ++g) res[g] = ll[g] > 0.f ? a[g] / ll[g] : 0.f;
+        T *out = reinterpret_cast<T *>(p.out) + (int64_t)pend_seq[k] * p.o_ss + dim;
+#pragma unroll
+        for (int g = 0; g < GP; ++g)
+          if (g < p.group) out[(int64_t)(kv * p.group + g) * p.o_sh] = E::from_float(res[g]);
+      }
+#ifdef PAGEDKV_TRACE
+      tw[7] += globaltimer_ns() - t_fin0;
+#endif
     }
   }
 
   // ---------------------------------------------------------------- teardown
+#ifdef PAGEDKV_TRACE
+  if (blockIdx.x < kTraceCtas && lane == 0 && warp <= 2) {
+    for (int i = 0; i < kTraceSlots; ++i) g_trace[blockIdx.x][warp][i] = tw[i];
+    if (warp == 0) {
+      g_trace[blockIdx.x][3][0] = globaltimer_ns() - t_kernel0;
+      g_trace[blockIdx.x][3][1] = t_kernel0;
+      g_trace[blockIdx.x][3][2] = (unsigned long long)(misc->hi - misc->lo);
+    }
+  }
+#endif
   if (threadIdx.x == 0 && *abort_flag) set_error(p.err, PAGEDKV_EFLAG_PIPE_TIMEOUT);
   tc_fence_before();
   __syncthreads();
@@ -540,7 +810,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 // ---- host side ----------------------------------------------------------------
 
 struct TcPlan {
-  int H, GP, N, stages, head_groups, chunk, num_chunks;
+  int H, GP, N, stages, head_groups, grid;
 };
 
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
@@ -554,26 +824,24 @@ TcPlan make_plan(int32_t num_seqs, int32_t hq, int32_t hkv, int32_t head_dim, in
   pl.N = round_up(pl.H * pl.GP, 16);
   pl.stages = pl.N <= 16 ? 3 : 2;
   pl.head_groups = (hkv + pl.H - 1) / pl.H;
-  const int mt = max_tokens > 0 ? max_tokens : 1;
-  int chunk = round_up(mt, kTile);
-  const int64_t want = (int64_t)num_sms * 4;
-  while (chunk > 2 * kTile) {
-    const int64_t items = (int64_t)num_seqs * pl.head_groups * ((mt + chunk - 1) / chunk);
-    if (items >= want) break;
-    chunk = round_up(chunk / 2, kTile);
-  }
-  pl.chunk = chunk;
-  pl.num_chunks = (mt + chunk - 1) / chunk;
+  const int64_t max_tiles = ((int64_t)(max_tokens > 0 ? max_tokens : 1) + kTile - 1) / kTile;
+  const int64_t tiles_upper = (int64_t)num_seqs * pl.head_groups * max_tiles;
+  int grid = num_sms;
+#ifdef PAGEDKV_TRACE
+  if (const char *e = getenv("PAGEDKV_TRACE_GRID")) grid = atoi(e);
+#endif
+  pl.grid = (int)(tiles_upper < grid ? tiles_upper : grid);
+  if (pl.grid < 1) pl.grid = 1;
   return pl;
 }
 
-size_t plan_workspace(const TcPlan &pl, int32_t num_seqs, int32_t hq, int32_t head_dim) {
-  if (pl.num_chunks <= 1) return 0;
-  const size_t slots = (size_t)num_seqs * hq * pl.num_chunks;
-  const size_t acc = ((slots * head_dim * sizeof(float) + 255) / 256) * 256;
-  const size_t ml = ((slots * sizeof(float2) + 255) / 256) * 256;
-  const size_t cnt = (size_t)num_seqs * pl.head_groups * sizeof(int32_t);
-  return acc + ml + cnt;
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+size_t plan_workspace(const TcPlan &pl, int32_t num_seqs, int32_t hq, int32_t hkv, int32_t head_dim) {
+  const size_t hqs = (size_t)pl.H * (hq / hkv);
+  const size_t slots = 2 * (size_t)pl.grid;
+  return align256(slots * hqs * head_dim * sizeof(float)) + align256(slots * hqs * sizeof(float2)) +
+         align256((size_t)num_seqs * pl.head_groups * sizeof(int32_t));
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -589,8 +857,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-bool make_map(CUtensorMap *map, const void *base, int dtype, uint64_t row_elems, uint64_t rows,
-              uint32_t box_rows) {
+bool encode_map(CUtensorMap *map, const void *base, int dtype, uint64_t row_elems, uint64_t rows,
+                uint32_t box_rows) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {row_elems, rows};
@@ -604,28 +872,84 @@ bool make_map(CUtensorMap *map, const void *base, int dtype, uint64_t row_elems,
   return r == CUDA_SUCCESS;
 }
 
-template <typename T, int H, int GP, int N, int STAGES>
+// Encoded tensor maps of recently used pools (a decode step reuses the same
+// per-layer K/V tensors every step), keyed by everything the encoding reads.
+struct MapKey {
+  const void *base;
+  uint64_t row_elems, rows;
+  uint32_t box_rows;
+  int dtype;
+  bool operator==(const MapKey &o) const {
+    return base == o.base && row_elems == o.row_elems && rows == o.rows && box_rows == o.box_rows &&
+           dtype == o.dtype;
+  }
+};
+
+bool make_map(CUtensorMap *map, const void *base, int dtype, uint64_t row_elems, uint64_t rows,
+              uint32_t box_rows) {
+  constexpr int kSlots = 128;
+  static std::mutex mu;
+  static MapKey keys[kSlots];
+  static CUtensorMap maps[kSlots];
+  static int used = 0, next = 0;
+  const MapKey key{base, row_elems, rows, box_rows, dtype};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    for (int i = 0; i < used; ++i) {
+      if (keys[i] == key) {
+        *map = maps[i];
+        return true;
+      }
+    }
+  }
+  if (!encode_map(map, base, dtype, row_elems, rows, box_rows)) return false;
+  std::lock_guard<std::mutex> lk(mu);
+  keys[next] = key;
+  maps[next] = *map;
+  next = (next + 1) % kSlots;
+  if (used < kSlots) ++used;
+  return true;
+}
+
+template <typename T, int H, int GP, int N, int SK, int SV>
 cudaError_t launch_tc(const CUtensorMap &mk, const CUtensorMap &mv, const TcParams &tp, int grid,
                       cudaStream_t stream) {
-  using L = SmemLayout<N, STAGES>;
-  auto kern = decode_tc_kernel<T, H, GP, N, STAGES>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+  using L = SmemLayout<N, SK, SV>;
+  auto kern = decode_tc_kernel<T, H, GP, N, SK, SV>;
+  // The shared-memory opt-in is a per-device function attribute: set it once
+  // per device (outside any stream capture that follows the first call).
+  static std::atomic<uint64_t> attr_done{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_done.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return e;
+    attr_done.fetch_or(bit, std::memory_order_acq_rel);
+  }
   kern<<<grid, kThreads, L::kAlloc, stream>>>(mk, mv, tp);
   return cudaGetLastError();
 }
 
 template <typename T>
 cudaError_t dispatch_tc(const TcPlan &pl, const CUtensorMap &mk, const CUtensorMap &mv, const TcParams &tp,
-                        int grid, cudaStream_t stream) {
-  if (pl.H == 2 && pl.GP == 8) return launch_tc<T, 2, 8, 16, 3>(mk, mv, tp, grid, stream);
-  if (pl.H == 2 && pl.GP == 16) return launch_tc<T, 2, 16, 32, 2>(mk, mv, tp, grid, stream);
-  if (pl.H == 1 && pl.GP == 8) return launch_tc<T, 1, 8, 16, 3>(mk, mv, tp, grid, stream);
-  if (pl.H == 1 && pl.GP == 16) return launch_tc<T, 1, 16, 16, 3>(mk, mv, tp, grid, stream);
+                        cudaStream_t stream) {
+  if (pl.H == 2 && pl.GP == 8) return launch_tc<T, 2, 8, 16, 3, 3>(mk, mv, tp, pl.grid, stream);
+  if (pl.H == 2 && pl.GP == 16) return launch_tc<T, 2, 16, 32, 2, 2>(mk, mv, tp, pl.grid, stream);
+  if (pl.H == 1 && pl.GP == 8) return launch_tc<T, 1, 8, 16, 3, 3>(mk, mv, tp, pl.grid, stream);
+  if (pl.H == 1 && pl.GP == 16) return launch_tc<T, 1, 16, 16, 3, 3>(mk, mv, tp, pl.grid, stream);
   return cudaErrorInvalidValue;
 }
 
 }  // namespace
+
+#ifdef PAGEDKV_TRACE
+extern "C" int pagedkv_trace_read(unsigned long long *host, size_t count) {
+  const size_t n = sizeof(g_trace) / sizeof(unsigned long long);
+  return cudaMemcpyFromSymbol(host, g_trace, (count < n ? count : n) * sizeof(unsigned long long)) == cudaSuccess ? 0 : 3;
+}
+#endif
 
 bool tc_eligible(int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size) {
   if (num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return false;
@@ -639,7 +963,7 @@ bool tc_eligible(int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, in
 size_t tc_workspace_bytes(int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
                           int32_t max_tokens, int32_t num_sms) {
   const TcPlan pl = make_plan(num_seqs, num_q_heads, num_kv_heads, head_dim, max_tokens, num_sms);
-  return plan_workspace(pl, num_seqs, num_q_heads, head_dim);
+  return plan_workspace(pl, num_seqs, num_q_heads, num_kv_heads, head_dim);
 }
 
 int tc_launch(DecodeParams &p, int dtype, void *workspace, size_t workspace_bytes, int32_t num_sms,
@@ -647,8 +971,8 @@ int tc_launch(DecodeParams &p, int dtype, void *workspace, size_t workspace_byte
   *launches = 0;
   const int32_t max_tokens = p.max_blocks * p.block_size;
   const TcPlan pl = make_plan(p.num_seqs, p.hq, p.hkv, p.head_dim, max_tokens, num_sms);
-  const size_t need = plan_workspace(pl, p.num_seqs, p.hq, p.head_dim);
-  if (need > workspace_bytes) {
+  const size_t need = plan_workspace(pl, p.num_seqs, p.hq, p.hkv, p.head_dim);
+  if (need > workspace_bytes || workspace == nullptr) {
     *error = "tensor-core decode: workspace too small";
     return PAGEDKV_ERR_WORKSPACE;
   }
@@ -665,40 +989,29 @@ int tc_launch(DecodeParams &p, int dtype, void *workspace, size_t workspace_byte
     return PAGEDKV_ERR_CUDA;
   }
   TcParams tp{};
-  p.split_tokens = pl.chunk;
-  p.num_splits = pl.num_chunks;
   tp.head_groups = pl.head_groups;
   tp.oob_row = (int32_t)rows;
-  const int64_t items = (int64_t)p.num_seqs * pl.head_groups * pl.num_chunks;
-  if (items > 0x7fffffffLL) {
-    *error = "tensor-core decode: too many work items";
-    return PAGEDKV_ERR_INVALID_ARGUMENT;
-  }
-  tp.total_items = (int32_t)items;
-  int n_launch = 1;
-  if (need > 0) {
-    const size_t slots = (size_t)p.num_seqs * p.hq * pl.num_chunks;
-    const size_t acc = ((slots * p.head_dim * sizeof(float) + 255) / 256) * 256;
-    const size_t ml = ((slots * sizeof(float2) + 255) / 256) * 256;
-    p.ws_acc = static_cast<float *>(workspace);
-    p.ws_ml = reinterpret_cast<float2 *>(static_cast<char *>(workspace) + acc);
-    tp.counters = reinterpret_cast<int32_t *>(static_cast<char *>(workspace) + acc + ml);
-    cudaError_t e = cudaMemsetAsync(tp.counters, 0, (size_t)p.num_seqs * pl.head_groups * sizeof(int32_t), stream);
-    if (e != cudaSuccess) {
-      *error = std::string("tensor-core decode: counter reset: ") + cudaGetErrorString(e);
-      return PAGEDKV_ERR_CUDA;
-    }
-    ++n_launch;
+  const size_t hqs = (size_t)pl.H * (p.hq / p.hkv);
+  const size_t slots = 2 * (size_t)pl.grid;
+  char *ws = static_cast<char *>(workspace);
+  tp.part_acc = reinterpret_cast<float *>(ws);
+  ws += align256(slots * hqs * p.head_dim * sizeof(float));
+  tp.part_ml = reinterpret_cast<float2 *>(ws);
+  ws += align256(slots * hqs * sizeof(float2));
+  tp.counters = reinterpret_cast<int32_t *>(ws);
+  cudaError_t e = cudaMemsetAsync(tp.counters, 0, (size_t)p.num_seqs * pl.head_groups * sizeof(int32_t), stream);
+  if (e != cudaSuccess) {
+    *error = std::string("tensor-core decode: counter reset: ") + cudaGetErrorString(e);
+    return PAGEDKV_ERR_CUDA;
   }
   tp.p = p;
-  const int grid = (int)(items < num_sms ? items : num_sms);
-  cudaError_t e = dtype == PAGEDKV_DTYPE_BF16 ? dispatch_tc<__nv_bfloat16>(pl, mk, mv, tp, grid, stream)
-                                              : dispatch_tc<__half>(pl, mk, mv, tp, grid, stream);
+  e = dtype == PAGEDKV_DTYPE_BF16 ? dispatch_tc<__nv_bfloat16>(pl, mk, mv, tp, stream)
+                                  : dispatch_tc<__half>(pl, mk, mv, tp, stream);
   if (e != cudaSuccess) {
     *error = std::string("tensor-core decode launch: ") + cudaGetErrorString(e);
     return PAGEDKV_ERR_CUDA;
   }
-  *launches = n_launch;
+  *launches = 2;  // counter reset + kernel
   return PAGEDKV_OK;
 }
 

@@ -127,17 +127,24 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // Shared-memory matrix descriptor (tcgen05 format): start address, leading and
-// stride byte offsets (16-byte units), version 1, layout type in bits 61-63
-// (2 = 128-byte swizzle).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_bytes,
-                                                    uint32_t sbo_bytes) {
+// stride byte offsets (16-byte units), version 1, layout type in bits 61-63.
+constexpr uint32_t kLayoutSwizzle128 = 2;
+constexpr uint32_t kLayoutSwizzle32 = 6;
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((addr & 0x3FFFFu) >> 4);
   d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
+  d |= (uint64_t)layout << 61;
   return d;
+}
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_bytes,
+                                                    uint32_t sbo_bytes) {
+  return smem_desc(addr, lbo_bytes, sbo_bytes, kLayoutSwizzle128);
 }
 
 // Instruction descriptor for kind::f16 with fp32 accumulation, M = 128.

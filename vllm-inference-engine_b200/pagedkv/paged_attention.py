@@ -38,6 +38,9 @@ _DTYPES = {torch.float16: _native.DTYPE_F16, torch.bfloat16: _native.DTYPE_BF16}
 
 # Split-K scratch, one cached buffer per device, grown on demand.
 _workspaces: dict[int, torch.Tensor] = {}
+# Workspace bytes per launch shape (the query is a host-side computation).
+_ws_sizes: dict[tuple, int] = {}
+_retired_workspaces: list[torch.Tensor] = []
 
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
@@ -46,6 +49,9 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
     idx = device.index if device.index is not None else torch.cuda.current_device()
     buf = _workspaces.get(idx)
     if buf is None or buf.numel() < nbytes:
+        if buf is not None:
+            # A CUDA graph captured earlier may still point at the old buffer.
+            _retired_workspaces.append(buf)
         size = max(nbytes, 1 << 20)
         buf = torch.empty(size, dtype=torch.uint8, device=device)
         _workspaces[idx] = buf
@@ -124,9 +130,13 @@ def _decode_into(
     guard = _device_guard(dev)
     ctx = guard if guard is not None else _NullCtx()
     with ctx:
-        nbytes = lib.pagedkv_decode_attention_workspace_size(
-            num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks, dtype
-        )
+        key = (dev.index, num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks, dtype)
+        nbytes = _ws_sizes.get(key)
+        if nbytes is None:
+            nbytes = lib.pagedkv_decode_attention_workspace_size(
+                num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks, dtype
+            )
+            _ws_sizes[key] = nbytes
         ws = _workspace(dev, nbytes)
         rc = lib.pagedkv_decode_attention(
             oo.data_ptr(), oo.stride(0), oo.stride(1),
