@@ -79,7 +79,11 @@ const char *pagedkv_last_error(void);
  *
  * workspace: device scratch of at least
  * pagedkv_decode_attention_workspace_size(...) bytes (may be NULL when that
- * size is 0); it is fully overwritten before it is read.
+ * size is 0). Its first 8 KiB hold cross-CTA completion flags: zero-fill the
+ * buffer once before its first use; every call leaves those bytes zero again
+ * (after a PAGEDKV_EFLAG_PIPE_TIMEOUT report, zero them again). The rest is
+ * overwritten before it is read. Calls that overlap on the GPU must not share
+ * a workspace.
  */
 int pagedkv_decode_attention(
     void *out, int64_t out_stride_seq, int64_t out_stride_head,

@@ -61,6 +61,7 @@ constexpr int kHalfBytes = kTile * 128;        // one 64-element half of a tile:
 constexpr int kOperandBytes = 2 * kHalfBytes;  // [128 x 128] K or V tile: 32 KB
 constexpr int kThreads = 224;                  // 7 warps
 constexpr uint64_t kTimeoutNs = 2000000000ull;
+constexpr float kRescaleLog2 = 8.f;            // lazy-rescale threshold (log2 units)
 
 // Optional wait-time trace (build with -DPAGEDKV_TRACE; off in the product
 // build): per CTA and warp role, nanoseconds spent in each pipeline wait.
@@ -70,16 +71,16 @@ constexpr int kTraceCtas = 160;
 __device__ unsigned long long g_trace[kTraceCtas][4][kTraceSlots];
 #define PKV_TW(slot, expr)             \
   ([&]() {                              \
-    const uint64_t _t0 = globaltimer_ns(); \
+    const uint64_t _t0 = clock64();     \
     const auto _r = (expr);             \
-    tw[slot] += globaltimer_ns() - _t0; \
+    tw[slot] += clock64() - _t0;        \
     return _r;                          \
   }())
 #define PKV_TV(slot, stmt)              \
   do {                                  \
-    const uint64_t _t0 = globaltimer_ns(); \
+    const uint64_t _t0 = clock64();     \
     stmt;                               \
-    tw[slot] += globaltimer_ns() - _t0; \
+    tw[slot] += clock64() - _t0;        \
   } while (0)
 #define PKV_TADD(slot, v) (tw[slot] += (v))
 #else
@@ -92,9 +93,9 @@ struct TcParams {
   DecodeParams p;
   int32_t head_groups;  // ceil(hkv / H)
   int32_t oob_row;      // num_blocks * block_size: first row past the pool
-  float *part_acc;      // [2 * grid][H * G][head_dim] partial sums of cut segments
-  float2 *part_ml;      // [2 * grid][H * G] (running max, denominator)
-  int32_t *counters;    // [num_seqs * head_groups] arrival counters (zeroed per launch)
+  float *part_acc;      // [grid][H * G][head_dim] published partial sums
+  float2 *part_ml;      // [grid][H * G] (reference max, denominator) of those
+  uint32_t *flags;      // [grid] 1 = CTA's partial published; reset to 0 when consumed
 };
 
 __device__ __forceinline__ int seq_len_clamped(const DecodeParams &p, int seq) {
@@ -231,6 +232,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 #ifdef PAGEDKV_TRACE
   uint64_t tw[kTraceSlots] = {0, 0, 0, 0, 0, 0, 0, 0};
   const uint64_t t_kernel0 = globaltimer_ns();
+  const uint64_t c_kernel0 = clock64();
 #endif
 
   if (threadIdx.x == 0) {
@@ -530,29 +532,25 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       }
     }
 
-    // Up to two pieces of this CTA are cut segments; their fence / arrival /
-    // combine is deferred to the end so it never stalls the tile pipeline.
-    int n_pend = 0;
-    int64_t pend_start[2] = {0, 0};
-    int pend_tiles[2] = {0, 0}, pend_seq[2] = {0, 0}, pend_hg[2] = {0, 0};
-
     Piece pc;
     while (walk.next(tp, pc)) {
-      float m_run[N], l_part[N], alpha_prev[N], acc[GP];
+      float m_ref[N], l_part[N], alpha_prev[N], acc[GP];
 #pragma unroll
       for (int n = 0; n < N; ++n) {
-        m_run[n] = kNegInf;
+        m_ref[n] = kNegInf;
         l_part[n] = 0.f;
         alpha_prev[n] = 1.f;
       }
 #pragma unroll
       for (int g = 0; g < GP; ++g) acc[g] = 0.f;
+      bool resc_prev = false;
 
-      // On a timed-out wait the pipeline is abandoned but the control flow of
-      // these 128 threads stays uniform (they share named barriers): later
-      // waits return at once and the results are garbage, flagged by the
-      // PIPE_TIMEOUT bit.
-      auto correction = [&](uint32_t g_tile) {
+      // Fold tile g_tile's O into the fp32 accumulators (rescaled first when
+      // that tile moved the reference max). On a timed-out wait the pipeline
+      // is abandoned but the control flow of these 128 threads stays uniform
+      // (they share named barriers): later waits return at once and the
+      // results are garbage, flagged by the PIPE_TIMEOUT bit.
+      auto correction = [&](uint32_t g_tile, bool resc) {
         const uint32_t b = g_tile & 1u;
         PKV_TW(3, mbar_wait(bar2(4, b), (g_tile >> 1) & 1u, abort_flag, kTimeoutNs));
         tc_fence_after();
@@ -561,10 +559,15 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(bar2(5, b));
+        if (resc) {
 #pragma unroll
-        for (int g = 0; g < GP; ++g) {
-          const float a = (H == 2 && hl == 1) ? alpha_prev[(GP + g) % N] : alpha_prev[g];
-          acc[g] = fmaf(acc[g], a, o[g]);
+          for (int g = 0; g < GP; ++g) {
+            const float a = (H == 2 && hl == 1) ? alpha_prev[(GP + g) % N] : alpha_prev[g];
+            acc[g] = fmaf(acc[g], a, o[g]);
+          }
+        } else {
+#pragma unroll
+          for (int g = 0; g < GP; ++g) acc[g] += o[g];
         }
       };
 
@@ -580,44 +583,57 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         tc_fence_before();
         mbar_arrive(bar2(1, b));
 
+        // Lazy rescaling: P is exponentiated against a per-column reference
+        // max m_ref and only re-based when some score of this tile exceeds it
+        // by more than 2^kRescaleLog2 (then P <= 2^8 stays exact in fp16/bf16
+        // and the fp32 sums cannot overflow). The decision is one vote over
+        // the 128 rows; the exact tile max is only reduced when it is taken.
         const bool valid = pc.t0 + j * kTile + row < pc.t1;
-        float *rm = red_max + red_buf * 4 * N;
-        float wm[N];
+        uint32_t need = 0;
 #pragma unroll
         for (int n = 0; n < N; ++n) {
           s[n] = valid ? s[n] * p.scale_log2 : kNegInf;
-          wm[n] = warp_max(s[n]);
+          need |= s[n] > m_ref[n] + kRescaleLog2 ? 1u : 0u;
         }
-        if (lane == 0) {
-#pragma unroll
-          for (int n = 0; n < N; n += 4)
-            *reinterpret_cast<float4 *>(rm + q4 * N + n) = make_float4(wm[n], wm[n + 1], wm[n + 2], wm[n + 3]);
-        }
-        named_bar(1, 128);
-#pragma unroll
-        for (int n = 0; n < N; n += 4) {
-          const float4 a0 = *reinterpret_cast<const float4 *>(rm + n);
-          const float4 a1 = *reinterpret_cast<const float4 *>(rm + N + n);
-          const float4 a2 = *reinterpret_cast<const float4 *>(rm + 2 * N + n);
-          const float4 a3 = *reinterpret_cast<const float4 *>(rm + 3 * N + n);
-          wm[n] = fmaxf(fmaxf(a0.x, a1.x), fmaxf(a2.x, a3.x));
-          wm[n + 1] = fmaxf(fmaxf(a0.y, a1.y), fmaxf(a2.y, a3.y));
-          wm[n + 2] = fmaxf(fmaxf(a0.z, a1.z), fmaxf(a2.z, a3.z));
-          wm[n + 3] = fmaxf(fmaxf(a0.w, a1.w), fmaxf(a2.w, a3.w));
-        }
+        const bool resc = named_bar_or(1, 128, need);
         float alpha[N];
+        if (resc) {
+          float *rm = red_max + red_buf * 4 * N;
+          float wm[N];
+#pragma unroll
+          for (int n = 0; n < N; ++n) wm[n] = warp_max(s[n]);
+          if (lane == 0) {
+#pragma unroll
+            for (int n = 0; n < N; n += 4)
+              *reinterpret_cast<float4 *>(rm + q4 * N + n) = make_float4(wm[n], wm[n + 1], wm[n + 2], wm[n + 3]);
+          }
+          named_bar(1, 128);
+#pragma unroll
+          for (int n = 0; n < N; n += 4) {
+            const float4 a0 = *reinterpret_cast<const float4 *>(rm + n);
+            const float4 a1 = *reinterpret_cast<const float4 *>(rm + N + n);
+            const float4 a2 = *reinterpret_cast<const float4 *>(rm + 2 * N + n);
+            const float4 a3 = *reinterpret_cast<const float4 *>(rm + 3 * N + n);
+            wm[n] = fmaxf(fmaxf(a0.x, a1.x), fmaxf(a2.x, a3.x));
+            wm[n + 1] = fmaxf(fmaxf(a0.y, a1.y), fmaxf(a2.y, a3.y));
+            wm[n + 2] = fmaxf(fmaxf(a0.z, a1.z), fmaxf(a2.z, a3.z));
+            wm[n + 3] = fmaxf(fmaxf(a0.w, a1.w), fmaxf(a2.w, a3.w));
+          }
+          red_buf ^= 1;
+#pragma unroll
+          for (int n = 0; n < N; ++n) {
+            const float mn = fmaxf(m_ref[n], wm[n]);
+            alpha[n] = mn == kNegInf ? 1.f : fast_exp2(m_ref[n] - mn);
+            l_part[n] *= alpha[n];
+            m_ref[n] = mn;
+          }
+        }
 #pragma unroll
         for (int n = 0; n < N; ++n) {
-          const float mn = fmaxf(m_run[n], wm[n]);
-          alpha[n] = mn == kNegInf ? 1.f : exp2f(m_run[n] - mn);
-          // The denominator sums P as rounded for the MMA, so the normalisation
-          // matches the numerator exactly.
-          const float pr = E::to_float(E::from_float(valid ? exp2f(s[n] - mn) : 0.f));
+          const float pr = valid ? fast_exp2(s[n] - m_ref[n]) : 0.f;
           s[n] = pr;
-          l_part[n] = fmaf(l_part[n], alpha[n], pr);
-          m_run[n] = mn;
+          l_part[n] += pr;
         }
-        red_buf ^= 1;
         PKV_TW(2, mbar_wait(bar2(3, b), bph ^ 1u, abort_flag, kTimeoutNs));
         // P^T as the B operand [128 tokens x N], MN-major with 32-byte swizzle:
         // token `row` owns 32 contiguous bytes (16 columns) in each 16-column
@@ -640,14 +656,17 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         }
         fence_proxy_async_smem();
         mbar_arrive(bar2(2, b));
-        if (j > 0) correction(gt - 1);
+        if (j > 0) correction(gt - 1, resc_prev);
+        if (resc) {
 #pragma unroll
-        for (int n = 0; n < N; ++n) alpha_prev[n] = alpha[n];
+          for (int n = 0; n < N; ++n) alpha_prev[n] = alpha[n];
+        }
+        resc_prev = resc;
         ++gt;
       }
-      if (pc.ntiles > 0) correction(gt - 1);
+      if (pc.ntiles > 0) correction(gt - 1, resc_prev);
 #ifdef PAGEDKV_TRACE
-      const uint64_t t_epi0 = globaltimer_ns();
+      const uint64_t t_epi0 = clock64();
       tw[6] += 1;
 #endif
 
@@ -668,15 +687,16 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         float l1 = 0.f;
         if (H == 2) l1 = red_l[n1] + red_l[N + n1] + red_l[2 * N + n1] + red_l[3 * N + n1];
         l_sel[g] = (H == 2 && hl == 1) ? l1 : l0;
-        m_sel[g] = (H == 2 && hl == 1) ? m_run[n1] : m_run[g];
+        m_sel[g] = (H == 2 && hl == 1) ? m_ref[n1] : m_ref[g];
       }
       named_bar(1, 128);  // red_l is rewritten by the next piece
 
       const int kv = pc.hg * H + hl;
       const bool have = kv < p.hkv;
+      T *out = reinterpret_cast<T *>(p.out) + (int64_t)pc.seq * p.o_ss + dim;
       if (pc.ntiles == pc.seg_tiles) {
+        // Whole segment in this CTA: normalise and store.
         if (have) {
-          T *out = reinterpret_cast<T *>(p.out) + (int64_t)pc.seq * p.o_ss + dim;
 #pragma unroll
           for (int g = 0; g < GP; ++g) {
             if (g < p.group) {
@@ -685,104 +705,94 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
             }
           }
         }
-      } else {
-        const int64_t slot = 2 * (int64_t)blockIdx.x + (pc.first ? 0 : 1);
+      } else if (pc.t0 > 0) {
+        // Continuation of a segment that began in an earlier CTA: this is this
+        // CTA's first piece. Publish it (partial + release flag) for the CTA
+        // owning the segment's first tile, which combines at its end.
         if (have) {
 #pragma unroll
           for (int g = 0; g < GP; ++g) {
             if (g < p.group) {
-              const int64_t hh = slot * HQS + hl * p.group + g;
+              const int64_t hh = (int64_t)blockIdx.x * HQS + hl * p.group + g;
               tp.part_acc[hh * D + dim] = acc[g];
               if (dim == 0) tp.part_ml[hh] = make_float2(m_sel[g], l_sel[g]);
             }
           }
         }
-        if (n_pend < 2) {
-          pend_start[n_pend] = pc.seg_start;
-          pend_tiles[n_pend] = pc.seg_tiles;
-          pend_seq[n_pend] = pc.seq;
-          pend_hg[n_pend] = pc.hg;
+        named_bar(1, 128);
+        if (row == 0) {
+          __threadfence();  // release every thread's partial (cumulative over the barrier)
+          st_volatile_u32(tp.flags + blockIdx.x, 1u);
         }
-        ++n_pend;
-      }
+      } else {
+        // First tile of the segment is here and the segment runs past this
+        // CTA's range: this is this CTA's last piece, and this CTA combines.
+        // The other pieces are the first pieces of CTAs b+1..b1, published
+        // early in their runs.
 #ifdef PAGEDKV_TRACE
-      tw[4] += globaltimer_ns() - t_epi0;
+        const uint64_t t_fin0 = clock64();
 #endif
-    }
-
-    // ---- cut segments: publish this CTA's partials, the last arrival combines
-    if (n_pend > 0) {
-#ifdef PAGEDKV_TRACE
-      const uint64_t t_fin0 = globaltimer_ns();
-#endif
-      named_bar(1, 128);  // every partial store of this CTA issued
-      if (row == 0) {
-        __threadfence();  // release them (cumulative over the barrier) before arriving
-        bool any = false;
-        for (int k = 0; k < n_pend && k < 2; ++k) {
-          const int64_t seg = (int64_t)pend_seq[k] * tp.head_groups + pend_hg[k];
-          const int pieces = (int)(owner_of(pend_start[k] + pend_tiles[k] - 1, T_total, G) -
-                                   owner_of(pend_start[k], T_total, G) + 1);
-          const int prev = atomicAdd(tp.counters + seg, 1);
-          misc->combine[k] = prev == pieces - 1 ? 1 : 0;
-          any |= misc->combine[k] != 0;
+        const int64_t b1 = owner_of(pc.seg_start + pc.seg_tiles - 1, T_total, G);
+        if (row == 0) {
+          for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) {
+            const uint64_t t0 = globaltimer_ns();
+            while (ld_acquire_u32(tp.flags + bb) == 0u) {
+              if (globaltimer_ns() - t0 > kTimeoutNs) {
+                *abort_flag = 1;
+                break;
+              }
+            }
+          }
         }
-        if (any) __threadfence();  // acquire the other CTAs' partials
-      }
-      named_bar(1, 128);
+        named_bar(1, 128);
 #ifdef PAGEDKV_TRACE
-      tw[1] += globaltimer_ns() - t_fin0;
+        tw[1] += clock64() - t_fin0;
 #endif
-      for (int k = 0; k < n_pend && k < 2; ++k) {
-        if (!misc->combine[k]) continue;
-        const int kv = pend_hg[k] * H + hl;
-        if (kv >= p.hkv) continue;
-        const int64_t b0 = owner_of(pend_start[k], T_total, G);
-        const int64_t b1 = owner_of(pend_start[k] + pend_tiles[k] - 1, T_total, G);
-        // CTA b0 reached this segment after another piece unless its range starts here.
-        const bool b0_second = range_lo(b0, T_total, G) < pend_start[k];
-        // Piece-outer: every head's (m, l) and partial sum of one piece are
-        // loaded together, so each piece costs one round trip to L2.
-        float mm[GP], ll[GP], a[GP], res[GP];
+        float mm[GP], ll[GP], a[GP];
 #pragma unroll
         for (int g = 0; g < GP; ++g) {
-          mm[g] = kNegInf;
-          ll[g] = 0.f;
-          a[g] = 0.f;
+          mm[g] = m_sel[g];
+          ll[g] = l_sel[g];
+          a[g] = acc[g];
         }
-        for (int64_t bb = b0; bb <= b1; ++bb) {
-          const int64_t slot = 2 * bb + ((bb == b0 && b0_second) ? 1 : 0);
-          const int64_t hh0 = slot * HQS + hl * p.group;
-          float2 ml[GP];
-          float av[GP];
+        if (have) {
+          for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) {
+            const int64_t hh0 = bb * HQS + hl * p.group;
+            float2 ml[GP];
+            float av[GP];
 #pragma unroll
-          for (int g = 0; g < GP; ++g) {
-            ml[g] = make_float2(kNegInf, 0.f);
-            av[g] = 0.f;
-            if (g < p.group) {
-              ml[g] = __ldcg(&tp.part_ml[hh0 + g]);
-              av[g] = __ldcg(&tp.part_acc[(hh0 + g) * D + dim]);
+            for (int g = 0; g < GP; ++g) {
+              ml[g] = make_float2(kNegInf, 0.f);
+              av[g] = 0.f;
+              if (g < p.group) {
+                ml[g] = __ldcg(&tp.part_ml[hh0 + g]);
+                av[g] = __ldcg(&tp.part_acc[(hh0 + g) * D + dim]);
+              }
+            }
+#pragma unroll
+            for (int g = 0; g < GP; ++g) {
+              const float mb = fmaxf(mm[g], ml[g].x);
+              const float sc = mm[g] == kNegInf ? 0.f : fast_exp2(mm[g] - mb);
+              const float f = ml[g].x == kNegInf ? 0.f : fast_exp2(ml[g].x - mb);
+              ll[g] = fmaf(f, ml[g].y, ll[g] * sc);
+              a[g] = fmaf(f, av[g], a[g] * sc);
+              mm[g] = mb;
             }
           }
 #pragma unroll
-          for (int g = 0; g < GP; ++g) {
-            const float mb = fmaxf(mm[g], ml[g].x);
-            const float sc = mm[g] == kNegInf ? 0.f : exp2f(mm[g] - mb);
-            const float f = ml[g].x == kNegInf ? 0.f : exp2f(ml[g].x - mb);
-            ll[g] = fmaf(f, ml[g].y, ll[g] * sc);
-            a[g] = fmaf(f, av[g], a[g] * sc);
-            mm[g] = mb;
-          }
+          for (int g = 0; g < GP; ++g)
+            if (g < p.group) out[(int64_t)(kv * p.group + g) * p.o_sh] = E::from_float(ll[g] > 0.f ? a[g] / ll[g] : 0.f);
         }
-#pragma unroll
-        for (int g = 0; g < GP; ++g) res[g] = ll[g] > 0.f ? a[g] / ll[g] : 0.f;
-        T *out = reinterpret_cast<T *>(p.out) + (int64_t)pend_seq[k] * p.o_ss + dim;
-#pragma unroll
-        for (int g = 0; g < GP; ++g)
-          if (g < p.group) out[(int64_t)(kv * p.group + g) * p.o_sh] = E::from_float(res[g]);
+        named_bar(1, 128);  // every partner partial read before its flag is cleared
+        if (row == 0) {
+          for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) st_volatile_u32(tp.flags + bb, 0u);
+        }
+#ifdef PAGEDKV_TRACE
+        tw[7] += clock64() - t_fin0;
+#endif
       }
 #ifdef PAGEDKV_TRACE
-      tw[7] += globaltimer_ns() - t_fin0;
+      tw[4] += clock64() - t_epi0;
 #endif
     }
   }
@@ -791,11 +801,15 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 #ifdef PAGEDKV_TRACE
   if (blockIdx.x < kTraceCtas && lane == 0 && warp <= 2) {
     for (int i = 0; i < kTraceSlots; ++i) g_trace[blockIdx.x][warp][i] = tw[i];
-    if (warp == 0) {
-      g_trace[blockIdx.x][3][0] = globaltimer_ns() - t_kernel0;
-      g_trace[blockIdx.x][3][1] = t_kernel0;
-      g_trace[blockIdx.x][3][2] = (unsigned long long)(misc->hi - misc->lo);
-    }
+    g_trace[blockIdx.x][3][5 + warp] = clock64() - c_kernel0;  // this role's own finish
+  }
+  __syncthreads();
+  if (blockIdx.x < kTraceCtas && threadIdx.x == 0) {
+    g_trace[blockIdx.x][3][0] = globaltimer_ns() - t_kernel0;
+    g_trace[blockIdx.x][3][1] = t_kernel0;
+    g_trace[blockIdx.x][3][2] = (unsigned long long)(misc->hi - misc->lo);
+    g_trace[blockIdx.x][3][3] = clock64() - c_kernel0;
+    g_trace[blockIdx.x][3][4] = globaltimer_ns();
   }
 #endif
   if (threadIdx.x == 0 && *abort_flag) set_error(p.err, PAGEDKV_EFLAG_PIPE_TIMEOUT);
@@ -838,10 +852,11 @@ TcPlan make_plan(int32_t num_seqs, int32_t hq, int32_t hkv, int32_t head_dim, in
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 size_t plan_workspace(const TcPlan &pl, int32_t num_seqs, int32_t hq, int32_t hkv, int32_t head_dim) {
+  (void)num_seqs;
   const size_t hqs = (size_t)pl.H * (hq / hkv);
-  const size_t slots = 2 * (size_t)pl.grid;
-  return align256(slots * hqs * head_dim * sizeof(float)) + align256(slots * hqs * sizeof(float2)) +
-         align256((size_t)num_seqs * pl.head_groups * sizeof(int32_t));
+  const size_t slots = (size_t)pl.grid;
+  return kWorkspaceHeaderBytes + align256(slots * hqs * sizeof(float2)) +
+         align256(slots * hqs * head_dim * sizeof(float));
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -988,30 +1003,29 @@ int tc_launch(DecodeParams &p, int dtype, void *workspace, size_t workspace_byte
     *error = "tensor-core decode: cuTensorMapEncodeTiled failed";
     return PAGEDKV_ERR_CUDA;
   }
+  if (pl.grid * sizeof(uint32_t) > kWorkspaceHeaderBytes) {
+    *error = "tensor-core decode: grid larger than the workspace flag header";
+    return PAGEDKV_ERR_UNSUPPORTED;
+  }
   TcParams tp{};
   tp.head_groups = pl.head_groups;
   tp.oob_row = (int32_t)rows;
   const size_t hqs = (size_t)pl.H * (p.hq / p.hkv);
-  const size_t slots = 2 * (size_t)pl.grid;
+  const size_t slots = (size_t)pl.grid;
   char *ws = static_cast<char *>(workspace);
-  tp.part_acc = reinterpret_cast<float *>(ws);
-  ws += align256(slots * hqs * p.head_dim * sizeof(float));
+  tp.flags = reinterpret_cast<uint32_t *>(ws);  // zero between launches
+  ws += kWorkspaceHeaderBytes;
   tp.part_ml = reinterpret_cast<float2 *>(ws);
   ws += align256(slots * hqs * sizeof(float2));
-  tp.counters = reinterpret_cast<int32_t *>(ws);
-  cudaError_t e = cudaMemsetAsync(tp.counters, 0, (size_t)p.num_seqs * pl.head_groups * sizeof(int32_t), stream);
-  if (e != cudaSuccess) {
-    *error = std::string("tensor-core decode: counter reset: ") + cudaGetErrorString(e);
-    return PAGEDKV_ERR_CUDA;
-  }
+  tp.part_acc = reinterpret_cast<float *>(ws);
   tp.p = p;
-  e = dtype == PAGEDKV_DTYPE_BF16 ? dispatch_tc<__nv_bfloat16>(pl, mk, mv, tp, stream)
+  cudaError_t e = dtype == PAGEDKV_DTYPE_BF16 ? dispatch_tc<__nv_bfloat16>(pl, mk, mv, tp, stream)
                                   : dispatch_tc<__half>(pl, mk, mv, tp, stream);
   if (e != cudaSuccess) {
     *error = std::string("tensor-core decode launch: ") + cudaGetErrorString(e);
     return PAGEDKV_ERR_CUDA;
   }
-  *launches = 2;  // counter reset + kernel
+  *launches = 1;
   return PAGEDKV_OK;
 }
 

@@ -6,6 +6,11 @@
 
 namespace pagedkv {
 
+// Every decode workspace starts with this many bytes of cross-CTA completion
+// flags. They must be zero before the first launch that uses the workspace;
+// each launch leaves them zero again. Split-K partials start after it.
+constexpr size_t kWorkspaceHeaderBytes = 8192;
+
 // Everything one decode-attention launch needs, resolved by the ABI layer.
 struct DecodeParams {
   void *out;

@@ -77,7 +77,7 @@ size_t simt_workspace_bytes(int32_t num_seqs, int32_t hq, int32_t head_dim, cons
   const size_t slots = (size_t)num_seqs * hq * plan.num_splits;
   const size_t acc = slots * head_dim * sizeof(float);
   const size_t ml = slots * sizeof(float2);
-  return ((acc + 255) / 256) * 256 + ml;
+  return kWorkspaceHeaderBytes + ((acc + 255) / 256) * 256 + ml;
 }
 
 }  // namespace
@@ -204,8 +204,9 @@ int pagedkv_decode_attention(void *out, int64_t out_stride_seq, int64_t out_stri
   if (need > 0) {
     const size_t slots = (size_t)num_seqs * num_q_heads * plan.num_splits;
     const size_t acc = ((slots * head_dim * sizeof(float) + 255) / 256) * 256;
-    p.ws_acc = static_cast<float *>(workspace);
-    p.ws_ml = reinterpret_cast<float2 *>(static_cast<char *>(workspace) + acc);
+    char *base = static_cast<char *>(workspace) + kWorkspaceHeaderBytes;
+    p.ws_acc = reinterpret_cast<float *>(base);
+    p.ws_ml = reinterpret_cast<float2 *>(base + acc);
   }
   cudaError_t e = launch_decode_simt(p, dtype, st);
   if (e != cudaSuccess) return cuda_fail(e, "decode_simt launch");

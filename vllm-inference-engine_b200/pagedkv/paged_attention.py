@@ -53,7 +53,9 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
             # A CUDA graph captured earlier may still point at the old buffer.
             _retired_workspaces.append(buf)
         size = max(nbytes, 1 << 20)
-        buf = torch.empty(size, dtype=torch.uint8, device=device)
+        # zero-filled once: the first 8 KiB are completion flags the kernels
+        # expect at zero and leave at zero
+        buf = torch.zeros(size, dtype=torch.uint8, device=device)
         _workspaces[idx] = buf
     return buf
 
