@@ -1,0 +1,297 @@
+"""Host-side drop-in for the reference engine's decode path.
+
+The reference imports its kernels by name (engine/kernels/
+paged_attention_integration.py:19-23) and runs one Python loop per sequence
+per layer for the KV append, with a device->host ``.item()`` sync in each
+iteration (:150-160). This module provides:
+
+* :func:`install` — put the B200 kernels in place of the reference's symbols
+  in ``engine.kernels.paged_attention`` and
+  ``engine.kernels.paged_attention_integration`` (and their batched decode
+  forward / context), so ``KernelPagedManualDecode``, the continuous-batching
+  scheduler, ``AsyncEngine`` and the HTTP server run unchanged on top;
+* :class:`PagedAttentionContext` — same constructor as the reference's
+  (:29-62); additionally builds the int64 ``slot_mapping`` of the token each
+  sequence writes this step, with ONE host->device copy for tables, lengths
+  and slots together;
+* :func:`paged_decode_attention_forward` — the reference's decode forward
+  (:65-176) with the append done by :func:`pagedkv.kv_append` (one launch per
+  layer, no host sync) and attention by the sm_100a kernel;
+* :func:`prepare_copy_on_write` — the block bookkeeping of a copy-on-write
+  append (fresh block for every sequence whose write block is shared), whose
+  data copy :func:`pagedkv.copy_blocks` performs for all layers at once.
+"""
+from __future__ import annotations
+
+import math
+from contextlib import contextmanager
+from typing import Any, Callable, Iterable, List, Optional, Sequence, Tuple, Union
+
+import torch
+
+from .paged_attention import (
+    copy_blocks,
+    kv_append,
+    pad_block_tables,
+    paged_attention_decode,
+    paged_attention_decode_batched,
+    paged_attention_decode_v1,
+    paged_attention_decode_v2,
+)
+
+
+def _block_ids(bt: Any) -> List[int]:
+    return list(bt.physical_block_ids) if hasattr(bt, "physical_block_ids") else list(bt)
+
+
+def build_decode_metadata(
+    block_tables: Sequence[Any],
+    seq_lens: Sequence[int],
+    block_size: int,
+    device: Union[torch.device, str],
+) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Padded int32 tables [N, max(1, W)], int32 seq_lens [N] and int64
+    slot_mapping [N] on ``device`` from one pinned host buffer.
+
+    The slot of sequence b is the position its decode step writes,
+    ``table[(len - 1) // BS] * BS + (len - 1) % BS`` (reference
+    integration.py:151-155); a sequence of length 0 gets slot -1 (skipped).
+    """
+    n = len(block_tables)
+    rows = [_block_ids(bt) for bt in block_tables]
+    width = max(1, max((len(r) for r in rows), default=0))
+    # int64 host image: [tables (n*width) | lens (n) | slots (n)]
+    host = torch.zeros(n * width + 2 * n, dtype=torch.int64)
+    tab = host[: n * width].view(n, width)
+    for i, r in enumerate(rows):
+        if r:
+            tab[i, : len(r)] = torch.tensor(r, dtype=torch.int64)
+    lens = torch.tensor([int(x) for x in seq_lens], dtype=torch.int64)
+    host[n * width : n * width + n] = lens
+    pos = lens - 1
+    slots = torch.full((n,), -1, dtype=torch.int64)
+    has = pos >= 0
+    if bool(has.any()):
+        idx = torch.nonzero(has).view(-1)
+        blk = tab[idx, pos[idx] // block_size]
+        slots[idx] = blk * block_size + pos[idx] % block_size
+    host[n * width + n :] = slots
+    dev = torch.device(device)
+    if dev.type == "cuda":
+        d = host.pin_memory().to(dev, non_blocking=True)
+    else:
+        d = host.to(dev)
+    tables_d = d[: n * width].view(n, width).to(torch.int32)
+    lens_d = d[n * width : n * width + n].to(torch.int32)
+    slots_d = d[n * width + n :]
+    return tables_d, lens_d, slots_d
+
+
+class PagedAttentionContext:
+    """Per-step context passed to the patched attention modules.
+
+    Constructor and attributes as the reference's (integration.py:29-62):
+    ``pool``, ``block_size``, ``is_decode``, ``is_batched``; batched:
+    ``block_table_list``, ``padded_block_tables``, ``seq_lens_tensor``;
+    single: ``single_block_table``, ``single_seq_len``, ``block_table_tensor``.
+    Added: ``slot_mapping`` (int64 [N]) for the one-launch append.
+    """
+
+    def __init__(
+        self,
+        pool: Any,
+        block_tables: Any,
+        seq_lens: Union[int, List[int], torch.Tensor],
+        block_size: int = 16,
+        is_decode: bool = True,
+    ):
+        self.pool = pool
+        self.block_size = block_size
+        self.is_decode = is_decode
+        device = pool.device
+        if hasattr(block_tables, "physical_block_ids") and not isinstance(block_tables, (list, tuple)):
+            self.is_batched = False
+            self.single_block_table = block_tables
+            self.single_seq_len = int(seq_lens)
+            tables, lens, slots = build_decode_metadata([block_tables], [self.single_seq_len], block_size, device)
+            self.block_table_tensor = tables[0, : max(1, len(block_tables.physical_block_ids))]
+            self.padded_block_tables = tables
+            self.seq_lens_tensor = lens
+            self.slot_mapping = slots
+        else:
+            self.is_batched = True
+            self.block_table_list = block_tables
+            if isinstance(seq_lens, torch.Tensor):
+                seq_lens = [int(x) for x in seq_lens.tolist()]
+            tables, lens, slots = build_decode_metadata(block_tables, list(seq_lens), block_size, device)
+            self.padded_block_tables = tables
+            self.seq_lens_tensor = lens
+            self.slot_mapping = slots
+
+
+def paged_decode_attention_forward(
+    self: torch.nn.Module,
+    hidden_states: torch.Tensor,
+    position_embeddings: Tuple[torch.Tensor, torch.Tensor],
+    attention_mask: Optional[torch.Tensor] = None,
+    past_key_values: Any = None,
+    **kwargs: Any,
+) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Decode-step replacement for ``Qwen2Attention.forward`` (reference
+    integration.py:65-176): projections, RoPE, KV append through the slot
+    mapping (one launch per layer), batched paged attention, o_proj."""
+    ctx = getattr(self, "_paged_attention_context", None)
+    if ctx is None or not ctx.is_decode:
+        orig_forward = getattr(self, "_orig_attention_forward", None)
+        if orig_forward is not None:
+            return orig_forward(
+                hidden_states=hidden_states,
+                position_embeddings=position_embeddings,
+                attention_mask=attention_mask,
+                past_key_values=past_key_values,
+                **kwargs,
+            )
+        raise RuntimeError("No fallback forward method found on attention module.")
+
+    from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
+
+    layer_idx = self.layer_idx
+    input_shape = hidden_states.shape[:-1]
+    hidden_shape = (*input_shape, -1, self.head_dim)
+    query_states = self.q_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+    key_states = self.k_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+    value_states = self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+    cos, sin = position_embeddings
+    query_states, key_states = apply_rotary_pos_emb(query_states, key_states, cos, sin)
+    scale = self.scaling if hasattr(self, "scaling") else 1.0 / math.sqrt(self.head_dim)
+
+    pool = ctx.pool
+    k_cache = pool.k_cache[layer_idx]
+    v_cache = pool.v_cache[layer_idx]
+    # [B, Hkv, 1, D] -> [B, Hkv, D] (views; the append takes strides)
+    kv_append(key_states.squeeze(2), value_states.squeeze(2), k_cache, v_cache, ctx.slot_mapping)
+    attn_output = paged_attention_decode_batched(
+        q=query_states.squeeze(2),
+        k_cache=k_cache,
+        v_cache=v_cache,
+        block_tables=ctx.padded_block_tables,
+        seq_lens=ctx.seq_lens_tensor,
+        scale=scale,
+    )
+    attn_output = attn_output.reshape(*input_shape, -1).contiguous()
+    attn_output = self.o_proj(attn_output)
+    return attn_output, None
+
+
+@contextmanager
+def patch_paged_attention(model: torch.nn.Module, context: PagedAttentionContext):
+    """Temporarily route every decoder attention module of ``model`` through
+    :func:`paged_decode_attention_forward` (reference integration.py:179-208)."""
+    patched: List[Tuple[torch.nn.Module, Callable]] = []
+    for module in model.modules():
+        if all(hasattr(module, a) for a in ("q_proj", "k_proj", "v_proj", "o_proj")):
+            orig = module.forward
+            module._orig_attention_forward = orig
+            module._paged_attention_context = context
+            module.forward = paged_decode_attention_forward.__get__(module, module.__class__)
+            patched.append((module, orig))
+    try:
+        yield context
+    finally:
+        for module, orig in patched:
+            module.forward = orig
+            for attr in ("_orig_attention_forward", "_paged_attention_context"):
+                if hasattr(module, attr):
+                    delattr(module, attr)
+
+
+def prepare_copy_on_write(
+    block_tables: Iterable[Any],
+    allocator: Any,
+    block_size: int,
+) -> List[Tuple[int, int]]:
+    """Give every sequence whose next write lands in a shared block a private
+    copy of that block; return the (src, dst) pairs for :func:`copy_blocks`.
+
+    For each table (an object with ``physical_block_ids`` and ``num_tokens``,
+    as the reference's ``BlockTable``), the write block is
+    ``num_tokens // block_size`` (reference integration.py:580). If the
+    allocator's ``ref_counts`` for it is above 1, a fresh block is allocated,
+    the table is pointed at it and one reference on the shared block is
+    dropped (``release`` when the allocator has it, else ``free``, as the
+    reference allocator's API at block_allocator.py:216-270). The data copy
+    itself must then run before the step's append.
+    """
+    pairs: List[Tuple[int, int]] = []
+    release = getattr(allocator, "release", None) or allocator.free
+    for bt in block_tables:
+        idx = bt.num_tokens // block_size
+        if idx >= len(bt.physical_block_ids):
+            continue
+        src = bt.physical_block_ids[idx]
+        if allocator.ref_counts.get(src, 0) > 1:
+            dst = allocator.allocate()
+            bt.physical_block_ids[idx] = dst
+            release(src)
+            pairs.append((src, dst))
+    return pairs
+
+
+def copy_on_write(pool: Any, pairs: Sequence[Tuple[int, int]]) -> None:
+    """Run the data copies of :func:`prepare_copy_on_write` for every layer of
+    ``pool`` (an object with ``k_cache`` / ``v_cache`` lists) in one launch."""
+    if not pairs:
+        return
+    dev = pool.k_cache[0].device
+    mapping = torch.tensor(list(pairs), dtype=torch.int64).to(dev)
+    copy_blocks(pool.k_cache, pool.v_cache, mapping)
+
+
+_INSTALL_NAMES_KERNELS = (
+    "paged_attention_decode_batched",
+    "paged_attention_decode_v1",
+    "paged_attention_decode_v2",
+    "paged_attention_decode",
+    "pad_block_tables",
+)
+
+
+def install(paged_attention_module: Any = None, integration_module: Any = None) -> dict:
+    """Install the B200 path into the reference's modules.
+
+    ``paged_attention_module`` defaults to ``engine.kernels.paged_attention``
+    and ``integration_module`` to ``engine.kernels.paged_attention_integration``
+    (imported if not given). Returns the replaced symbols for :func:`uninstall`.
+    The reference's ``naive_reference_paged_attention`` is left untouched.
+    """
+    if paged_attention_module is None:
+        import importlib
+
+        paged_attention_module = importlib.import_module("engine.kernels.paged_attention")
+    if integration_module is None:
+        import importlib
+
+        integration_module = importlib.import_module("engine.kernels.paged_attention_integration")
+    ours = {
+        "paged_attention_decode_batched": paged_attention_decode_batched,
+        "paged_attention_decode_v1": paged_attention_decode_v1,
+        "paged_attention_decode_v2": paged_attention_decode_v2,
+        "paged_attention_decode": paged_attention_decode,
+        "pad_block_tables": pad_block_tables,
+        "PagedAttentionContext": PagedAttentionContext,
+        "paged_decode_attention_forward": paged_decode_attention_forward,
+        "patch_paged_attention": patch_paged_attention,
+    }
+    saved: dict = {}
+    for mod in (paged_attention_module, integration_module):
+        for name, fn in ours.items():
+            if hasattr(mod, name):
+                saved[(mod, name)] = getattr(mod, name)
+                setattr(mod, name, fn)
+    return saved
+
+
+def uninstall(saved: dict) -> None:
+    """Undo :func:`install`."""
+    for (mod, name), fn in saved.items():
+        setattr(mod, name, fn)
