@@ -151,6 +151,30 @@ int pagedkv_copy_blocks(
 int pagedkv_read_error_flags(uint32_t *flags_out, int32_t clear, void *stream);
 
 /*
+ * Decode attention that allocates nothing: the same computation, arguments and
+ * result as pagedkv_decode_attention, minus the workspace. No counterpart in
+ * the reference (its Triton path needs no scratch).
+ *
+ * For callers that cannot allocate device memory on the decode path (a fixed
+ * memory budget reserved up front, an allocator owned by another component, a
+ * binding with no allocator at all). The scratch comes from a 4 MiB array
+ * compiled into the library, held by every GPU that loads it until exit;
+ * shapes needing more return PAGEDKV_ERR_WORKSPACE. All calls on a device
+ * share the array: calls that overlap on the GPU race and must be serialised.
+ * The first call on a device resolves the array's address; make it before any
+ * stream capture. Each call clears the array's flag header on `stream` first.
+ */
+int pagedkv_decode_attention_noalloc(
+    void *out, int64_t out_stride_seq, int64_t out_stride_head,
+    const void *q, int64_t q_stride_seq, int64_t q_stride_head,
+    const void *k_cache, const void *v_cache,
+    const int32_t *block_tables, int64_t block_tables_stride,
+    const int32_t *seq_lens, int32_t uniform_seq_len,
+    int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
+    int32_t head_dim, int64_t num_blocks, int32_t block_size,
+    int32_t max_blocks_per_seq, float scale, int32_t dtype, void *stream);
+
+/*
  * Number of kernel launches the last pagedkv_decode_attention call on this
  * thread issued (1 or 2: the split-K combine is a second launch), and the
  * name of the decode kernel family it chose ("tc" = tcgen05/TMA, "simt").

@@ -42,6 +42,9 @@ struct SplitPlan {
 SplitPlan plan_simt_splits(int32_t num_seqs, int32_t num_kv_heads, int32_t group,
                            int32_t max_tokens, int32_t num_sms);
 
+// Set the calling thread's pagedkv_last_error() message.
+void set_last_error_message(const char *msg);
+
 cudaError_t launch_decode_simt(const DecodeParams &p, int dtype, cudaStream_t stream);
 cudaError_t launch_decode_combine(const DecodeParams &p, int dtype, cudaStream_t stream);
 

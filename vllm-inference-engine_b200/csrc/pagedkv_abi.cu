@@ -81,6 +81,9 @@ size_t simt_workspace_bytes(int32_t num_seqs, int32_t hq, int32_t head_dim, cons
 }
 
 }  // namespace
+
+void set_last_error_message(const char *msg) { t_last_error = msg; }
+
 }  // namespace pagedkv
 
 using namespace pagedkv;

@@ -81,6 +81,21 @@ _SIGNATURES = [
         ctypes.c_int,
         [_c_vp, _c_vp, _c_i32, _c_vp, _c_i32, _c_i64, _c_i64, _c_vp],
     ),
+    (
+        "pagedkv_decode_attention_noalloc",
+        ctypes.c_int,
+        [
+            _c_vp, _c_i64, _c_i64,
+            _c_vp, _c_i64, _c_i64,
+            _c_vp, _c_vp,
+            _c_vp, _c_i64,
+            _c_vp, _c_i32,
+            _c_i32, _c_i32, _c_i32, _c_i32,
+            _c_i64, _c_i32, _c_i32,
+            _c_f32, _c_i32,
+            _c_vp,
+        ],
+    ),
     ("pagedkv_read_error_flags", ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), _c_i32, _c_vp]),
     ("pagedkv_last_decode_launches", _c_i32, []),
     ("pagedkv_last_decode_kernel", ctypes.c_char_p, []),
