@@ -383,11 +383,11 @@ def run_ours(args) -> None:
     clocks = sampler.stop() if sampler else None
     attn_ms = timed(g_attn.replay, args.steps) / args.steps
     eager_ms = timed(step, max(10, args.steps // 10)) / max(10, args.steps // 10)
+    append_ms = _max_over_ranks(dist, max(0.0, total_ms / args.steps - attn_ms), dev)
     total_ms = _max_over_ranks(dist, total_ms, dev)
     attn_ms_max = _max_over_ranks(dist, attn_ms, dev)
     eager_ms = _max_over_ranks(dist, eager_ms, dev)
     ms_per_step = total_ms / args.steps
-    append_ms = max(0.0, ms_per_step - attn_ms_max)
 
     max_blocks = CTX // BLOCK_SIZE
     a_bytes = attention_bytes(NUM_SEQS, CTX, max_blocks)

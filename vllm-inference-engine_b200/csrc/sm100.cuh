@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a primitives the tensor-core decode
-// kernel uses: mbarriers, TMA tile loads (no multicast), tcgen05 MMA / TMEM.
+// kernel uses: mbarriers, single-CTA TMA tile loads, tcgen05 MMA / TMEM.
 #pragma once
 
 #include <cuda.h>
@@ -80,7 +80,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
 }
 
 // 2-D tiled bulk tensor load global -> shared, completing on an mbarrier.
-// No multicast: the copy lands in this CTA's shared memory only.
+// The copy lands in this CTA's own shared memory only.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, int32_t x, int32_t y,
                                             uint32_t bar, uint64_t policy) {
   asm volatile(
