@@ -1,8 +1,7 @@
 // Paged GQA decode attention on CUDA cores (sm_100a), split-K over the context.
 //
-// Used for GQA groups below 4 (one or two query heads per K/V row: the dot
-// products are too thin for tensor cores to pay) and for head_dim / group
-// shapes the tcgen05 kernel does not cover.
+// Serves the shapes the tcgen05 kernel is not built for: head_dim 32 or 256,
+// block_size below 8 or not a power of two, GQA groups above 16.
 //
 // Algorithm (restates engine/kernels/paged_attention.py:508-631, the batched
 // online-softmax kernel, with its grid changed from one program per QUERY head

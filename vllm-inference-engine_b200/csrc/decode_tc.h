@@ -11,8 +11,8 @@
 
 namespace pagedkv {
 
-// True when the tensor-core kernel covers this shape (GQA group >= 4 and a
-// head_dim / block_size it was built for).
+// True when the tensor-core kernel covers this shape (GQA group 1..16,
+// head_dim 64 or 128, power-of-two block_size 8..128).
 bool tc_eligible(int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size);
 
 // Scratch the tensor-core path needs (split-K partials), in bytes.
