@@ -264,6 +264,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     tmem_relinquish();
   }
 
+  // Everything above touched only shared memory and TMEM, so it overlaps the
+  // tail of the preceding kernel; global inputs are read only after it ends.
+  grid_dependency_wait();
+  grid_launch_dependents();
+
   // ---- prologue: total tile count and the start of this CTA's range ----------
   {
     long long *scan = reinterpret_cast<long long *>(smem + L::kOffRedMax);  // [6] warp sums
@@ -801,7 +806,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 #ifdef PAGEDKV_TRACE
   if (blockIdx.x < kTraceCtas && lane == 0 && warp <= 2) {
     for (int i = 0; i < kTraceSlots; ++i) g_trace[blockIdx.x][warp][i] = tw[i];
-    g_trace[blockIdx.x][3][5 + warp] = clock64() - c_kernel0;  // this role's own finish
+    if (warp >= 1) g_trace[blockIdx.x][3][5 + warp] = clock64() - c_kernel0;  // this role's own finish
   }
   __syncthreads();
   if (blockIdx.x < kTraceCtas && threadIdx.x == 0) {
@@ -810,6 +815,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     g_trace[blockIdx.x][3][2] = (unsigned long long)(misc->hi - misc->lo);
     g_trace[blockIdx.x][3][3] = clock64() - c_kernel0;
     g_trace[blockIdx.x][3][4] = globaltimer_ns();
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    g_trace[blockIdx.x][3][5] = smid;
   }
 #endif
   if (threadIdx.x == 0 && *abort_flag) set_error(p.err, PAGEDKV_EFLAG_PIPE_TIMEOUT);
@@ -943,8 +951,19 @@ cudaError_t launch_tc(const CUtensorMap &mk, const CUtensorMap &mv, const TcPara
     if (e != cudaSuccess) return e;
     attr_done.fetch_or(bit, std::memory_order_acq_rel);
   }
-  kern<<<grid, kThreads, L::kAlloc, stream>>>(mk, mv, tp);
-  return cudaGetLastError();
+  // Launched as a programmatic dependent of the previous kernel in the stream
+  // (griddepcontrol in the kernel orders the global reads after it).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, mk, mv, tp);
 }
 
 template <typename T>

@@ -20,6 +20,11 @@ kv_append_vec_kernel(char *__restrict__ k_cache, char *__restrict__ v_cache,
                      const char *__restrict__ v_new, int64_t vs_tok, int64_t vs_head,
                      const int64_t *__restrict__ slots, int32_t num_tokens,
                      int32_t num_kv_heads, int32_t head_dim, int64_t num_slots, unsigned int *err) {
+  // Programmatic dependent launch: let the next kernel (the attention that
+  // reads these rows) start its prologue now; wait for the previous grid's
+  // writes before touching memory.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int chunks_per_head = head_dim >> 3;
   const int chunks_per_row = num_kv_heads * chunks_per_head;
   const int64_t total = (int64_t)num_tokens * chunks_per_row;
@@ -53,6 +58,8 @@ kv_append_scalar_kernel(uint16_t *__restrict__ k_cache, uint16_t *__restrict__ v
                         const int64_t *__restrict__ slots, int32_t num_tokens,
                         int32_t num_kv_heads, int32_t head_dim, int64_t num_slots,
                         unsigned int *err) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int per_row = num_kv_heads * head_dim;
   const int64_t total = (int64_t)num_tokens * per_row;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -115,24 +122,30 @@ cudaError_t launch_kv_append(void *k_cache, void *v_cache, const void *k_new, in
                              bool vectorized, unsigned int *err, cudaStream_t stream) {
   if (num_tokens == 0) return cudaSuccess;
   const int threads = 256;
+  // Launched as a programmatic dependent (see the griddepcontrol pair above).
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(threads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (vectorized) {
     const int64_t total = (int64_t)num_tokens * num_kv_heads * (head_dim / 8);
     const int64_t blocks = (total + threads - 1) / threads;
-    kv_append_vec_kernel<<<(unsigned)(blocks < 65535 * 8 ? blocks : 65535 * 8), threads, 0,
-                           stream>>>(
-        (char *)k_cache, (char *)v_cache, (const char *)k_new, ks_tok, ks_head,
-        (const char *)v_new, vs_tok, vs_head, slots, num_tokens, num_kv_heads, head_dim,
-        num_slots, err);
-  } else {
-    const int64_t total = (int64_t)num_tokens * num_kv_heads * head_dim;
-    const int64_t blocks = (total + threads - 1) / threads;
-    kv_append_scalar_kernel<<<(unsigned)(blocks < 65535 * 8 ? blocks : 65535 * 8), threads, 0,
-                              stream>>>(
-        (uint16_t *)k_cache, (uint16_t *)v_cache, (const uint16_t *)k_new, ks_tok, ks_head,
-        (const uint16_t *)v_new, vs_tok, vs_head, slots, num_tokens, num_kv_heads, head_dim,
-        num_slots, err);
+    cfg.gridDim = dim3((unsigned)(blocks < 65535 * 8 ? blocks : 65535 * 8));
+    return cudaLaunchKernelEx(&cfg, kv_append_vec_kernel, (char *)k_cache, (char *)v_cache,
+                              (const char *)k_new, ks_tok, ks_head, (const char *)v_new, vs_tok,
+                              vs_head, slots, num_tokens, num_kv_heads, head_dim, num_slots, err);
   }
-  return cudaGetLastError();
+  const int64_t total = (int64_t)num_tokens * num_kv_heads * head_dim;
+  const int64_t blocks = (total + threads - 1) / threads;
+  cfg.gridDim = dim3((unsigned)(blocks < 65535 * 8 ? blocks : 65535 * 8));
+  return cudaLaunchKernelEx(&cfg, kv_append_scalar_kernel, (uint16_t *)k_cache, (uint16_t *)v_cache,
+                            (const uint16_t *)k_new, ks_tok, ks_head, (const uint16_t *)v_new,
+                            vs_tok, vs_head, slots, num_tokens, num_kv_heads, head_dim, num_slots,
+                            err);
 }
 
 cudaError_t launch_copy_blocks(void *const *k_ptrs, void *const *v_ptrs, int32_t num_layers,

@@ -228,6 +228,16 @@ __device__ __forceinline__ float warp_max(float v) {
   return r;
 }
 
+// Programmatic dependent launch: wait until the preceding grid in the stream
+// has completed and its memory is visible (a no-op when this grid was not
+// launched as a programmatic dependent), and allow the next grid to launch.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Named barrier over `count` threads that also ORs a predicate across them.
 __device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t count, uint32_t pred) {
   uint32_t r;
