@@ -1,14 +1,22 @@
 #!/usr/bin/env python
 """Benchmark of the B200 paged KV-cache decode path (one JSON line on rank 0).
 
-Workload (one GPU's shard): 256 sequences x 2048-token
-contexts, Qwen2.5-0.5B attention shape (14 query / 2 kv heads, head_dim 64),
-block_size 16, fp16 pool of 40960 blocks with shuffled block tables. One
-"step" = one decode layer-step of the hot path over that batch: the KV append
-of 256 new tokens through a slot mapping, then batched decode attention over
-all 256 contexts (which include the appended token).
+Default workload (one GPU's shard): 256 sequences x
+2048-token contexts, Qwen2.5-0.5B attention shape (14 query / 2 kv heads,
+head_dim 64), block_size 16, fp16 pool of 40960 blocks with shuffled block
+tables. One "step" = one decode layer-step of the hot path over that batch:
+the KV append of 256 new tokens through a slot mapping, then batched decode
+attention over all 256 contexts (which include the appended token).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload cfg2|cfg3|cfg4|cfg4-cow] [--gqa G]
+
+Extra workloads (not the headline): ``cfg3`` = BASELINE config 3 (head_dim
+128, 8 kv heads, GQA G, 128 sequences with log-uniform lengths 16..8192,
+q x30); ``cfg4`` = config 4 (512 sequences in 8 groups sharing a 1024-token
+prefix + 256 own tokens); ``cfg4-cow`` = its copy-on-write variant (each
+group's partially filled fork block is copied to a private block for every
+sequence before its append, every step).
 
 N > 1 runs under torchrun, one process per GPU; sequences are sharded
 data-parallel (each rank owns its own pool, weak scaling) and nothing crosses
@@ -31,6 +39,7 @@ import statistics
 import subprocess
 import sys
 import time
+from dataclasses import dataclass
 from datetime import timedelta
 from pathlib import Path
 
@@ -41,65 +50,193 @@ sys.path.insert(0, str(ROOT))
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-# ---- workload ---------------------------------------------------------------
-NUM_SEQS = 256
-NUM_Q_HEADS = 14
-NUM_KV_HEADS = 2
-HEAD_DIM = 64
-BLOCK_SIZE = 16
-CTX = 2048
-NUM_BLOCKS = 40960
-ELEM = 2  # fp16 bytes
 L2_BYTES = 126 * 1024 * 1024
-
-WORKLOAD = (
-    "cfg2: KV append (256 tokens) + paged GQA decode attention, 256 seqs x 2048 ctx, "
-    "14q/2kv heads, head_dim 64, block_size 16, fp16 pool 40960 blocks, shuffled tables"
-)
+ELEM = 2  # fp16 bytes
+METRIC = "paged-decode KV HBM GB/s"
 
 
-def attention_bytes(num_seqs: int, ctx: int, max_blocks: int) -> int:
-    """Algorithmic bytes of one decode-attention call: every K and V row of every
-    context once, plus q, out, the block tables and seq_lens."""
-    kv = num_seqs * ctx * NUM_KV_HEADS * HEAD_DIM * ELEM * 2
-    qo = num_seqs * NUM_Q_HEADS * HEAD_DIM * ELEM * 2
-    tables = num_seqs * max_blocks * 4 + num_seqs * 4
-    return kv + qo + tables
+# ---- workloads ------------------------------------------------------------------
+@dataclass
+class Workload:
+    """One GPU's shard: host tensors of the step's inputs and the pool shape."""
+
+    name: str
+    description: str
+    num_q_heads: int
+    num_kv_heads: int
+    head_dim: int
+    block_size: int
+    num_blocks: int
+    tables: torch.Tensor        # int32 [N, W]
+    lens: torch.Tensor          # int32 [N] (include the appended token)
+    slots: torch.Tensor         # int64 [N] slot of the appended token
+    q: torch.Tensor             # fp16 [N, Hq, D]
+    k_new: torch.Tensor         # fp16 [N, Hkv, D]
+    v_new: torch.Tensor
+    pairs: torch.Tensor | None  # int64 [M, 2] copy-on-write (src, dst), or None
+
+    @property
+    def num_seqs(self) -> int:
+        return int(self.lens.numel())
+
+    @property
+    def row_bytes(self) -> int:
+        return self.num_kv_heads * self.head_dim * ELEM
+
+    def attention_bytes(self) -> int:
+        """Algorithmic bytes of one decode-attention call: every K and V row of
+        every context once (shared prefixes counted per sequence, as the
+        reference's formula does), plus q, out, the block tables and lengths."""
+        kv = int(self.lens.to(torch.int64).sum()) * self.row_bytes * 2
+        qo = self.num_seqs * self.num_q_heads * self.head_dim * ELEM * 2
+        return kv + qo + self.tables.numel() * 4 + self.num_seqs * 4
+
+    def append_bytes(self) -> int:
+        """Read new K/V, write them into the pool, read the slots."""
+        return self.num_seqs * self.row_bytes * 2 * 2 + self.num_seqs * 8
+
+    def copy_bytes(self) -> int:
+        if self.pairs is None:
+            return 0
+        block = self.block_size * self.row_bytes
+        return int(self.pairs.shape[0]) * (block * 2 * 2 + 16)
+
+    def step_bytes(self) -> int:
+        return self.attention_bytes() + self.append_bytes() + self.copy_bytes()
+
+    def flops(self) -> int:
+        return int(self.lens.to(torch.int64).sum()) * 4 * self.head_dim * self.num_q_heads
+
+    def unique_kv_bytes(self) -> int:
+        """K/V bytes of the distinct blocks the step reads (shared prefixes once)."""
+        blocks = set()
+        for s in range(self.num_seqs):
+            nb = (int(self.lens[s]) + self.block_size - 1) // self.block_size
+            blocks.update(self.tables[s, :nb].tolist())
+        return len(blocks) * self.block_size * self.row_bytes * 2
 
 
-def append_bytes(num_tokens: int) -> int:
-    """Algorithmic bytes of one KV append: read new K/V, write them, read slots."""
-    row = NUM_KV_HEADS * HEAD_DIM * ELEM
-    return num_tokens * row * 2 * 2 + num_tokens * 8
+def _slots_for(tables: torch.Tensor, lens: torch.Tensor, bs: int) -> torch.Tensor:
+    pos = lens.to(torch.int64) - 1
+    blk = tables.to(torch.int64).gather(1, (pos // bs).view(-1, 1)).view(-1)
+    return blk * bs + pos % bs
 
 
-def attention_flops(num_seqs: int, ctx: int) -> int:
-    return num_seqs * ctx * 4 * HEAD_DIM * NUM_Q_HEADS
+def _tables_from_lists(rows: list[list[int]]) -> torch.Tensor:
+    width = max(1, max(len(r) for r in rows))
+    t = torch.zeros(len(rows), width, dtype=torch.int32)
+    for i, r in enumerate(rows):
+        t[i, : len(r)] = torch.tensor(r, dtype=torch.int32)
+    return t
 
 
-def build_shard(rank: int, device, num_seqs: int = NUM_SEQS, ctx: int = CTX, num_blocks: int = NUM_BLOCKS):
-    """Seeded per-rank shard: pool, shuffled tables, new-token K/V, slots, q."""
+def _qkv(g: torch.Generator, n: int, hq: int, hkv: int, d: int, q_scale: float = 1.0):
+    q = (torch.randn(n, hq, d, generator=g) * q_scale).half()
+    return q, torch.randn(n, hkv, d, generator=g).half(), torch.randn(n, hkv, d, generator=g).half()
+
+
+def build_shard(rank: int, device=None, num_seqs: int = 256, ctx: int = 2048, num_blocks: int = 40960):
+    """Config 2 shard as a dict (seeded per rank): shuffled tables, lengths,
+    slots of the appended tokens, q and the new K/V; with a device, also the
+    N(0,1) fp16 K/V pools."""
+    bs, hq, hkv, d = 16, 14, 2, 64
     g = torch.Generator(device="cpu").manual_seed(1000 + rank)
-    blocks_per_seq = (ctx + BLOCK_SIZE - 1) // BLOCK_SIZE
+    blocks_per_seq = (ctx + bs - 1) // bs
     assert num_seqs * blocks_per_seq <= num_blocks
     perm = list(range(num_blocks))
     random.Random(42 + rank).shuffle(perm)
     tables = torch.tensor(perm[: num_seqs * blocks_per_seq], dtype=torch.int32).view(num_seqs, blocks_per_seq)
     lens = torch.full((num_seqs,), ctx, dtype=torch.int32)
-    pos = lens.to(torch.int64) - 1
-    slots = tables.to(torch.int64).gather(1, (pos // BLOCK_SIZE).view(-1, 1)).view(-1) * BLOCK_SIZE + pos % BLOCK_SIZE
-    shard = dict(
-        tables=tables, lens=lens, slots=slots,
-        q=torch.randn(num_seqs, NUM_Q_HEADS, HEAD_DIM, generator=g).half(),
-        k_new=torch.randn(num_seqs, NUM_KV_HEADS, HEAD_DIM, generator=g).half(),
-        v_new=torch.randn(num_seqs, NUM_KV_HEADS, HEAD_DIM, generator=g).half(),
-    )
+    q, k_new, v_new = _qkv(g, num_seqs, hq, hkv, d)
+    shard = dict(tables=tables, lens=lens, slots=_slots_for(tables, lens, bs), q=q, k_new=k_new, v_new=v_new)
     if device is not None:
-        gd = torch.Generator(device=device).manual_seed(2000 + rank)
-        shape = (num_blocks, BLOCK_SIZE, NUM_KV_HEADS, HEAD_DIM)
-        shard["k_cache"] = torch.randn(shape, generator=gd, device=device, dtype=torch.float16)
-        shard["v_cache"] = torch.randn(shape, generator=gd, device=device, dtype=torch.float16)
+        shard.update(make_pools(rank, device, num_blocks, bs, hkv, d))
     return shard
+
+
+def make_pools(rank: int, device, num_blocks: int, bs: int, hkv: int, d: int) -> dict:
+    gd = torch.Generator(device=device).manual_seed(2000 + rank)
+    shape = (num_blocks, bs, hkv, d)
+    return dict(
+        k_cache=torch.randn(shape, generator=gd, device=device, dtype=torch.float16),
+        v_cache=torch.randn(shape, generator=gd, device=device, dtype=torch.float16),
+    )
+
+
+def make_workload(name: str, rank: int, gqa: int = 7) -> Workload:
+    if name == "cfg2":
+        s = build_shard(rank)
+        return Workload(
+            "cfg2",
+            "cfg2: KV append (256 tokens) + paged GQA decode attention, 256 seqs x 2048 ctx, 14q/2kv heads, "
+            "head_dim 64, block_size 16, fp16 pool 40960 blocks, shuffled tables",
+            14, 2, 64, 16, 40960, s["tables"], s["lens"], s["slots"], s["q"], s["k_new"], s["v_new"], None,
+        )
+    if name == "cfg3":
+        n, hkv, d, bs = 128, 8, 128, 16
+        hq = hkv * gqa
+        rng = np.random.default_rng(3000 + rank)
+        lens_l = [int(round(math.exp(x))) for x in rng.uniform(math.log(16), math.log(8192), n)]
+        need = [(x + bs - 1) // bs for x in lens_l]
+        nb = sum(need) + 1024
+        perm = list(range(nb))
+        random.Random(43 + rank).shuffle(perm)
+        rows, at = [], 0
+        for c in need:
+            rows.append(perm[at : at + c])
+            at += c
+        tables = _tables_from_lists(rows)
+        lens = torch.tensor(lens_l, dtype=torch.int32)
+        g = torch.Generator().manual_seed(1100 + rank)
+        q, k_new, v_new = _qkv(g, n, hq, hkv, d, q_scale=30.0)
+        return Workload(
+            "cfg3",
+            f"cfg3: KV append + paged decode attention, 128 seqs, lengths log-uniform 16..8192, head_dim 128, "
+            f"{hq}q/{hkv}kv heads (GQA {gqa}), block_size 16, q x30, shuffled tables",
+            hq, hkv, d, bs, nb, tables, lens, _slots_for(tables, lens, bs), q, k_new, v_new, None,
+        )
+    if name in ("cfg4", "cfg4-cow"):
+        groups, per_group, hq, hkv, d, bs = 8, 64, 14, 2, 64, 16
+        n = groups * per_group
+        prefix_blocks = 1024 // bs
+        cow = name == "cfg4-cow"
+        own = 1 if cow else 256 // bs
+        nb = groups * (prefix_blocks + (1 if cow else 0)) + n * own + 64
+        perm = list(range(nb))
+        random.Random(44 + rank).shuffle(perm)
+        at = 0
+        prefixes, forks = [], []
+        for _ in range(groups):
+            prefixes.append(perm[at : at + prefix_blocks])
+            at += prefix_blocks
+            if cow:
+                forks.append(perm[at])
+                at += 1
+        rows, pairs = [], []
+        for s in range(n):
+            gi = s // per_group
+            mine = perm[at : at + own]
+            at += own
+            rows.append(prefixes[gi] + mine)
+            if cow:
+                pairs.append((forks[gi], mine[0]))
+        tables = _tables_from_lists(rows)
+        ctx = 1024 + (8 + 1 if cow else 256)
+        lens = torch.full((n,), ctx, dtype=torch.int32)
+        g = torch.Generator().manual_seed(1200 + rank)
+        q, k_new, v_new = _qkv(g, n, hq, hkv, d)
+        desc = (
+            "cfg4-cow: copy-on-write of each group's shared fork block (8 tokens) to 512 private blocks, "
+            "then KV append + decode attention; 8 groups x 64 seqs sharing a 1024-token prefix, ctx 1033"
+            if cow
+            else "cfg4: KV append + decode attention; 8 groups x 64 seqs sharing a 1024-token prefix "
+            "(identical block ids) + 256 own tokens, ctx 1280"
+        ) + ", 14q/2kv heads, head_dim 64, block_size 16, fp16"
+        return Workload(
+            name, desc, hq, hkv, d, bs, nb, tables, lens, _slots_for(tables, lens, bs), q, k_new, v_new,
+            torch.tensor(pairs, dtype=torch.int64) if cow else None,
+        )
+    raise SystemExit(f"unknown workload {name}")
 
 
 # ---- clocks -------------------------------------------------------------------
@@ -116,7 +253,6 @@ class ClockSampler:
         self.gpus = gpu_indices
         self.interval = interval_ms
         self.proc = None
-        self.lines: list[str] = []
 
     def start(self):
         try:
@@ -169,52 +305,85 @@ class ClockSampler:
 
 
 # ---- reference arm / CPU baseline ---------------------------------------------
-def _cpu_sample(num_seqs: int):
-    """A bounded sample of the workload for the CPU reference: ``num_seqs``
-    sequences of the rank-0 shard with their pool blocks gathered into a
-    compact pool (same values the GPU reads; fp32 as the reference's CPU path)."""
-    shard = build_shard(0, None, num_seqs=num_seqs, ctx=CTX, num_blocks=num_seqs * (CTX // BLOCK_SIZE))
+def _cpu_sample(wl: Workload, num_seqs: int):
+    """A bounded sample of the workload for the CPU reference: its first
+    ``num_seqs`` sequences with their pool blocks gathered into a compact fp32
+    pool (shared blocks stay shared)."""
+    n = min(num_seqs, wl.num_seqs)
+    blocks = []
+    rows = []
+    index = {}
+    for s in range(n):
+        nb = (int(wl.lens[s]) + wl.block_size - 1) // wl.block_size
+        row = []
+        for b in wl.tables[s, :nb].tolist():
+            if b not in index:
+                index[b] = len(blocks)
+                blocks.append(b)
+            row.append(index[b])
+        rows.append(row)
+    pairs = None
+    if wl.pairs is not None:
+        pl = []
+        for src, dst in wl.pairs[:n].tolist():
+            for b in (src, dst):
+                if b not in index:
+                    index[b] = len(blocks)
+                    blocks.append(b)
+            pl.append((index[src], index[dst]))
+        pairs = np.asarray(pl, dtype=np.int64)
     g = torch.Generator().manual_seed(7)
-    nb = num_seqs * (CTX // BLOCK_SIZE)
-    k = torch.randn(nb, BLOCK_SIZE, NUM_KV_HEADS, HEAD_DIM, generator=g).half().float()
-    v = torch.randn(nb, BLOCK_SIZE, NUM_KV_HEADS, HEAD_DIM, generator=g).half().float()
-    return shard, k, v
+    shape = (len(blocks), wl.block_size, wl.num_kv_heads, wl.head_dim)
+    k = torch.randn(shape, generator=g).half().float()
+    v = torch.randn(shape, generator=g).half().float()
+    lens = [int(x) for x in wl.lens[:n]]
+    slots = np.asarray(
+        [rows[s][(lens[s] - 1) // wl.block_size] * wl.block_size + (lens[s] - 1) % wl.block_size for s in range(n)],
+        dtype=np.int64,
+    )
+    sample_bytes = (
+        sum(lens) * wl.row_bytes * 2 + n * wl.num_q_heads * wl.head_dim * ELEM * 2 + n * wl.tables.shape[1] * 4 + n * 4
+        + n * wl.row_bytes * 2 * 2 + n * 8
+        + (0 if pairs is None else len(pairs) * (wl.block_size * wl.row_bytes * 2 * 2 + 16))
+    )
+    return dict(rows=rows, lens=lens, slots=slots, pairs=pairs, k=k, v=v, q=wl.q[:n].float(),
+                k_new=wl.k_new[:n].float().numpy(), v_new=wl.v_new[:n].float().numpy(), n=n,
+                bytes=sample_bytes, scale=1.0 / math.sqrt(wl.head_dim))
 
 
-def cpu_reference_step(shard, k, v) -> None:
+def cpu_reference_step(sm: dict) -> None:
     from oracle import paged_ref
 
-    tables = shard["tables"].tolist()
-    lens = shard["lens"].tolist()
-    kc, vc = k.numpy(), v.numpy()
-    paged_ref.kv_append_ref(kc, vc, shard["k_new"].float().numpy(), shard["v_new"].float().numpy(), shard["slots"].numpy())
-    paged_ref.paged_attention_ref(shard["q"].float(), k, v, tables, lens, 1.0 / math.sqrt(HEAD_DIM))
+    kc, vc = sm["k"].numpy(), sm["v"].numpy()
+    if sm["pairs"] is not None:
+        paged_ref.copy_blocks_ref([kc], [vc], sm["pairs"])
+    paged_ref.kv_append_ref(kc, vc, sm["k_new"], sm["v_new"], sm["slots"])
+    paged_ref.paged_attention_ref(sm["q"], sm["k"], sm["v"], sm["rows"], sm["lens"], sm["scale"])
 
 
-def time_cpu_reference(num_seqs: int, min_seconds: float) -> dict:
-    shard, k, v = _cpu_sample(num_seqs)
+def time_cpu_reference(wl: Workload, num_seqs: int, min_seconds: float) -> dict:
+    sm = _cpu_sample(wl, num_seqs)
     threads = torch.get_num_threads()
-    cpu_reference_step(shard, k, v)  # warm
+    cpu_reference_step(sm)  # warm
     n, t0 = 0, time.perf_counter()
     while True:
-        cpu_reference_step(shard, k, v)
+        cpu_reference_step(sm)
         n += 1
         el = time.perf_counter() - t0
         if el >= min_seconds:
             break
     per = el / n
-    nbytes = attention_bytes(num_seqs, CTX, CTX // BLOCK_SIZE) + append_bytes(num_seqs)
     return {
-        "value": round(nbytes / per / 1e9, 3),
+        "value": round(sm["bytes"] / per / 1e9, 3),
         "unit": "GB/s",
         "cores": threads,
         "kind": "port",
         "sample": (
-            f"{num_seqs} of the 256 sequences (2048 tokens each), fp32 torch restatement of the reference's "
-            f"naive_reference_paged_attention + append, {n} calls over {el:.1f} s, {threads} threads "
-            f"(os.cpu_count()={os.cpu_count()})"
+            f"first {sm['n']} of the {wl.num_seqs} sequences of {wl.name}, fp32 torch restatement of the "
+            f"reference's naive_reference_paged_attention + append"
+            f"{' + copy-on-write' if sm['pairs'] is not None else ''}, {n} calls over {el:.1f} s, "
+            f"{threads} threads (os.cpu_count()={os.cpu_count()})"
         ),
-        "seconds_per_sample": per,
     }
 
 
@@ -223,22 +392,21 @@ def run_reference_arm(args) -> None:
     if rank != 0:
         return
     torch.set_num_threads(os.cpu_count() or 1)
-    sample = 8
-    shard, k, v = _cpu_sample(sample)
+    wl = make_workload(args.workload, 0, args.gqa)
+    sm = _cpu_sample(wl, 8)
     for _ in range(args.warmup):
-        cpu_reference_step(shard, k, v)
+        cpu_reference_step(sm)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        cpu_reference_step(shard, k, v)
+        cpu_reference_step(sm)
         times.append(time.perf_counter() - t0)
     per = sum(times) / len(times)
-    nbytes = attention_bytes(sample, CTX, CTX // BLOCK_SIZE) + append_bytes(sample)
-    value = nbytes / per / 1e9
+    value = sm["bytes"] / per / 1e9
     threads = torch.get_num_threads()
     line = {
         "impl": "reference",
-        "metric": "paged-decode KV HBM GB/s",
+        "metric": METRIC,
         "value": round(value, 3),
         "unit": "GB/s",
         "n_gpus": args.gpus,
@@ -250,10 +418,10 @@ def run_reference_arm(args) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample_seqs_per_step": sample, "parallelism": "host cores of rank 0"},
+        "config": {"workload": wl.description, "sample_seqs_per_step": sm["n"], "parallelism": "host cores of rank 0"},
         "cpu_baseline": {
             "value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{sample} sequences x 2048 tokens per step (fp32 oracle restatement, torch CPU)",
+            "sample": f"first {sm['n']} sequences of {wl.name} per step (fp32 oracle restatement, torch CPU)",
         },
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -292,9 +460,9 @@ def _sum_over_ranks(dist, value: float, device) -> float:
     return float(t.item())
 
 
-def _read_traffic(kernel: str) -> int | None:
+def _read_traffic(kernel: str, workload: str) -> int | None:
     p = ROOT / "profiles" / "traffic.json"
-    if not p.exists():
+    if not p.exists() or workload != "cfg2":
         return None
     try:
         data = json.loads(p.read_text())
@@ -307,37 +475,42 @@ def _read_traffic(kernel: str) -> int | None:
 def run_ours(args) -> None:
     import pagedkv
     from pagedkv import _native
+    from oracle import paged_ref  # checker only, outside the timed region
 
     dist, rank, world, local = _dist_setup(args)
     dev = torch.device("cuda", local)
     _native.lib()
-    shard = build_shard(rank, dev)
-    q = shard["q"].to(dev)
-    tables = shard["tables"].to(dev)
-    lens = shard["lens"].to(dev)
-    slots = shard["slots"].to(dev)
-    k_new = shard["k_new"].to(dev)
-    v_new = shard["v_new"].to(dev)
-    kc, vc = shard["k_cache"], shard["v_cache"]
-    scale = 1.0 / math.sqrt(HEAD_DIM)
+    wl = make_workload(args.workload, rank, args.gqa)
+    pools = make_pools(rank, dev, wl.num_blocks, wl.block_size, wl.num_kv_heads, wl.head_dim)
+    kc, vc = pools["k_cache"], pools["v_cache"]
+    q = wl.q.to(dev)
+    tables = wl.tables.to(dev)
+    lens = wl.lens.to(dev)
+    slots = wl.slots.to(dev)
+    k_new = wl.k_new.to(dev)
+    v_new = wl.v_new.to(dev)
+    pairs = wl.pairs.to(dev) if wl.pairs is not None else None
+    scale = 1.0 / math.sqrt(wl.head_dim)
     stream = torch.cuda.current_stream(dev)
 
     def step():
+        if pairs is not None:
+            pagedkv.copy_blocks([kc], [vc], pairs)
         pagedkv.kv_append(k_new, v_new, kc, vc, slots)
         return pagedkv.paged_attention_decode_batched(q, kc, vc, tables, lens, scale)
 
-    # correctness spot-check of this shard against the oracle (2 sequences)
+    # correctness spot-check of this shard against the oracle (first and last sequence)
     out = step()
     torch.cuda.synchronize(dev)
-    from oracle import paged_ref  # checker only, outside the timed region
-
-    sel = [0, NUM_SEQS - 1]
-    used = sorted({int(b) for s in sel for b in shard["tables"][s].tolist()})
+    sel = [0, wl.num_seqs - 1]
+    nbk = [(int(wl.lens[s]) + wl.block_size - 1) // wl.block_size for s in sel]
+    used = sorted({int(b) for s, n in zip(sel, nbk) for b in wl.tables[s, :n].tolist()})
     remap = {b: i for i, b in enumerate(used)}
     idx = torch.tensor(used, device=dev)
     ref = paged_ref.paged_attention_ref(
         q[sel].float().cpu(), kc[idx].float().cpu(), vc[idx].float().cpu(),
-        [[remap[int(b)] for b in shard["tables"][s].tolist()] for s in sel], [CTX, CTX], scale,
+        [[remap[int(b)] for b in wl.tables[s, :n].tolist()] for s, n in zip(sel, nbk)],
+        [int(wl.lens[s]) for s in sel], scale,
     )
     max_err = (out[sel].float().cpu() - ref).abs().max().item()
     if not max_err < 2e-3 + 2e-3 * ref.abs().max().item():
@@ -348,9 +521,9 @@ def run_ours(args) -> None:
         step()
     torch.cuda.synchronize(dev)
 
-    # The decode step (append + attention) and the attention alone, each
-    # captured once as a CUDA graph and replayed: a serving engine replays the
-    # decode step the same way, so the device time is not bounded by Python.
+    # The decode step and the attention alone, each captured once as a CUDA
+    # graph and replayed: a serving engine replays the decode step the same
+    # way, so the device time is not bounded by Python.
     g_step = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_step):
         step()
@@ -389,30 +562,33 @@ def run_ours(args) -> None:
     eager_ms = _max_over_ranks(dist, eager_ms, dev)
     ms_per_step = total_ms / args.steps
 
-    max_blocks = CTX // BLOCK_SIZE
-    a_bytes = attention_bytes(NUM_SEQS, CTX, max_blocks)
-    p_bytes = append_bytes(NUM_SEQS)
-    step_bytes = a_bytes + p_bytes
+    a_bytes = wl.attention_bytes()
+    step_bytes = wl.step_bytes()
     value = world * step_bytes / (ms_per_step * 1e-3) / 1e9
 
     # ---- end to end through the public API from pinned host buffers -------------
-    h_q = shard["q"].pin_memory()
-    h_k = shard["k_new"].pin_memory()
-    h_v = shard["v_new"].pin_memory()
-    h_slots = shard["slots"].pin_memory()
-    h_tables = shard["tables"].pin_memory()
-    h_lens = shard["lens"].pin_memory()
+    # The step's inputs (q, new K/V, slots, tables, lengths) are staged in one
+    # pinned host buffer and moved with ONE host->device copy; the output comes
+    # back with one device->host copy. Every step copies them again.
+    parts = [wl.q, wl.k_new, wl.v_new, wl.slots, wl.tables, wl.lens]
+    sizes = [t.numel() * t.element_size() for t in parts]
+    offs = [0]
+    for sz in sizes:
+        offs.append(offs[-1] + (sz + 255) // 256 * 256)
+    h_in = torch.empty(offs[-1], dtype=torch.uint8).pin_memory()
+    for t, o, sz in zip(parts, offs, sizes):
+        h_in[o : o + sz].copy_(t.contiguous().view(-1).view(torch.uint8))
+    d_in = torch.empty(offs[-1], dtype=torch.uint8, device=dev)
+    views = [d_in[o : o + sz].view(t.dtype).view(t.shape) for t, o, sz in zip(parts, offs, sizes)]
     h_out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_slots, h_tables, h_lens))
+    h2d = sum(sizes)
     d2h = h_out.numel() * h_out.element_size()
 
     def e2e_step():
-        dq = h_q.to(dev, non_blocking=True)
-        dk = h_k.to(dev, non_blocking=True)
-        dv = h_v.to(dev, non_blocking=True)
-        ds = h_slots.to(dev, non_blocking=True)
-        dt = h_tables.to(dev, non_blocking=True)
-        dl = h_lens.to(dev, non_blocking=True)
+        d_in.copy_(h_in, non_blocking=True)
+        dq, dk, dv, ds, dt, dl = views
+        if pairs is not None:
+            pagedkv.copy_blocks([kc], [vc], pairs)
         pagedkv.kv_append(dk, dv, kc, vc, ds)
         o = pagedkv.paged_attention_decode_batched(dq, kc, vc, dt, dl, scale)
         h_out.copy_(o, non_blocking=True)
@@ -420,40 +596,31 @@ def run_ours(args) -> None:
     for _ in range(max(3, args.warmup)):
         e2e_step()
     torch.cuda.synchronize(dev)
-    if dist:
-        dist.barrier()
-    e_s, e_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_s.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e_e.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = _max_over_ranks(dist, e_s.elapsed_time(e_e), dev) / args.steps
+    e2e_ms = _max_over_ranks(dist, timed(e2e_step, args.steps), dev) / args.steps
     e2e_value = world * step_bytes / (e2e_ms * 1e-3) / 1e9
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
-        cpu = time_cpu_reference(num_seqs=16, min_seconds=args.cpu_seconds)
-        cpu.pop("seconds_per_sample", None)
+        cpu = time_cpu_reference(wl, 16, args.cpu_seconds)
 
     peaks = {}
     pp = ROOT / "MEASURED_PEAKS.json"
     if pp.exists():
         peaks = json.loads(pp.read_text())
     peak = float(peaks.get("hbm_gbs", 6650.0))
-    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    measured_peak = "hbm_gbs" in peaks
     achieved = a_bytes / (attn_ms * 1e-3) / 1e9
     kernel_name = f"decode_{family}"
-    traffic = _read_traffic(kernel_name)
-    launches_per_step = 1 + launches_attn  # append + (counter reset and) attention kernel
+    traffic = _read_traffic(kernel_name, wl.name)
+    launches_per_step = 1 + launches_attn + (1 if pairs is not None else 0)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
     line = {
-        "metric": "paged-decode KV HBM GB/s",
+        "metric": METRIC,
         "value": round(value, 2),
         "unit": "GB/s",
         "n_gpus": world,
@@ -466,34 +633,36 @@ def run_ours(args) -> None:
         "dtype": "f16",
         "data": "synthetic",
         "config": {
-            "workload": WORKLOAD,
-            "num_seqs_per_gpu": NUM_SEQS,
-            "ctx": CTX,
-            "heads": f"{NUM_Q_HEADS}q/{NUM_KV_HEADS}kv",
-            "head_dim": HEAD_DIM,
-            "block_size": BLOCK_SIZE,
-            "num_blocks": NUM_BLOCKS,
+            "workload": wl.description,
+            "num_seqs_per_gpu": wl.num_seqs,
+            "total_context_tokens_per_gpu": int(wl.lens.to(torch.int64).sum()),
+            "heads": f"{wl.num_q_heads}q/{wl.num_kv_heads}kv",
+            "head_dim": wl.head_dim,
+            "block_size": wl.block_size,
+            "num_blocks": wl.num_blocks,
             "decode_kernel": family,
-            "l2": f"inputs exceed L2: {a_bytes / 1e6:.1f} MB read per step vs {L2_BYTES / 2**20:.0f} MiB L2, no flush",
+            "l2": f"inputs exceed L2: {a_bytes / 1e6:.1f} MB read per step vs {L2_BYTES / 2**20:.0f} MiB L2, no flush"
+            if a_bytes > L2_BYTES else f"{a_bytes / 1e6:.1f} MB read per step, below the {L2_BYTES / 2**20:.0f} MiB L2",
             "parallelism": f"dp{world}: sequences sharded, one pool per GPU, no collective on the data path",
             "bytes_per_step": step_bytes,
+            "unique_kv_bytes_per_step": wl.unique_kv_bytes(),
         },
-        "decode_tokens_per_s": round(world * NUM_SEQS / (ms_per_step * 1e-3), 1),
+        "decode_tokens_per_s": round(world * wl.num_seqs / (ms_per_step * 1e-3), 1),
         "attention_ms": round(attn_ms_max, 5),
         "append_ms": round(append_ms, 5),
-        "timing": "CUDA-graph replay of the step (append + attention), CUDA events on the launch stream",
+        "timing": "CUDA-graph replay of the step, CUDA events on the launch stream",
         "eager_ms_per_step": round(eager_ms, 5),
         "roofline": {
             "bound": "hbm",
             "kernel": kernel_name,
             "achieved": round(achieved, 1),
             "peak": peak,
-            "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else "fallback 6650 GB/s",
+            "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if measured_peak else "fallback 6650 GB/s",
             "unit": "GB/s",
             "frac": round(achieved / peak, 4),
             "traffic": traffic,
             "algorithmic_bytes_per_launch": a_bytes,
-            "flops_per_launch": attention_flops(NUM_SEQS, CTX),
+            "flops_per_launch": wl.flops(),
         },
         "cpu_baseline": cpu,
         "e2e": {
@@ -502,7 +671,7 @@ def run_ours(args) -> None:
             "ms_per_step": round(e2e_ms, 5),
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
-            "api": "pagedkv.kv_append + pagedkv.paged_attention_decode_batched from pinned host buffers",
+            "api": "pagedkv public API; step inputs staged in one pinned buffer, one H2D and one D2H copy per step",
         },
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
@@ -517,6 +686,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg4-cow"], default="cfg2")
+    ap.add_argument("--gqa", type=int, default=7, help="GQA group for --workload cfg3 (1, 2, 4 or 7)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()

@@ -66,7 +66,7 @@ constexpr float kRescaleLog2 = 8.f;            // lazy-rescale threshold (log2 u
 // Optional wait-time trace (build with -DPAGEDKV_TRACE; off in the product
 // build): per CTA and warp role, nanoseconds spent in each pipeline wait.
 #ifdef PAGEDKV_TRACE
-constexpr int kTraceSlots = 8;
+constexpr int kTraceSlots = 16;
 constexpr int kTraceCtas = 160;
 __device__ unsigned long long g_trace[kTraceCtas][4][kTraceSlots];
 #define PKV_TW(slot, expr)             \
@@ -83,10 +83,12 @@ __device__ unsigned long long g_trace[kTraceCtas][4][kTraceSlots];
     tw[slot] += clock64() - _t0;        \
   } while (0)
 #define PKV_TADD(slot, v) (tw[slot] += (v))
+#define PKV_STAMP(var) const uint64_t var = clock64()
 #else
 #define PKV_TW(slot, expr) (expr)
 #define PKV_TV(slot, stmt) stmt
 #define PKV_TADD(slot, v) ((void)0)
+#define PKV_STAMP(var) ((void)0)
 #endif
 
 struct TcParams {
@@ -230,7 +232,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
   const int lane = threadIdx.x & 31;
   const DecodeParams &p = tp.p;
 #ifdef PAGEDKV_TRACE
-  uint64_t tw[kTraceSlots] = {0, 0, 0, 0, 0, 0, 0, 0};
+  uint64_t tw[kTraceSlots] = {};
   const uint64_t t_kernel0 = globaltimer_ns();
   const uint64_t c_kernel0 = clock64();
 #endif
@@ -336,69 +338,83 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 
   if (warp == 0 || warp == 6) {
     // ------------------------------------------------ producers: warp 0 K (+ Q), warp 6 V
+    // Global loads the TMA issue depends on are issued one tile ahead: the
+    // block-table entries of the next tile (also across a piece boundary) and
+    // the next piece's Q rows (K producer), so a stage freed by the consumer is
+    // refilled without a dependent round trip to L2.
     const bool is_k = warp == 0;
     const CUtensorMap *tmap = is_k ? &tmap_k : &tmap_v;
     const int nst = is_k ? SK : SV;
     const uint32_t ring = sbase + (is_k ? L::kOffK : L::kOffV);
     if (lane == 0) tma_prefetch_desc(tmap);
     const uint64_t policy = l2_policy_evict_first();
-    const int blocks_per_tile = kTile / p.block_size;
+    const int blocks_per_tile = kTile / p.block_size;  // <= 16 lanes
+    constexpr int kQChunks = 16 * N / 32;               // Q 16-byte chunks per lane
     int stage = 0;
     uint32_t sphase = 0;
     uint32_t qi = 0;
     int issued = 0;
     bool ok = true;
-    Piece pc;
-    while (ok && walk.next(tp, pc)) {
-      if (is_k) {
-        // Stage Q for this piece: block-diagonal B operand [N rows x 128], K-major SW128.
-        const uint32_t qb = qi & 1u;
-        if (!PKV_TW(0, mbar_wait(bar2(7, qb), ((qi >> 1) & 1u) ^ 1u, abort_flag, kTimeoutNs))) { ok = false; break; }
-        const uint32_t qbuf = sbase + L::kOffQ + qb * L::kQBytes;
-        for (int idx = lane; idx < 16 * N; idx += 32) {
-          const int xh = idx / (8 * N);
-          const int rem = idx - xh * 8 * N;
-          const int n = rem >> 3, ch = rem & 7;
-          const int hl = n / GP, g = n - hl * GP;
-          const int kv = pc.hg * H + hl;
-          uint4 val = make_uint4(0u, 0u, 0u, 0u);
-          if (hl < H && g < p.group && kv < p.hkv && (H == 1 || xh == hl)) {
-            const int d = (H == 1 ? xh * 64 : 0) + ch * 8;
-            val = ldg16(reinterpret_cast<const T *>(p.q) + (int64_t)pc.seq * p.q_ss +
+
+    // Block-table entry this lane needs for tile j of piece q, or kNoBlock
+    // when the lane's block lies past the piece (fetched as zeros).
+    constexpr int64_t kNoBlock = -(1ll << 40);
+    auto bt_entry = [&](const Piece &q, int j) -> int64_t {
+      const int lb = (q.t0 + j * kTile) / p.block_size + lane;
+      const int need = (q.t1 + p.block_size - 1) / p.block_size;
+      if (lane >= blocks_per_tile || lb >= need) return kNoBlock;
+      return (int64_t)__ldg(p.bt + (int64_t)q.seq * p.bt_s + lb);
+    };
+    auto q_load = [&](const Piece &q, uint4 (&qr)[kQChunks]) {
+#pragma unroll
+      for (int c = 0; c < kQChunks; ++c) {
+        const int idx = lane + c * 32;
+        const int xh = idx / (8 * N);
+        const int rem = idx - xh * 8 * N;
+        const int n = rem >> 3, ch = rem & 7;
+        const int hl = n / GP, g = n - hl * GP;
+        const int kv = q.hg * H + hl;
+        qr[c] = make_uint4(0u, 0u, 0u, 0u);
+        if (hl < H && g < p.group && kv < p.hkv && (H == 1 || xh == hl)) {
+          const int d = (H == 1 ? xh * 64 : 0) + ch * 8;
+          qr[c] = ldg16(reinterpret_cast<const T *>(p.q) + (int64_t)q.seq * p.q_ss +
                         (int64_t)(kv * p.group + g) * p.q_sh + d);
-          }
-          const uint32_t addr = qbuf + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
-          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(val.x), "r"(val.y),
-                       "r"(val.z), "r"(val.w)
-                       : "memory");
         }
-        fence_proxy_async_smem();
-        mbar_arrive(bar2(6, qb));
-        ++qi;
       }
-      const int need_blocks = (pc.t1 + p.block_size - 1) / p.block_size;
-      const int32_t *bt = p.bt + (int64_t)pc.seq * p.bt_s;
-      const int x0 = pc.hg * 128;
+    };
+
+    Piece pc;
+    bool have = walk.next(tp, pc);
+    Walker peek = walk;  // walker positioned after pc: peek.next() yields the piece after it
+    int64_t bt_next = have ? bt_entry(pc, 0) : kNoBlock;
+    uint4 qr[kQChunks];
+    if (have && is_k) q_load(pc, qr);
+    while (ok && have) {
+      Piece nx;
+      Walker after = peek;
+      const bool have_nx = after.next(tp, nx);
       for (int j = 0; j < pc.ntiles; ++j) {
+        const int64_t blk = bt_next;
+        // Prefetch the entries of the tile after this one.
+        if (j + 1 < pc.ntiles) bt_next = bt_entry(pc, j + 1);
+        else bt_next = have_nx ? bt_entry(nx, 0) : kNoBlock;
+        if (!PKV_TW(1, mbar_wait(is_k ? kempty(stage) : vempty(stage), sphase ^ 1u, abort_flag, kTimeoutNs))) {
+          ok = false;
+          break;
+        }
         const uint32_t full = is_k ? kfull(stage) : vfull(stage);
-        const uint32_t emp = is_k ? kempty(stage) : vempty(stage);
-        if (!PKV_TW(1, mbar_wait(emp, sphase ^ 1u, abort_flag, kTimeoutNs))) { ok = false; break; }
         if (lane == 0) mbar_arrive_expect_tx(full, kOperandBytes);
         __syncwarp();
-        const int lb0 = (pc.t0 + j * kTile) / p.block_size;
         const uint32_t dst = ring + stage * kOperandBytes;
-        for (int bi = lane; bi < blocks_per_tile; bi += 32) {
-          const int lb = lb0 + bi;
+        const int x0 = pc.hg * 128;
+        if (lane < blocks_per_tile) {
           int32_t y = tp.oob_row;  // out of range: TMA fills zeros, reads nothing
-          if (lb < need_blocks) {
-            const int blk = __ldg(bt + lb);
-            if (blk >= 0 && (int64_t)blk < p.num_blocks) {
-              y = blk * p.block_size;
-            } else if (is_k) {
-              set_error(p.err, PAGEDKV_EFLAG_BLOCK_ID_RANGE);
-            }
+          if (blk >= 0 && blk < p.num_blocks) {
+            y = (int32_t)blk * p.block_size;
+          } else if (blk != kNoBlock && is_k) {
+            set_error(p.err, PAGEDKV_EFLAG_BLOCK_ID_RANGE);
           }
-          const uint32_t off = bi * p.block_size * 128;
+          const uint32_t off = lane * p.block_size * 128;
           tma_load_2d(dst + off, tmap, x0, y, full, policy);
           tma_load_2d(dst + kHalfBytes + off, tmap, x0 + 64, y, full, policy);
         }
@@ -407,7 +423,35 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           stage = 0;
           sphase ^= 1u;
         }
+        if (is_k && j == 0) {
+          // Stage Q (loaded into registers one piece ahead) as the
+          // block-diagonal B operand [N rows x 128], K-major SW128.
+          const uint32_t qb = qi & 1u;
+          if (!PKV_TW(0, mbar_wait(bar2(7, qb), ((qi >> 1) & 1u) ^ 1u, abort_flag, kTimeoutNs))) {
+            ok = false;
+            break;
+          }
+          const uint32_t qbuf = sbase + L::kOffQ + qb * L::kQBytes;
+#pragma unroll
+          for (int c = 0; c < kQChunks; ++c) {
+            const int idx = lane + c * 32;
+            const int xh = idx / (8 * N);
+            const int rem = idx - xh * 8 * N;
+            const int n = rem >> 3, ch = rem & 7;
+            const uint32_t addr = qbuf + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(qr[c].x), "r"(qr[c].y),
+                         "r"(qr[c].z), "r"(qr[c].w)
+                         : "memory");
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(bar2(6, qb));
+          ++qi;
+          if (have_nx) q_load(nx, qr);  // next piece's Q, in flight while its tiles wait
+        }
       }
+      pc = nx;
+      have = have_nx;
+      peek = after;
     }
     // Drain: the last min(issued, ring size) tiles' loads must have landed
     // before this CTA's shared memory is released (immediate on the normal path).
@@ -538,6 +582,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     }
 
     Piece pc;
+#ifdef PAGEDKV_TRACE
+    uint64_t t_piece_end = clock64();
+#endif
     while (walk.next(tp, pc)) {
       float m_ref[N], l_part[N], alpha_prev[N], acc[GP];
 #pragma unroll
@@ -579,8 +626,16 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       for (int j = 0; j < pc.ntiles; ++j) {
         const uint32_t b = gt & 1u;
         const uint32_t bph = (gt >> 1) & 1u;
+#ifdef PAGEDKV_TRACE
+        if (j == 0) tw[11] += clock64() - t_piece_end;
+        const uint64_t t_sw0 = clock64();
+#endif
         PKV_TW(0, mbar_wait(bar2(0, b), bph, abort_flag, kTimeoutNs));
         PKV_TADD(5, 1);
+#ifdef PAGEDKV_TRACE
+        if (j == 0) tw[14] += clock64() - t_sw0;
+        const uint64_t t_sm0 = clock64();
+#endif
         tc_fence_after();
         float s[N];
         tmem_ld<N>(tl + b * N, s);
@@ -661,6 +716,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         }
         fence_proxy_async_smem();
         mbar_arrive(bar2(2, b));
+#ifdef PAGEDKV_TRACE
+        tw[13] += clock64() - t_sm0;
+#endif
         if (j > 0) correction(gt - 1, resc_prev);
         if (resc) {
 #pragma unroll
@@ -669,9 +727,13 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         resc_prev = resc;
         ++gt;
       }
+#ifdef PAGEDKV_TRACE
+      const uint64_t t_cor0 = clock64();
+#endif
       if (pc.ntiles > 0) correction(gt - 1, resc_prev);
 #ifdef PAGEDKV_TRACE
       const uint64_t t_epi0 = clock64();
+      tw[12] += t_epi0 - t_cor0;
       tw[6] += 1;
 #endif
 
@@ -684,6 +746,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         if (lane == 0) red_l[q4 * N + n] = v;
       }
       named_bar(1, 128);
+#ifdef PAGEDKV_TRACE
+      const uint64_t t_e1 = clock64();
+      tw[8] += t_e1 - t_epi0;
+#endif
       float l_sel[GP], m_sel[GP];
 #pragma unroll
       for (int g = 0; g < GP; ++g) {
@@ -695,6 +761,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         m_sel[g] = (H == 2 && hl == 1) ? m_ref[n1] : m_ref[g];
       }
       named_bar(1, 128);  // red_l is rewritten by the next piece
+#ifdef PAGEDKV_TRACE
+      const uint64_t t_e2 = clock64();
+      tw[9] += t_e2 - t_e1;
+#endif
 
       const int kv = pc.hg * H + hl;
       const bool have = kv < p.hkv;
@@ -710,6 +780,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
             }
           }
         }
+#ifdef PAGEDKV_TRACE
+        tw[10] += clock64() - t_e2;
+#endif
       } else if (pc.t0 > 0) {
         // Continuation of a segment that began in an earlier CTA: this is this
         // CTA's first piece. Publish it (partial + release flag) for the CTA
@@ -797,7 +870,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 #endif
       }
 #ifdef PAGEDKV_TRACE
-      tw[4] += clock64() - t_epi0;
+      t_piece_end = clock64();
+      tw[4] += t_piece_end - t_epi0;
 #endif
     }
   }
