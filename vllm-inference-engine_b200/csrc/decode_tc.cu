@@ -21,21 +21,31 @@
 //     (block-diagonal Q when H = 2, so one MMA serves both kv heads).
 //     Accumulator in TMEM, one token row per TMEM lane.
 //   * Softmax warps (128 threads, one token row each) read S, mask tokens past
-//     the end, take the tile max with redux.sync, write P (fp16/bf16) to shared
-//     memory as the (MN-major) B operand of the second MMA.
+//     the end, vote on a lazy rescale (the tile max is reduced only when some
+//     score exceeds the reference max by 2^8), write P (fp16/bf16) to shared
+//     memory as the (MN-major) B operand of the second MMA, and keep per-row
+//     denominators that one butterfly reduction per piece hands over.
 //   * O^T = V^T P^T on the tensor core: M = 128 (kv head, dim) rows read from
 //     the SAME swizzled V tile as an MN-major operand, N = query columns,
-//     K = 128 tokens. Fresh TMEM accumulator per tile; the softmax warps fold
-//     it into fp32 registers with the online-softmax rescale.
+//     K = 128 tokens. Fresh TMEM accumulator per tile (double-buffered).
+//   * Correction warps (128 threads, one (kv head, dim) row each) fold every
+//     tile's O into fp32 registers with the rescale factors the softmax warps
+//     record per tile, then normalise and store, publish a partial, or
+//     combine partials — off the softmax warps' path, so a piece boundary does
+//     not stall S -> P.
 //   * Work split (stream-K): the (sequence, head group) segments are laid end
 //     to end as one sequence of 128-token tiles; CTA b takes tiles
-//     [b*T/grid, (b+1)*T/grid). A segment cut by a CTA boundary is finished by
-//     the last of its CTAs to arrive (arrival counter), which folds the <= 2
-//     partial results each CTA leaves — no second launch, equal work per SM.
-//   * Warp roles: warp 0 K-tile TMA producer (also stages Q), warp 6 V-tile
-//     TMA producer, warp 1 MMA issuer and TMEM owner, warps 2-5 softmax /
-//     correction / epilogue. K and V have separate smem rings: a K tile is
-//     freed once the S MMA has read it, so K prefetch runs deeper than V.
+//     [b*T/grid, (b+1)*T/grid). A segment cut by CTA boundaries is combined by
+//     the CTA holding its first tile, at the end of its range; the other
+//     pieces are the first pieces of the following CTAs, published early
+//     (partial + release flag) — no second launch, equal tiles per SM.
+//   * Warp roles (12 warps): 0 K-tile TMA producer (also copies each piece's
+//     Q), 6 V-tile TMA producer, 1 S-MMA issuer (TMEM owner), 11 O-MMA issuer,
+//     2-5 softmax, 7-10 correction / epilogue. Each tcgen05.mma costs its
+//     issuing thread tens of nanoseconds, so S and O are issued from two
+//     warps. K and V have separate smem rings: a K tile is freed once the S
+//     MMA has read it, so K prefetch runs deeper than V. Block-table entries
+//     and Q are copied ahead with cp.async, so no TMA issue waits on L2.
 //   * Every mbarrier wait is bounded (2 s): on timeout the kernel sets
 //     PAGEDKV_EFLAG_PIPE_TIMEOUT, unwinds every role, drains its own TMA loads
 //     and MMAs, frees TMEM and returns.
@@ -59,7 +69,10 @@ namespace {
 constexpr int kTile = 128;                     // tokens per tile (MMA M of S^T)
 constexpr int kHalfBytes = kTile * 128;        // one 64-element half of a tile: 16 KB
 constexpr int kOperandBytes = 2 * kHalfBytes;  // [128 x 128] K or V tile: 32 KB
-constexpr int kThreads = 224;                  // 7 warps
+constexpr int kThreads = 384;                  // 12 warps
+constexpr int kRescaleSlots = 4;               // softmax -> correction records in flight
+constexpr int kQSlots = 4;                     // staged Q operands (pieces) in flight
+constexpr int kLSlots = 8;                     // per-piece denominator partials in flight
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr float kRescaleLog2 = 8.f;            // lazy-rescale threshold (log2 units)
 
@@ -68,7 +81,7 @@ constexpr float kRescaleLog2 = 8.f;            // lazy-rescale threshold (log2 u
 #ifdef PAGEDKV_TRACE
 constexpr int kTraceSlots = 16;
 constexpr int kTraceCtas = 160;
-__device__ unsigned long long g_trace[kTraceCtas][4][kTraceSlots];
+__device__ unsigned long long g_trace[kTraceCtas][7][kTraceSlots];
 #define PKV_TW(slot, expr)             \
   ([&]() {                              \
     const uint64_t _t0 = clock64();     \
@@ -126,24 +139,39 @@ struct Piece {
 };
 
 // Walks this CTA's tile range segment by segment. Every role runs its own copy
-// and sees the same pieces in the same order.
+// and sees the same pieces in the same order. Sequence lengths are loaded one
+// sequence ahead, so moving to the next sequence does not wait on memory.
 struct Walker {
   int64_t cur, hi;
   int seq, hg, off;
   bool started;
+  int len_cur, len_nxt;  // clamped lengths of seq and seq + 1
+
+  __device__ void prime(const TcParams &tp) {
+    const DecodeParams &p = tp.p;
+    len_cur = seq < p.num_seqs ? seq_len_clamped(p, seq) : 0;
+    len_nxt = seq + 1 < p.num_seqs ? seq_len_clamped(p, seq + 1) : 0;
+  }
+
+  __device__ void advance_seq(const TcParams &tp) {
+    const DecodeParams &p = tp.p;
+    ++seq;
+    hg = 0;
+    off = 0;
+    len_cur = len_nxt;
+    len_nxt = seq + 1 < p.num_seqs ? seq_len_clamped(p, seq + 1) : 0;
+  }
 
   __device__ bool next(const TcParams &tp, Piece &pc) {
     const DecodeParams &p = tp.p;
     if (cur >= hi || seq >= p.num_seqs) return false;
-    int len = seq_len_clamped(p, seq);
-    int nt = tiles_of(len);
+    int nt = tiles_of(len_cur);
     while (nt == 0) {  // zero-length sequences own no tiles
-      if (++seq >= p.num_seqs) return false;
-      hg = 0;
-      off = 0;
-      len = seq_len_clamped(p, seq);
-      nt = tiles_of(len);
+      advance_seq(tp);
+      if (seq >= p.num_seqs) return false;
+      nt = tiles_of(len_cur);
     }
+    const int len = len_cur;
     const int64_t avail = hi - cur;
     const int take = (int)((int64_t)(nt - off) < avail ? (int64_t)(nt - off) : avail);
     pc.seq = seq;
@@ -160,10 +188,7 @@ struct Walker {
     off += take;
     if (off == nt) {
       off = 0;
-      if (++hg == tp.head_groups) {
-        hg = 0;
-        ++seq;
-      }
+      if (++hg == tp.head_groups) advance_seq(tp);
     }
     return true;
   }
@@ -173,26 +198,41 @@ template <int N, int SK, int SV>
 struct SmemLayout {
   static constexpr int kQBytes = 2 * N * 128;  // B operand [N x 128], two K-halves
   static constexpr int kPBytes = N * 256;      // B operand P^T, MN-major SW32: N/16 atoms x 4 KB
+  static constexpr int kSlotBytes = 8 * N + 16;  // per-tile rescale record, see RescaleSlot
   static constexpr int kOffK = 0;                               // K ring: SK tiles
   static constexpr int kOffV = kOffK + SK * kOperandBytes;      // V ring: SV tiles
-  static constexpr int kOffQ = kOffV + SV * kOperandBytes;
-  static constexpr int kOffP = kOffQ + 2 * kQBytes;
+  static constexpr int kOffQ = kOffV + SV * kOperandBytes;      // Q ring: kQSlots operands
+  static constexpr int kOffP = kOffQ + kQSlots * kQBytes;
   static constexpr int kOffRedMax = kOffP + 2 * kPBytes;        // float [2][4][N]; prologue scratch
-  static constexpr int kOffRedL = kOffRedMax + 2 * 4 * N * 4;   // float [4][N]
-  static constexpr int kOffBars = kOffRedL + 4 * N * 4;         // uint64 barriers
+  static constexpr int kOffSlots = kOffRedMax + 2 * 4 * N * 4;  // kRescaleSlots records
+  static constexpr int kOffL = kOffSlots + kRescaleSlots * kSlotBytes;  // float [kLSlots][4][N]
+  static constexpr int kOffBtWin = kOffL + kLSlots * 4 * N * 4;  // int32 [2 producers][3][32]
+  static constexpr int kOffBars = kOffBtWin + 2 * 3 * 32 * 4;        // uint64 barriers
   // kfull, kempty [SK]; vfull, vempty [SV]; s_full, s_empty, p_full, p_empty,
-  // o_full, o_empty, q_full, q_empty [2]; mma_done [1]
-  static constexpr int kNumBars = 2 * SK + 2 * SV + 8 * 2 + 1;
+  // o_full, o_empty [2]; mma_done [1]; a_full [kRescaleSlots]; q_full, q_empty
+  // [kQSlots]; l_full [kLSlots]
+  static constexpr int kNumBars = 2 * SK + 2 * SV + 6 * 2 + 1 + kRescaleSlots + 2 * kQSlots + kLSlots;
   static constexpr int kOffMisc = kOffBars + kNumBars * 8;  // see MiscSmem
   static constexpr int kBytes = kOffMisc + 80;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
-  static_assert(2 * 4 * N * 4 >= 8 * 8, "prologue scan scratch fits the max-reduction buffer");
+  static_assert(2 * 4 * N * 4 >= 8 * (kThreads / 32), "prologue scan scratch fits the max-reduction buffer");
+  static_assert(kOffSlots % 16 == 0 && kSlotBytes % 16 == 0 && kOffL % 16 == 0 && kOffBars % 8 == 0, "alignment");
+};
+
+// Per-tile record the softmax warps hand to the correction warps: whether the
+// tile moved the reference max, and if so the factors and the new max.
+template <int N>
+struct RescaleSlot {
+  float alpha[N];  // exp2(old max - new max) per query column
+  float m[N];      // new reference max (log2 units) per query column
+  uint32_t resc;
+  uint32_t pad[3];
 };
 
 struct MiscSmem {
   uint32_t tmem;
   int abort;
-  int combine[2];
+  int pad0[2];
   int seq0, hg0, off0, pad;
   long long lo, hi, total, grid;
 };
@@ -203,12 +243,14 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
                  const __grid_constant__ CUtensorMap tmap_v, const TcParams tp) {
   using L = SmemLayout<N, SK, SV>;
   using E = Elem<T>;
-  constexpr int D = 128 / H;         // head_dim
-  constexpr uint32_t kCols = 4 * N;  // TMEM: S[2] then O[2]
+  using Slot = RescaleSlot<N>;
+  constexpr int D = 128 / H;                          // head_dim
+  constexpr uint32_t kCols = 4 * N;                  // TMEM: S[2] then O[2]
   constexpr uint32_t kFmt = E::kDtype == PAGEDKV_DTYPE_BF16 ? 1u : 0u;
   constexpr uint32_t kIdescS = idesc_f16(kFmt, N, false, false);
   constexpr uint32_t kIdescO = idesc_f16(kFmt, N, true, true);
   static_assert(H * GP <= N && N % 16 == 0 && N <= 32, "column layout");
+  static_assert(sizeof(Slot) == L::kSlotBytes, "slot size");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -221,12 +263,20 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
   auto vfull = [&](int s) { return bars + 8u * (2 * SK + s); };
   auto vempty = [&](int s) { return bars + 8u * (2 * SK + SV + s); };
   auto bar2 = [&](int which, int b) { return bars + 8u * (2 * SK + 2 * SV + 2 * which + b); };
-  // which: 0 s_full, 1 s_empty, 2 p_full, 3 p_empty, 4 o_full, 5 o_empty, 6 q_full, 7 q_empty
-  const uint32_t mma_done = bars + 8u * (2 * SK + 2 * SV + 16);
+  // which: 0 s_full, 1 s_empty, 2 p_full, 3 p_empty, 4 o_full, 5 o_empty
+  constexpr int kBarTail = 2 * SK + 2 * SV + 12;
+  const uint32_t mma_done = bars + 8u * kBarTail;
+  auto a_full = [&](int s) { return bars + 8u * (kBarTail + 1 + s); };
+  auto q_full = [&](uint32_t i) { return bars + 8u * (kBarTail + 1 + kRescaleSlots + i % kQSlots); };
+  auto q_empty = [&](uint32_t i) { return bars + 8u * (kBarTail + 1 + kRescaleSlots + kQSlots + i % kQSlots); };
+  auto l_full = [&](uint32_t i) { return bars + 8u * (kBarTail + 1 + kRescaleSlots + 2 * kQSlots + i % kLSlots); };
+  // Phase parity of the (i / ring)-th use of ring slot i % ring.
+  auto ring_parity = [](uint32_t i, uint32_t ring) { return (i / ring) & 1u; };
   MiscSmem *misc = reinterpret_cast<MiscSmem *>(smem + L::kOffMisc);
   volatile int *abort_flag = &misc->abort;
   float *red_max = reinterpret_cast<float *>(smem + L::kOffRedMax);
-  float *red_l = reinterpret_cast<float *>(smem + L::kOffRedL);
+  Slot *slots = reinterpret_cast<Slot *>(smem + L::kOffSlots);
+  float *lpart = reinterpret_cast<float *>(smem + L::kOffL);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -249,16 +299,19 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar2(0, b), 1);    // s_full: MMA commit
       mbar_init(bar2(1, b), 128);  // s_empty: every softmax thread
-      mbar_init(bar2(2, b), 128);  // p_full
+      mbar_init(bar2(2, b), 128);  // p_full: every softmax thread
       mbar_init(bar2(3, b), 1);    // p_empty: MMA commit
       mbar_init(bar2(4, b), 1);    // o_full: MMA commit
-      mbar_init(bar2(5, b), 128);  // o_empty
-      mbar_init(bar2(6, b), 32);   // q_full: every producer lane
-      mbar_init(bar2(7, b), 1);    // q_empty: MMA commit
+      mbar_init(bar2(5, b), 128);  // o_empty: every correction thread
     }
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, 2);  // one commit from each MMA issuer
+    for (int s = 0; s < kRescaleSlots; ++s) mbar_init(a_full(s), 1);  // one softmax thread
+    for (int s = 0; s < kQSlots; ++s) {
+      mbar_init(q_full(s), 32);  // every K-producer lane, when its Q copies land
+      mbar_init(q_empty(s), 1);  // MMA commit after the piece's last S
+    }
+    for (int s = 0; s < kLSlots; ++s) mbar_init(l_full(s), 4);  // lane 0 of each softmax warp
     misc->abort = 0;
-    misc->combine[0] = misc->combine[1] = 0;
     fence_mbarrier_init();
   }
   if (warp == 1) {
@@ -273,7 +326,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 
   // ---- prologue: total tile count and the start of this CTA's range ----------
   {
-    long long *scan = reinterpret_cast<long long *>(smem + L::kOffRedMax);  // [6] warp sums
+    long long *scan = reinterpret_cast<long long *>(smem + L::kOffRedMax);  // [warps] sums
     const int ns = p.num_seqs;
     const int per = (ns + kThreads - 1) / kThreads;
     const int s_begin = min(ns, (int)threadIdx.x * per);
@@ -334,38 +387,65 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
   const uint32_t tmem = misc->tmem;
   const int64_t T_total = misc->total;
   const int64_t G = misc->grid;
-  Walker walk{misc->lo, misc->hi, misc->seq0, misc->hg0, misc->off0, false};
+  Walker walk{misc->lo, misc->hi, misc->seq0, misc->hg0, misc->off0, false, 0, 0};
+  walk.prime(tp);
 
   if (warp == 0 || warp == 6) {
     // ------------------------------------------------ producers: warp 0 K (+ Q), warp 6 V
-    // Global loads the TMA issue depends on are issued one tile ahead: the
-    // block-table entries of the next tile (also across a piece boundary) and
-    // the next piece's Q rows (K producer), so a stage freed by the consumer is
-    // refilled without a dependent round trip to L2.
+    // The global loads a TMA issue depends on run ahead of it: block-table
+    // entries are staged in windows of 32 consecutive blocks, two windows
+    // ahead (also across piece boundaries), by cp.async into shared memory,
+    // and the K producer copies the next piece's Q rows into the Q ring one
+    // piece ahead (cp.async, completing on the slot's q_full barrier). A
+    // stage freed by the consumer is refilled without a round trip to L2.
     const bool is_k = warp == 0;
     const CUtensorMap *tmap = is_k ? &tmap_k : &tmap_v;
     const int nst = is_k ? SK : SV;
     const uint32_t ring = sbase + (is_k ? L::kOffK : L::kOffV);
     if (lane == 0) tma_prefetch_desc(tmap);
     const uint64_t policy = l2_policy_evict_first();
-    const int blocks_per_tile = kTile / p.block_size;  // <= 16 lanes
-    constexpr int kQChunks = 16 * N / 32;               // Q 16-byte chunks per lane
+    const int bpt = kTile / p.block_size;  // blocks per tile: 1..16, divides 32
+    constexpr int kQChunks = 16 * N / 32;  // Q 16-byte chunks per lane
     int stage = 0;
     uint32_t sphase = 0;
     uint32_t qi = 0;
     int issued = 0;
     bool ok = true;
 
-    // Block-table entry this lane needs for tile j of piece q, or kNoBlock
-    // when the lane's block lies past the piece (fetched as zeros).
-    constexpr int64_t kNoBlock = -(1ll << 40);
-    auto bt_entry = [&](const Piece &q, int j) -> int64_t {
-      const int lb = (q.t0 + j * kTile) / p.block_size + lane;
-      const int need = (q.t1 + p.block_size - 1) / p.block_size;
-      if (lane >= blocks_per_tile || lb >= need) return kNoBlock;
-      return (int64_t)__ldg(p.bt + (int64_t)q.seq * p.bt_s + lb);
+    // Window k (k = 0, 1, ... over this CTA's pieces in order; window w of a
+    // piece q covers its logical blocks q.t0 / block_size + 32 w + [0, 32))
+    // lands in slot k % 3; lanes past the piece's last block copy nothing.
+    const uint32_t win_base = sbase + L::kOffBtWin + (is_k ? 0u : 3u * 32u * 4u);
+    const int32_t *win = reinterpret_cast<const int32_t *>(smem + L::kOffBtWin) + (is_k ? 0 : 3 * 32);
+    Walker gwalk = walk;  // generator of the window sequence
+    Piece gp;
+    bool gvalid = gwalk.next(tp, gp);
+    int gw = 0;
+    uint32_t gk = 0;  // windows issued
+    auto issue_window = [&]() {
+      if (gvalid) {
+        const int lb = gp.t0 / p.block_size + 32 * gw + lane;
+        const int need = (gp.t1 + p.block_size - 1) / p.block_size;
+        const bool in = lb < need;
+        const int32_t *src = in ? p.bt + (int64_t)gp.seq * p.bt_s + lb : p.bt;
+        cp_async_4(win_base + ((gk % 3u) * 32u + lane) * 4u, src, in ? 4u : 0u);
+        if (++gw == (gp.ntiles * bpt + 31) / 32) {
+          gw = 0;
+          gvalid = gwalk.next(tp, gp);
+        }
+      }
+      cp_async_commit();  // possibly empty: one group per window slot, always
+      ++gk;
     };
-    auto q_load = [&](const Piece &q, uint4 (&qr)[kQChunks]) {
+    issue_window();
+    issue_window();
+    uint32_t wk = 0;  // windows consumed
+
+    // Q of piece q into ring slot i as the block-diagonal B operand
+    // [N rows x 128], K-major SW128; padding rows and halves are zero-filled.
+    auto q_issue = [&](const Piece &q, uint32_t i) -> bool {
+      if (!PKV_TW(0, mbar_wait(q_empty(i), ring_parity(i, kQSlots) ^ 1u, abort_flag, kTimeoutNs))) return false;
+      const uint32_t qbuf = sbase + L::kOffQ + (i % kQSlots) * L::kQBytes;
 #pragma unroll
       for (int c = 0; c < kQChunks; ++c) {
         const int idx = lane + c * 32;
@@ -374,30 +454,39 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         const int n = rem >> 3, ch = rem & 7;
         const int hl = n / GP, g = n - hl * GP;
         const int kv = q.hg * H + hl;
-        qr[c] = make_uint4(0u, 0u, 0u, 0u);
-        if (hl < H && g < p.group && kv < p.hkv && (H == 1 || xh == hl)) {
-          const int d = (H == 1 ? xh * 64 : 0) + ch * 8;
-          qr[c] = ldg16(reinterpret_cast<const T *>(p.q) + (int64_t)q.seq * p.q_ss +
-                        (int64_t)(kv * p.group + g) * p.q_sh + d);
-        }
+        const bool in = hl < H && g < p.group && kv < p.hkv && (H == 1 || xh == hl);
+        const int d = (H == 1 ? xh * 64 : 0) + ch * 8;
+        const T *src = reinterpret_cast<const T *>(p.q) +
+                       (in ? (int64_t)q.seq * p.q_ss + (int64_t)(kv * p.group + g) * p.q_sh + d : 0);
+        const uint32_t addr = qbuf + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
+        cp_async_16(addr, src, in ? 16u : 0u);
       }
+      cp_async_mbar_arrive(q_full(i));
+      return true;
     };
 
     Piece pc;
     bool have = walk.next(tp, pc);
-    Walker peek = walk;  // walker positioned after pc: peek.next() yields the piece after it
-    int64_t bt_next = have ? bt_entry(pc, 0) : kNoBlock;
-    uint4 qr[kQChunks];
-    if (have && is_k) q_load(pc, qr);
+    if (have && is_k) ok = q_issue(pc, qi++);
     while (ok && have) {
       Piece nx;
-      Walker after = peek;
-      const bool have_nx = after.next(tp, nx);
+      const bool have_nx = walk.next(tp, nx);
+      // The next piece's Q, landing while this piece's tiles stream.
+      if (is_k && have_nx && !q_issue(nx, qi++)) break;
+      const int lb0 = pc.t0 / p.block_size;
+      const int need = (pc.t1 + p.block_size - 1) / p.block_size;
       for (int j = 0; j < pc.ntiles; ++j) {
-        const int64_t blk = bt_next;
-        // Prefetch the entries of the tile after this one.
-        if (j + 1 < pc.ntiles) bt_next = bt_entry(pc, j + 1);
-        else bt_next = have_nx ? bt_entry(nx, 0) : kNoBlock;
+        const int wofs = (j * bpt) & 31;
+        if (wofs == 0) {
+          // Entering a window: stage the one two ahead (into the slot of the
+          // window just finished), then wait for this one.
+          __syncwarp();
+          issue_window();
+          cp_async_wait<2>();
+          __syncwarp();
+        }
+        const uint32_t slot = wk % 3u;
+        if (wofs + bpt >= 32 || j + 1 == pc.ntiles) ++wk;  // last tile of this window
         if (!PKV_TW(1, mbar_wait(is_k ? kempty(stage) : vempty(stage), sphase ^ 1u, abort_flag, kTimeoutNs))) {
           ok = false;
           break;
@@ -405,54 +494,33 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         const uint32_t full = is_k ? kfull(stage) : vfull(stage);
         if (lane == 0) mbar_arrive_expect_tx(full, kOperandBytes);
         __syncwarp();
-        const uint32_t dst = ring + stage * kOperandBytes;
-        const int x0 = pc.hg * 128;
-        if (lane < blocks_per_tile) {
+        if (lane < 2 * bpt) {
+          // lane -> (block b of the tile, 64-element half h)
+          const int h = lane >= bpt ? 1 : 0;
+          const int b = lane - h * bpt;
+          const int lb = lb0 + j * bpt + b;
           int32_t y = tp.oob_row;  // out of range: TMA fills zeros, reads nothing
-          if (blk >= 0 && blk < p.num_blocks) {
-            y = (int32_t)blk * p.block_size;
-          } else if (blk != kNoBlock && is_k) {
-            set_error(p.err, PAGEDKV_EFLAG_BLOCK_ID_RANGE);
+          if (lb < need) {
+            const int32_t blk = win[slot * 32 + wofs + b];
+            if (blk >= 0 && blk < p.num_blocks) {
+              y = blk * p.block_size;
+            } else if (is_k && h == 0) {
+              set_error(p.err, PAGEDKV_EFLAG_BLOCK_ID_RANGE);
+            }
           }
-          const uint32_t off = lane * p.block_size * 128;
-          tma_load_2d(dst + off, tmap, x0, y, full, policy);
-          tma_load_2d(dst + kHalfBytes + off, tmap, x0 + 64, y, full, policy);
+          const uint32_t dst = ring + stage * kOperandBytes + h * kHalfBytes + b * p.block_size * 128;
+          tma_load_2d(dst, tmap, pc.hg * 128 + h * 64, y, full, policy);
         }
         ++issued;
         if (++stage == nst) {
           stage = 0;
           sphase ^= 1u;
         }
-        if (is_k && j == 0) {
-          // Stage Q (loaded into registers one piece ahead) as the
-          // block-diagonal B operand [N rows x 128], K-major SW128.
-          const uint32_t qb = qi & 1u;
-          if (!PKV_TW(0, mbar_wait(bar2(7, qb), ((qi >> 1) & 1u) ^ 1u, abort_flag, kTimeoutNs))) {
-            ok = false;
-            break;
-          }
-          const uint32_t qbuf = sbase + L::kOffQ + qb * L::kQBytes;
-#pragma unroll
-          for (int c = 0; c < kQChunks; ++c) {
-            const int idx = lane + c * 32;
-            const int xh = idx / (8 * N);
-            const int rem = idx - xh * 8 * N;
-            const int n = rem >> 3, ch = rem & 7;
-            const uint32_t addr = qbuf + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
-            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(qr[c].x), "r"(qr[c].y),
-                         "r"(qr[c].z), "r"(qr[c].w)
-                         : "memory");
-          }
-          fence_proxy_async_smem();
-          mbar_arrive(bar2(6, qb));
-          ++qi;
-          if (have_nx) q_load(nx, qr);  // next piece's Q, in flight while its tiles wait
-        }
       }
       pc = nx;
       have = have_nx;
-      peek = after;
     }
+    cp_async_wait<0>();  // no copy into shared memory outlives this role
     // Drain: the last min(issued, ring size) tiles' loads must have landed
     // before this CTA's shared memory is released (immediate on the normal path).
     for (int k = 0; k < nst && k < issued; ++k) {
@@ -464,49 +532,69 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       mbar_wait(is_k ? kfull(stage) : vfull(stage), sphase, &never, kTimeoutNs / 4);
     }
   } else if (warp == 1) {
-    // --------------------------------------------------------------- MMA issuer
-    int kst = 0, vst = 0;  // K / V ring positions of the current tile
-    uint32_t kph = 0, vph = 0;
-    uint32_t gt = 0;  // global tile counter (S/P/O double buffers)
-    uint32_t qi = 0;
+    // ------------------------------------------------------------------ S issuer
+    // S^T = K Q^T per tile into the S double buffer, as far ahead as the
+    // softmax warps' reads of S allow. (The S and O MMAs are issued by two
+    // warps: each tcgen05.mma costs its issuing thread tens of nanoseconds.)
+    int kst = 0;
+    uint32_t kph = 0, gt = 0, qi = 0;
     bool ok = true;
-    auto issue_s = [&](int st, uint32_t ph, uint32_t g, uint32_t qbuf) -> bool {
-      const uint32_t b = g & 1u;
-      if (!PKV_TW(1, mbar_wait(kfull(st), ph, abort_flag, kTimeoutNs))) return false;
-      if (!PKV_TW(2, mbar_wait(bar2(1, b), ((g >> 1) & 1u) ^ 1u, abort_flag, kTimeoutNs))) return false;
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t ka = sbase + L::kOffK + st * kOperandBytes;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = smem_desc_sw128(ka + (kk >> 2) * kHalfBytes + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(qbuf + (kk >> 2) * (N * 128) + (kk & 3) * 32, 16, 1024);
-          mma_f16_ss(tmem + b * N, ad, bd, kIdescS, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(bar2(0, b));  // s_full
-        mma_commit(kempty(st));  // K tile read: free it for the next load
-      }
-      __syncwarp();
-      return true;
-    };
     Piece pc;
-    while (ok && walk.next(tp, pc)) {
-      const uint32_t qb = qi & 1u;
-      if (!PKV_TW(0, mbar_wait(bar2(6, qb), (qi >> 1) & 1u, abort_flag, kTimeoutNs))) { ok = false; break; }
-      const uint32_t qbuf = sbase + L::kOffQ + qb * L::kQBytes;
-      if (!issue_s(kst, kph, gt, qbuf)) { ok = false; break; }
+    bool have = walk.next(tp, pc);
+    while (ok && have) {
+      Piece nx;
+      const bool have_nx = walk.next(tp, nx);
+      if (!PKV_TW(0, mbar_wait(q_full(qi), ring_parity(qi, kQSlots), abort_flag, kTimeoutNs))) break;
+      fence_proxy_async_smem();  // Q landed through cp.async (generic proxy); the MMA reads it
+      const uint32_t qbuf = sbase + L::kOffQ + (qi % kQSlots) * L::kQBytes;
+      for (int j = 0; j < pc.ntiles; ++j) {
+        const uint32_t b = gt & 1u;
+        if (!PKV_TW(1, mbar_wait(kfull(kst), kph, abort_flag, kTimeoutNs))) { ok = false; break; }
+        if (!PKV_TW(2, mbar_wait(bar2(1, b), ((gt >> 1) & 1u) ^ 1u, abort_flag, kTimeoutNs))) { ok = false; break; }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t ka = sbase + L::kOffK + kst * kOperandBytes;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t ad = smem_desc_sw128(ka + (kk >> 2) * kHalfBytes + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(qbuf + (kk >> 2) * (N * 128) + (kk & 3) * 32, 16, 1024);
+            mma_f16_ss(tmem + b * N, ad, bd, kIdescS, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(bar2(0, b));   // s_full
+          mma_commit(kempty(kst));  // K tile read: free it for the next load
+          if (j + 1 == pc.ntiles) mma_commit(q_empty(qi));  // piece's last S: Q read
+        }
+        __syncwarp();
+        ++gt;
+        if (++kst == SK) {
+          kst = 0;
+          kph ^= 1u;
+        }
+      }
+      ++qi;
+      pc = nx;
+      have = have_nx;
+    }
+    // Every MMA this thread issued has completed before TMEM is released.
+    if (lane == 0) mma_commit(mma_done);
+    __syncwarp();
+    volatile int never = 0;
+    mbar_wait(mma_done, 0, &never, kTimeoutNs / 4);
+  } else if (warp == 11) {
+    // ------------------------------------------------------------------ O issuer
+    // O^T = V^T P^T per tile into the O double buffer once the softmax warps
+    // have written P and the correction warps have drained the buffer.
+    int vst = 0;
+    uint32_t vph = 0, gt = 0;
+    bool ok = true;
+    Piece pc;
+    bool have = walk.next(tp, pc);
+    while (ok && have) {
+      Piece nx;
+      const bool have_nx = walk.next(tp, nx);
       for (int j = 0; j < pc.ntiles; ++j) {
         const uint32_t b = gt & 1u;
         const uint32_t bph = (gt >> 1) & 1u;
-        int nkst = kst + 1;
-        uint32_t nkph = kph;
-        if (nkst == SK) {
-          nkst = 0;
-          nkph ^= 1u;
-        }
-        if (j + 1 < pc.ntiles) {
-          if (!issue_s(nkst, nkph, gt + 1, qbuf)) { ok = false; break; }
-        }
         if (!PKV_TW(3, mbar_wait(vfull(vst), vph, abort_flag, kTimeoutNs))) { ok = false; break; }
         const uint32_t va = sbase + L::kOffV + vst * kOperandBytes;
         // Rows of the last block past the sequence end hold stale pool data:
@@ -538,104 +626,50 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
             const uint64_t bd = smem_desc(pbuf + kk * 512, 4096, 256, kLayoutSwizzle32);
             mma_f16_ss(tmem + 2 * N + b * N, ad, bd, kIdescO, kk > 0 ? 1u : 0u);
           }
-          mma_commit(bar2(4, b));  // o_full
+          mma_commit(bar2(4, b));   // o_full
           mma_commit(vempty(vst));  // V tile read
-          mma_commit(bar2(3, b));  // p_empty
-          if (j == pc.ntiles - 1) mma_commit(bar2(7, qb));  // q_empty
+          mma_commit(bar2(3, b));   // p_empty
         }
         __syncwarp();
         ++gt;
-        kst = nkst;
-        kph = nkph;
         if (++vst == SV) {
           vst = 0;
           vph ^= 1u;
         }
       }
-      ++qi;
+      pc = nx;
+      have = have_nx;
     }
-    // Every MMA this thread issued has completed before TMEM is released.
     if (lane == 0) mma_commit(mma_done);
     __syncwarp();
     volatile int never = 0;
     mbar_wait(mma_done, 0, &never, kTimeoutNs / 4);
-  } else {
-    // ------------------------------------------------- softmax / correction / epilogue
+  } else if (warp <= 5) {
+    // ----------------------------------------------------------- softmax: S -> P
     const int q4 = warp & 3;         // TMEM lane quarter of this warp
-    const int row = q4 * 32 + lane;  // TMEM lane: token row (S) / (kv head, dim) row (O)
-    const int hl = H == 2 ? (row >> 6) : 0;
-    const int dim = H == 2 ? (row & 63) : row;
+    const int row = q4 * 32 + lane;  // TMEM lane: token row of S
     const uint32_t tl = tmem + ((uint32_t)(q4 * 32) << 16);
-    const int HQS = H * p.group;  // query heads per segment
-    uint32_t gt = 0;
+    uint32_t gt = 0, pi = 0;
     int red_buf = 0;
-
-    // Sequences of length 0 own no tiles: CTA (seq % grid) writes their zeros.
-    for (int s = blockIdx.x; s < p.num_seqs; s += gridDim.x) {
-      const int raw = p.lens ? __ldg(p.lens + s) : p.uniform_len;
-      if (raw > p.max_blocks * p.block_size && row == 0) set_error(p.err, PAGEDKV_EFLAG_SEQ_LEN_RANGE);
-      if (seq_len_clamped(p, s) == 0) {
-        T *out = reinterpret_cast<T *>(p.out) + (int64_t)s * p.o_ss;
-        for (int idx = row; idx < p.hq * D; idx += 128)
-          out[(int64_t)(idx / D) * p.o_sh + idx % D] = E::from_float(0.f);
-      }
-    }
-
+    // On a timed-out wait the pipeline is abandoned but the control flow of
+    // these 128 threads stays uniform (they share named barriers): later waits
+    // return at once and the results are garbage, flagged by PIPE_TIMEOUT.
     Piece pc;
-#ifdef PAGEDKV_TRACE
-    uint64_t t_piece_end = clock64();
-#endif
-    while (walk.next(tp, pc)) {
-      float m_ref[N], l_part[N], alpha_prev[N], acc[GP];
+    bool have = walk.next(tp, pc);
+    while (have) {
+      Piece nx;
+      const bool have_nx = walk.next(tp, nx);  // its length load overlaps this piece
+      float m_ref[N], l_part[N];
 #pragma unroll
       for (int n = 0; n < N; ++n) {
         m_ref[n] = kNegInf;
         l_part[n] = 0.f;
-        alpha_prev[n] = 1.f;
       }
-#pragma unroll
-      for (int g = 0; g < GP; ++g) acc[g] = 0.f;
-      bool resc_prev = false;
-
-      // Fold tile g_tile's O into the fp32 accumulators (rescaled first when
-      // that tile moved the reference max). On a timed-out wait the pipeline
-      // is abandoned but the control flow of these 128 threads stays uniform
-      // (they share named barriers): later waits return at once and the
-      // results are garbage, flagged by the PIPE_TIMEOUT bit.
-      auto correction = [&](uint32_t g_tile, bool resc) {
-        const uint32_t b = g_tile & 1u;
-        PKV_TW(3, mbar_wait(bar2(4, b), (g_tile >> 1) & 1u, abort_flag, kTimeoutNs));
-        tc_fence_after();
-        float o[GP];
-        tmem_ld<GP>(tl + 2 * N + b * N + hl * GP, o);
-        tmem_ld_wait();
-        tc_fence_before();
-        mbar_arrive(bar2(5, b));
-        if (resc) {
-#pragma unroll
-          for (int g = 0; g < GP; ++g) {
-            const float a = (H == 2 && hl == 1) ? alpha_prev[(GP + g) % N] : alpha_prev[g];
-            acc[g] = fmaf(acc[g], a, o[g]);
-          }
-        } else {
-#pragma unroll
-          for (int g = 0; g < GP; ++g) acc[g] += o[g];
-        }
-      };
-
       for (int j = 0; j < pc.ntiles; ++j) {
         const uint32_t b = gt & 1u;
         const uint32_t bph = (gt >> 1) & 1u;
-#ifdef PAGEDKV_TRACE
-        if (j == 0) tw[11] += clock64() - t_piece_end;
-        const uint64_t t_sw0 = clock64();
-#endif
         PKV_TW(0, mbar_wait(bar2(0, b), bph, abort_flag, kTimeoutNs));
         PKV_TADD(5, 1);
-#ifdef PAGEDKV_TRACE
-        if (j == 0) tw[14] += clock64() - t_sw0;
-        const uint64_t t_sm0 = clock64();
-#endif
         tc_fence_after();
         float s[N];
         tmem_ld<N>(tl + b * N, s);
@@ -690,9 +724,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         }
 #pragma unroll
         for (int n = 0; n < N; ++n) {
-          const float pr = valid ? fast_exp2(s[n] - m_ref[n]) : 0.f;
-          s[n] = pr;
-          l_part[n] += pr;
+          s[n] = valid ? fast_exp2(s[n] - m_ref[n]) : 0.f;
+          l_part[n] += s[n];
         }
         PKV_TW(2, mbar_wait(bar2(3, b), bph ^ 1u, abort_flag, kTimeoutNs));
         // P^T as the B operand [128 tokens x N], MN-major with 32-byte swizzle:
@@ -715,89 +748,159 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           }
         }
         fence_proxy_async_smem();
-        mbar_arrive(bar2(2, b));
-#ifdef PAGEDKV_TRACE
-        tw[13] += clock64() - t_sm0;
-#endif
-        if (j > 0) correction(gt - 1, resc_prev);
-        if (resc) {
+        if (row == 0) {
+          // This tile's rescale record for the correction warps. Slot gt % 4 is
+          // rewritten only after the correction warps released O of tile gt
+          // (o_empty -> O MMA of gt + 2 -> p_empty of gt + 4), and they read
+          // the record before that release.
+          Slot &sl = slots[gt % kRescaleSlots];
+          if (resc) {
 #pragma unroll
-          for (int n = 0; n < N; ++n) alpha_prev[n] = alpha[n];
+            for (int n = 0; n < N; n += 4) {
+              *reinterpret_cast<float4 *>(&sl.alpha[n]) = make_float4(alpha[n], alpha[n + 1], alpha[n + 2], alpha[n + 3]);
+              *reinterpret_cast<float4 *>(&sl.m[n]) = make_float4(m_ref[n], m_ref[n + 1], m_ref[n + 2], m_ref[n + 3]);
+            }
+          }
+          sl.resc = resc ? 1u : 0u;
+          mbar_arrive(a_full(gt % kRescaleSlots));
         }
-        resc_prev = resc;
+        mbar_arrive(bar2(2, b));
         ++gt;
       }
-#ifdef PAGEDKV_TRACE
-      const uint64_t t_cor0 = clock64();
-#endif
-      if (pc.ntiles > 0) correction(gt - 1, resc_prev);
-#ifdef PAGEDKV_TRACE
-      const uint64_t t_epi0 = clock64();
-      tw[12] += t_epi0 - t_cor0;
-      tw[6] += 1;
-#endif
-
-      // ---- per-piece epilogue: denominators across the 128 rows
+      // The piece's denominators: each warp sums its 32 token rows and hands
+      // the partial to the correction warps. Slot pi % kLSlots is rewritten
+      // kLSlots pieces later, after the correction warps have left this piece
+      // (the p_empty / o_empty chain, as for the rescale records).
+      {
+        // Butterfly reduce-scatter: each stage exchanges half of the columns
+        // still held with the partner lane (N - 1 shuffles in all instead of
+        // 5 N); lane l ends with column (l >> log2(32 / N)) summed over the
+        // lanes that share it, then over the rest.
+        static_assert(N == 16 || N == 32, "column count");
 #pragma unroll
-      for (int n = 0; n < N; ++n) {
-        float v = l_part[n];
+        for (int w = N / 2, bit = 16; w >= 1; w >>= 1, bit >>= 1) {
+          const bool up = (lane & bit) != 0;
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0) red_l[q4 * N + n] = v;
+          for (int i = 0; i < w; ++i) {
+            const float keep = up ? l_part[i + w] : l_part[i];
+            const float send = up ? l_part[i] : l_part[i + w];
+            l_part[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+          }
+        }
+        constexpr int kShare = 32 / N;  // lanes holding the same column
+        if (kShare == 2) l_part[0] += __shfl_xor_sync(0xffffffffu, l_part[0], 1);
+        if ((lane & (kShare - 1)) == 0) lpart[((pi % kLSlots) * 4 + q4) * N + lane / kShare] = l_part[0];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(l_full(pi));
       }
-      named_bar(1, 128);
-#ifdef PAGEDKV_TRACE
-      const uint64_t t_e1 = clock64();
-      tw[8] += t_e1 - t_epi0;
-#endif
-      float l_sel[GP], m_sel[GP];
+      ++pi;
+      pc = nx;
+      have = have_nx;
+    }
+  } else {
+    // ---------------------------------------- correction / epilogue: O -> output
+    const int q4 = warp & 3;         // TMEM lane quarter of this warp
+    const int row = q4 * 32 + lane;  // TMEM lane: (kv head, dim) row of O
+    const int hl = H == 2 ? (row >> 6) : 0;
+    const int dim = H == 2 ? (row & 63) : row;
+    const uint32_t tl = tmem + ((uint32_t)(q4 * 32) << 16);
+    const int HQS = H * p.group;  // query heads per segment
+    uint32_t gt = 0, pi = 0;
+
+    // Sequences of length 0 own no tiles: CTA (seq % grid) writes their zeros.
+    for (int s = blockIdx.x; s < p.num_seqs; s += gridDim.x) {
+      const int raw = p.lens ? __ldg(p.lens + s) : p.uniform_len;
+      if (raw > p.max_blocks * p.block_size && row == 0) set_error(p.err, PAGEDKV_EFLAG_SEQ_LEN_RANGE);
+      if (seq_len_clamped(p, s) == 0) {
+        T *out = reinterpret_cast<T *>(p.out) + (int64_t)s * p.o_ss;
+        for (int idx = row; idx < p.hq * D; idx += 128)
+          out[(int64_t)(idx / D) * p.o_sh + idx % D] = E::from_float(0.f);
+      }
+    }
+
+    Piece pc;
+    bool have = walk.next(tp, pc);
+    while (have) {
+      Piece nx;
+      const bool have_nx = walk.next(tp, nx);
+      float acc[GP], msel[GP];
 #pragma unroll
       for (int g = 0; g < GP; ++g) {
-        const int n0 = g, n1 = (GP + g) % N;
-        const float l0 = red_l[n0] + red_l[N + n0] + red_l[2 * N + n0] + red_l[3 * N + n0];
-        float l1 = 0.f;
-        if (H == 2) l1 = red_l[n1] + red_l[N + n1] + red_l[2 * N + n1] + red_l[3 * N + n1];
-        l_sel[g] = (H == 2 && hl == 1) ? l1 : l0;
-        m_sel[g] = (H == 2 && hl == 1) ? m_ref[n1] : m_ref[g];
+        acc[g] = 0.f;
+        msel[g] = kNegInf;
       }
-      named_bar(1, 128);  // red_l is rewritten by the next piece
+      for (int j = 0; j < pc.ntiles; ++j) {
+        const uint32_t b = gt & 1u;
+        const uint32_t si = gt % kRescaleSlots;
+        PKV_TW(0, mbar_wait(a_full(si), (gt / kRescaleSlots) & 1u, abort_flag, kTimeoutNs));
+        const Slot &sl = slots[si];
+        const bool resc = sl.resc != 0u;
+        float a[GP];
+        if (resc) {
+#pragma unroll
+          for (int g = 0; g < GP; ++g) {
+            a[g] = sl.alpha[(hl * GP + g) % N];
+            msel[g] = sl.m[(hl * GP + g) % N];
+          }
+        }
+        PKV_TW(1, mbar_wait(bar2(4, b), (gt >> 1) & 1u, abort_flag, kTimeoutNs));
+        tc_fence_after();
+        float o[GP];
+        tmem_ld<GP>(tl + 2 * N + b * N + hl * GP, o);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(bar2(5, b));
+        if (resc) {
+#pragma unroll
+          for (int g = 0; g < GP; ++g) acc[g] = fmaf(acc[g], a[g], o[g]);
+        } else {
+#pragma unroll
+          for (int g = 0; g < GP; ++g) acc[g] += o[g];
+        }
+        ++gt;
+      }
+      // Denominators of this thread's query columns: the four warp partials.
+      float lsum[GP];
+      PKV_TW(2, mbar_wait(l_full(pi), ring_parity(pi, kLSlots), abort_flag, kTimeoutNs));
+      {
+        const float *src = lpart + (pi % kLSlots) * 4 * N + hl * GP;
+#pragma unroll
+        for (int g = 0; g < GP; ++g) lsum[g] = (src[g] + src[N + g]) + (src[2 * N + g] + src[3 * N + g]);
+      }
+      ++pi;
 #ifdef PAGEDKV_TRACE
-      const uint64_t t_e2 = clock64();
-      tw[9] += t_e2 - t_e1;
+      const uint64_t t_epi0 = clock64();
+      tw[6] += 1;
 #endif
-
       const int kv = pc.hg * H + hl;
-      const bool have = kv < p.hkv;
+      const bool have_kv = kv < p.hkv;
       T *out = reinterpret_cast<T *>(p.out) + (int64_t)pc.seq * p.o_ss + dim;
       if (pc.ntiles == pc.seg_tiles) {
         // Whole segment in this CTA: normalise and store.
-        if (have) {
+        if (have_kv) {
 #pragma unroll
           for (int g = 0; g < GP; ++g) {
             if (g < p.group) {
-              const float v = l_sel[g] > 0.f ? acc[g] / l_sel[g] : 0.f;
+              const float v = lsum[g] > 0.f ? __fdividef(acc[g], lsum[g]) : 0.f;
               out[(int64_t)(kv * p.group + g) * p.o_sh] = E::from_float(v);
             }
           }
         }
-#ifdef PAGEDKV_TRACE
-        tw[10] += clock64() - t_e2;
-#endif
       } else if (pc.t0 > 0) {
         // Continuation of a segment that began in an earlier CTA: this is this
         // CTA's first piece. Publish it (partial + release flag) for the CTA
         // owning the segment's first tile, which combines at its end.
-        if (have) {
+        if (have_kv) {
 #pragma unroll
           for (int g = 0; g < GP; ++g) {
             if (g < p.group) {
               const int64_t hh = (int64_t)blockIdx.x * HQS + hl * p.group + g;
               tp.part_acc[hh * D + dim] = acc[g];
-              if (dim == 0) tp.part_ml[hh] = make_float2(m_sel[g], l_sel[g]);
+              if (dim == 0) tp.part_ml[hh] = make_float2(msel[g], lsum[g]);
             }
           }
         }
-        named_bar(1, 128);
+        named_bar(2, 128);
         if (row == 0) {
           __threadfence();  // release every thread's partial (cumulative over the barrier)
           st_volatile_u32(tp.flags + blockIdx.x, 1u);
@@ -807,9 +910,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         // CTA's range: this is this CTA's last piece, and this CTA combines.
         // The other pieces are the first pieces of CTAs b+1..b1, published
         // early in their runs.
-#ifdef PAGEDKV_TRACE
-        const uint64_t t_fin0 = clock64();
-#endif
         const int64_t b1 = owner_of(pc.seg_start + pc.seg_tiles - 1, T_total, G);
         if (row == 0) {
           for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) {
@@ -822,18 +922,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
             }
           }
         }
-        named_bar(1, 128);
+        named_bar(2, 128);
 #ifdef PAGEDKV_TRACE
-        tw[1] += clock64() - t_fin0;
+        tw[7] += clock64() - t_epi0;
 #endif
-        float mm[GP], ll[GP], a[GP];
-#pragma unroll
-        for (int g = 0; g < GP; ++g) {
-          mm[g] = m_sel[g];
-          ll[g] = l_sel[g];
-          a[g] = acc[g];
-        }
-        if (have) {
+        if (have_kv) {
           for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) {
             const int64_t hh0 = bb * HQS + hl * p.group;
             float2 ml[GP];
@@ -849,38 +942,42 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
             }
 #pragma unroll
             for (int g = 0; g < GP; ++g) {
-              const float mb = fmaxf(mm[g], ml[g].x);
-              const float sc = mm[g] == kNegInf ? 0.f : fast_exp2(mm[g] - mb);
+              const float mb = fmaxf(msel[g], ml[g].x);
+              const float sc = msel[g] == kNegInf ? 0.f : fast_exp2(msel[g] - mb);
               const float f = ml[g].x == kNegInf ? 0.f : fast_exp2(ml[g].x - mb);
-              ll[g] = fmaf(f, ml[g].y, ll[g] * sc);
-              a[g] = fmaf(f, av[g], a[g] * sc);
-              mm[g] = mb;
+              lsum[g] = fmaf(f, ml[g].y, lsum[g] * sc);
+              acc[g] = fmaf(f, av[g], acc[g] * sc);
+              msel[g] = mb;
             }
           }
 #pragma unroll
           for (int g = 0; g < GP; ++g)
-            if (g < p.group) out[(int64_t)(kv * p.group + g) * p.o_sh] = E::from_float(ll[g] > 0.f ? a[g] / ll[g] : 0.f);
+            if (g < p.group)
+              out[(int64_t)(kv * p.group + g) * p.o_sh] = E::from_float(lsum[g] > 0.f ? __fdividef(acc[g], lsum[g]) : 0.f);
         }
-        named_bar(1, 128);  // every partner partial read before its flag is cleared
+        named_bar(2, 128);  // every partner partial read before its flag is cleared
         if (row == 0) {
           for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) st_volatile_u32(tp.flags + bb, 0u);
         }
-#ifdef PAGEDKV_TRACE
-        tw[7] += clock64() - t_fin0;
-#endif
       }
 #ifdef PAGEDKV_TRACE
-      t_piece_end = clock64();
-      tw[4] += t_piece_end - t_epi0;
+      tw[4] += clock64() - t_epi0;
 #endif
+      pc = nx;
+      have = have_nx;
     }
   }
 
   // ---------------------------------------------------------------- teardown
 #ifdef PAGEDKV_TRACE
-  if (blockIdx.x < kTraceCtas && lane == 0 && warp <= 2) {
-    for (int i = 0; i < kTraceSlots; ++i) g_trace[blockIdx.x][warp][i] = tw[i];
-    if (warp >= 1) g_trace[blockIdx.x][3][5 + warp] = clock64() - c_kernel0;  // this role's own finish
+  {
+    // rows: 0 K producer, 1 S issuer, 2 softmax, 4 correction, 5 V producer,
+    // 6 O issuer (lane 0 of the role's first warp); row 3 the CTA's totals.
+    const int trow = warp == 0 ? 0 : warp == 1 ? 1 : warp == 2 ? 2 : warp == 7 ? 4 : warp == 6 ? 5 : warp == 11 ? 6 : -1;
+    if (blockIdx.x < kTraceCtas && lane == 0 && trow >= 0) {
+      for (int i = 0; i < kTraceSlots; ++i) g_trace[blockIdx.x][trow][i] = tw[i];
+      g_trace[blockIdx.x][3][8 + trow] = clock64() - c_kernel0;  // this role's own finish
+    }
   }
   __syncthreads();
   if (blockIdx.x < kTraceCtas && threadIdx.x == 0) {
