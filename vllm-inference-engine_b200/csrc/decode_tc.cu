@@ -147,12 +147,6 @@ struct Walker {
   bool started;
   int len_cur, len_nxt;  // clamped lengths of seq and seq + 1
 
-  __device__ void prime(const TcParams &tp) {
-    const DecodeParams &p = tp.p;
-    len_cur = seq < p.num_seqs ? seq_len_clamped(p, seq) : 0;
-    len_nxt = seq + 1 < p.num_seqs ? seq_len_clamped(p, seq + 1) : 0;
-  }
-
   __device__ void advance_seq(const TcParams &tp) {
     const DecodeParams &p = tp.p;
     ++seq;
@@ -194,6 +188,61 @@ struct Walker {
   }
 };
 
+// Running (sum, denominator, reference max) of one correction thread's
+// query columns.
+template <int GP>
+struct PieceAcc {
+  float acc[GP], lsum[GP], msel[GP];
+};
+
+// Stream-K combine, run by the 128 correction threads of the CTA holding a
+// cut segment's first tile: wait for the partials CTAs b+1..b1 published, fold
+// them into this CTA's piece, store the normalised output and clear the flags
+// (at most once per CTA per launch).
+template <typename T, int GP, int D>
+__device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP> a, int64_t b1, int hl, int dim,
+                                            int kv, bool have_kv, T *out, volatile int *abort_flag, int row) {
+  using E = Elem<T>;
+  const DecodeParams &p = tp.p;
+  const int HQS = (128 / D) * p.group;
+  if (row == 0) {
+    for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_u32(tp.flags + bb) == 0u) {
+        if (globaltimer_ns() - t0 > kTimeoutNs) {
+          *abort_flag = 1;
+          break;
+        }
+      }
+    }
+  }
+  named_bar(2, 128);
+  if (have_kv) {
+    for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) {
+      const int64_t hh0 = bb * HQS + hl * p.group;
+      for (int g = 0; g < GP; ++g) {
+        if (g < p.group) {
+          const float2 ml = __ldcg(&tp.part_ml[hh0 + g]);
+          const float av = __ldcg(&tp.part_acc[(hh0 + g) * D + dim]);
+          const float mb = fmaxf(a.msel[g], ml.x);
+          const float sc = a.msel[g] == kNegInf ? 0.f : fast_exp2(a.msel[g] - mb);
+          const float f = ml.x == kNegInf ? 0.f : fast_exp2(ml.x - mb);
+          a.lsum[g] = fmaf(f, ml.y, a.lsum[g] * sc);
+          a.acc[g] = fmaf(f, av, a.acc[g] * sc);
+          a.msel[g] = mb;
+        }
+      }
+    }
+    for (int g = 0; g < GP; ++g)
+      if (g < p.group)
+        out[(int64_t)(kv * p.group + g) * p.o_sh] = E::from_float(a.lsum[g] > 0.f ? __fdividef(a.acc[g], a.lsum[g]) : 0.f);
+  }
+  named_bar(2, 128);  // every partner partial read before its flag is cleared
+  if (row == 0) {
+    for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) st_volatile_u32(tp.flags + bb, 0u);
+  }
+}
+
 template <int N, int SK, int SV>
 struct SmemLayout {
   static constexpr int kQBytes = 2 * N * 128;  // B operand [N x 128], two K-halves
@@ -232,7 +281,7 @@ struct RescaleSlot {
 struct MiscSmem {
   uint32_t tmem;
   int abort;
-  int pad0[2];
+  int len0, len1;  // clamped lengths of seq0 and seq0 + 1
   int seq0, hg0, off0, pad;
   long long lo, hi, total, grid;
 };
@@ -240,7 +289,7 @@ struct MiscSmem {
 template <typename T, int H, int GP, int N, int SK, int SV>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
-                 const __grid_constant__ CUtensorMap tmap_v, const TcParams tp) {
+                 const __grid_constant__ CUtensorMap tmap_v, const __grid_constant__ TcParams tp) {
   using L = SmemLayout<N, SK, SV>;
   using E = Elem<T>;
   using Slot = RescaleSlot<N>;
@@ -364,17 +413,23 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       misc->seq0 = ns;  // empty range unless a thread below claims lo
       misc->hg0 = 0;
       misc->off0 = 0;
+      misc->len0 = 0;
+      misc->len1 = 0;
     }
     __syncthreads();
     if (lo < Tt && HG * excl <= lo && lo < HG * (excl + local)) {
       long long acc_t = HG * excl;
       for (int s = s_begin; s < s_end; ++s) {
-        const int nt = tiles_of(seq_len_clamped(p, s));
+        const int len = seq_len_clamped(p, s);
+        const int nt = tiles_of(len);
         if (lo < acc_t + HG * nt) {
           const long long rel = lo - acc_t;
           misc->seq0 = s;
           misc->hg0 = (int)(rel / nt);
           misc->off0 = (int)(rel % nt);
+          // Every role's walker starts from these, without a load of its own.
+          misc->len0 = len;
+          misc->len1 = s + 1 < ns ? seq_len_clamped(p, s + 1) : 0;
           break;
         }
         acc_t += HG * nt;
@@ -387,8 +442,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
   const uint32_t tmem = misc->tmem;
   const int64_t T_total = misc->total;
   const int64_t G = misc->grid;
-  Walker walk{misc->lo, misc->hi, misc->seq0, misc->hg0, misc->off0, false, 0, 0};
-  walk.prime(tp);
+  Walker walk{misc->lo, misc->hi, misc->seq0, misc->hg0, misc->off0, false, misc->len0, misc->len1};
 
   if (warp == 0 || warp == 6) {
     // ------------------------------------------------ producers: warp 0 K (+ Q), warp 6 V
@@ -910,55 +964,15 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         // CTA's range: this is this CTA's last piece, and this CTA combines.
         // The other pieces are the first pieces of CTAs b+1..b1, published
         // early in their runs.
-        const int64_t b1 = owner_of(pc.seg_start + pc.seg_tiles - 1, T_total, G);
-        if (row == 0) {
-          for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) {
-            const uint64_t t0 = globaltimer_ns();
-            while (ld_acquire_u32(tp.flags + bb) == 0u) {
-              if (globaltimer_ns() - t0 > kTimeoutNs) {
-                *abort_flag = 1;
-                break;
-              }
-            }
-          }
-        }
-        named_bar(2, 128);
-#ifdef PAGEDKV_TRACE
-        tw[7] += clock64() - t_epi0;
-#endif
-        if (have_kv) {
-          for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) {
-            const int64_t hh0 = bb * HQS + hl * p.group;
-            float2 ml[GP];
-            float av[GP];
+        PieceAcc<GP> pa;
 #pragma unroll
-            for (int g = 0; g < GP; ++g) {
-              ml[g] = make_float2(kNegInf, 0.f);
-              av[g] = 0.f;
-              if (g < p.group) {
-                ml[g] = __ldcg(&tp.part_ml[hh0 + g]);
-                av[g] = __ldcg(&tp.part_acc[(hh0 + g) * D + dim]);
-              }
-            }
-#pragma unroll
-            for (int g = 0; g < GP; ++g) {
-              const float mb = fmaxf(msel[g], ml[g].x);
-              const float sc = msel[g] == kNegInf ? 0.f : fast_exp2(msel[g] - mb);
-              const float f = ml[g].x == kNegInf ? 0.f : fast_exp2(ml[g].x - mb);
-              lsum[g] = fmaf(f, ml[g].y, lsum[g] * sc);
-              acc[g] = fmaf(f, av[g], acc[g] * sc);
-              msel[g] = mb;
-            }
-          }
-#pragma unroll
-          for (int g = 0; g < GP; ++g)
-            if (g < p.group)
-              out[(int64_t)(kv * p.group + g) * p.o_sh] = E::from_float(lsum[g] > 0.f ? __fdividef(acc[g], lsum[g]) : 0.f);
+        for (int g = 0; g < GP; ++g) {
+          pa.acc[g] = acc[g];
+          pa.lsum[g] = lsum[g];
+          pa.msel[g] = msel[g];
         }
-        named_bar(2, 128);  // every partner partial read before its flag is cleared
-        if (row == 0) {
-          for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) st_volatile_u32(tp.flags + bb, 0u);
-        }
+        combine_pieces<T, GP, D>(tp, pa, owner_of(pc.seg_start + pc.seg_tiles - 1, T_total, G), hl, dim, kv,
+                                 have_kv, out, abort_flag, row);
       }
 #ifdef PAGEDKV_TRACE
       tw[4] += clock64() - t_epi0;
