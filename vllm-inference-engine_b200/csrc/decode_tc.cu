@@ -122,10 +122,20 @@ __device__ __forceinline__ int seq_len_clamped(const DecodeParams &p, int seq) {
 
 __device__ __forceinline__ int tiles_of(int len) { return (len + kTile - 1) / kTile; }
 
-// First tile of CTA b and the CTA owning global tile t, for T tiles over G CTAs.
-__device__ __forceinline__ int64_t range_lo(int64_t b, int64_t T, int64_t G) { return b * T / G; }
-__device__ __forceinline__ int64_t owner_of(int64_t t, int64_t T, int64_t G) {
-  return ((t + 1) * G + T - 1) / T - 1;
+// Stream-K cost model. The segments are laid end to end in cost units: a
+// segment of nt tiles costs kSegUnits + nt * kTileUnits (the per-segment part
+// is its first piece's fixed work: Q copy, the full max reduction of its first
+// tile, the epilogue; measured, a one-tile segment costs about two streaming
+// tiles). CTA b takes the units [b*U/G, (b+1)*U/G) and owns every tile whose
+// last unit falls in them, so SMs that draw many short sequences get fewer
+// tiles and each CTA still owns one contiguous run of tiles.
+constexpr int64_t kTileUnits = 8;
+constexpr int64_t kSegUnits = 8;
+
+// First unit of CTA b and the CTA owning unit u, for U units over G CTAs.
+__device__ __forceinline__ int64_t range_lo(int64_t b, int64_t U, int64_t G) { return b * U / G; }
+__device__ __forceinline__ int64_t owner_of(int64_t u, int64_t U, int64_t G) {
+  return ((u + 1) * G + U - 1) / U - 1;
 }
 
 // One contiguous run of tiles of a (sequence, head group) segment.
@@ -134,7 +144,7 @@ struct Piece {
   int t0, t1;         // token range [t0, t1)
   int ntiles;         // tiles in this piece
   int seg_tiles;      // tiles in the whole segment
-  int64_t seg_start;  // global index of the segment's first tile
+  int64_t seg_units;  // first cost unit of the segment
   bool first;         // first piece of this CTA
 };
 
@@ -142,7 +152,7 @@ struct Piece {
 // and sees the same pieces in the same order. Sequence lengths are loaded one
 // sequence ahead, so moving to the next sequence does not wait on memory.
 struct Walker {
-  int64_t cur, hi;
+  int64_t ucur, hi;  // first unit of the current segment; end of this CTA's units
   int seq, hg, off;
   bool started;
   int len_cur, len_nxt;  // clamped lengths of seq and seq + 1
@@ -158,16 +168,20 @@ struct Walker {
 
   __device__ bool next(const TcParams &tp, Piece &pc) {
     const DecodeParams &p = tp.p;
-    if (cur >= hi || seq >= p.num_seqs) return false;
+    if (seq >= p.num_seqs) return false;
     int nt = tiles_of(len_cur);
-    while (nt == 0) {  // zero-length sequences own no tiles
+    while (nt == 0) {  // zero-length sequences own no tiles (and no units)
       advance_seq(tp);
       if (seq >= p.num_seqs) return false;
       nt = tiles_of(len_cur);
     }
     const int len = len_cur;
-    const int64_t avail = hi - cur;
-    const int take = (int)((int64_t)(nt - off) < avail ? (int64_t)(nt - off) : avail);
+    // Tiles i of this segment whose last unit ucur + kSegUnits + (i+1)*kTileUnits - 1 < hi.
+    const int64_t room = hi - ucur - kSegUnits;
+    const int64_t fit = room < kTileUnits ? 0 : room / kTileUnits;
+    const int lim = fit < nt ? (int)fit : nt;
+    if (lim <= off) return false;
+    const int take = lim - off;
     pc.seq = seq;
     pc.hg = hg;
     pc.len = len;
@@ -175,13 +189,13 @@ struct Walker {
     pc.t1 = min(len, (off + take) * kTile);
     pc.ntiles = take;
     pc.seg_tiles = nt;
-    pc.seg_start = cur - off;
+    pc.seg_units = ucur;
     pc.first = !started;
     started = true;
-    cur += take;
     off += take;
     if (off == nt) {
       off = 0;
+      ucur += kSegUnits + nt * kTileUnits;
       if (++hg == tp.head_groups) advance_seq(tp);
     }
     return true;
@@ -243,6 +257,14 @@ __device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP> 
   }
 }
 
+struct MiscSmem {
+  uint32_t tmem;
+  int abort;
+  int len0, len1;  // clamped lengths of seq0 and seq0 + 1
+  int seq0, hg0, off0, pad;
+  long long lo, hi, total, grid, u0;
+};
+
 template <int N, int SK, int SV>
 struct SmemLayout {
   static constexpr int kQBytes = 2 * N * 128;  // B operand [N x 128], two K-halves
@@ -262,7 +284,7 @@ struct SmemLayout {
   // [kQSlots]; l_full [kLSlots]
   static constexpr int kNumBars = 2 * SK + 2 * SV + 6 * 2 + 1 + kRescaleSlots + 2 * kQSlots + kLSlots;
   static constexpr int kOffMisc = kOffBars + kNumBars * 8;  // see MiscSmem
-  static constexpr int kBytes = kOffMisc + 80;
+  static constexpr int kBytes = kOffMisc + (int)sizeof(MiscSmem);
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
   static_assert(2 * 4 * N * 4 >= 8 * (kThreads / 32), "prologue scan scratch fits the max-reduction buffer");
   static_assert(kOffSlots % 16 == 0 && kSlotBytes % 16 == 0 && kOffL % 16 == 0 && kOffBars % 8 == 0, "alignment");
@@ -278,13 +300,6 @@ struct RescaleSlot {
   uint32_t pad[3];
 };
 
-struct MiscSmem {
-  uint32_t tmem;
-  int abort;
-  int len0, len1;  // clamped lengths of seq0 and seq0 + 1
-  int seq0, hg0, off0, pad;
-  long long lo, hi, total, grid;
-};
 
 template <typename T, int H, int GP, int N, int SK, int SV>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -373,15 +388,19 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
   grid_dependency_wait();
   grid_launch_dependents();
 
-  // ---- prologue: total tile count and the start of this CTA's range ----------
+  // ---- prologue: total cost units and the start of this CTA's range ----------
   {
     long long *scan = reinterpret_cast<long long *>(smem + L::kOffRedMax);  // [warps] sums
     const int ns = p.num_seqs;
     const int per = (ns + kThreads - 1) / kThreads;
     const int s_begin = min(ns, (int)threadIdx.x * per);
     const int s_end = min(ns, s_begin + per);
-    long long local = 0;
-    for (int s = s_begin; s < s_end; ++s) local += tiles_of(seq_len_clamped(p, s));
+    const long long HG = tp.head_groups;
+    long long local = 0;  // units of this thread's sequences
+    for (int s = s_begin; s < s_end; ++s) {
+      const int nt = tiles_of(seq_len_clamped(p, s));
+      if (nt > 0) local += HG * (kSegUnits + nt * kTileUnits);
+    }
     long long incl = local;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -397,19 +416,22 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       warp_off += w < warp ? v : 0;
       total += v;
     }
-    const long long excl = warp_off + incl - local;  // tiles of sequences before s_begin
-    const long long HG = tp.head_groups;
-    const long long Tt = HG * total;
-    // Effective grid: never more CTAs than tiles, so every participating CTA
-    // owns at least one tile and the owners of a segment are consecutive.
-    const long long Ge = Tt < (long long)gridDim.x ? Tt : (long long)gridDim.x;
-    const long long lo = (long long)blockIdx.x < Ge ? range_lo(blockIdx.x, Tt, Ge) : Tt;
-    const long long hi = (long long)blockIdx.x < Ge ? range_lo(blockIdx.x + 1, Tt, Ge) : Tt;
+    const long long excl = warp_off + incl - local;  // units of sequences before s_begin
+    const long long Ut = total;
+    // Effective grid: every CTA's unit range is at least one tile plus one
+    // segment wide, so it holds the last unit of some tile (consecutive tiles'
+    // last units are at most that far apart): every participating CTA owns a
+    // tile, and the owners of a segment are consecutive.
+    const long long wide = Ut / (kSegUnits + kTileUnits);
+    const long long Ge = wide < (long long)gridDim.x ? wide : (long long)gridDim.x;
+    const long long lo = (long long)blockIdx.x < Ge ? range_lo(blockIdx.x, Ut, Ge) : Ut;
+    const long long hi = (long long)blockIdx.x < Ge ? range_lo(blockIdx.x + 1, Ut, Ge) : Ut;
     if (threadIdx.x == 0) {
       misc->lo = lo;
       misc->hi = hi;
-      misc->total = Tt;
+      misc->total = Ut;
       misc->grid = Ge;
+      misc->u0 = Ut;
       misc->seq0 = ns;  // empty range unless a thread below claims lo
       misc->hg0 = 0;
       misc->off0 = 0;
@@ -417,22 +439,29 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       misc->len1 = 0;
     }
     __syncthreads();
-    if (lo < Tt && HG * excl <= lo && lo < HG * (excl + local)) {
-      long long acc_t = HG * excl;
+    if (lo < Ut && excl <= lo && lo < excl + local) {
+      // This thread's sequences hold unit lo: the CTA's first tile is the
+      // first one whose last unit is >= lo.
+      long long acc_u = excl;
       for (int s = s_begin; s < s_end; ++s) {
         const int len = seq_len_clamped(p, s);
         const int nt = tiles_of(len);
-        if (lo < acc_t + HG * nt) {
-          const long long rel = lo - acc_t;
+        if (nt == 0) continue;
+        const long long seg_u = kSegUnits + nt * kTileUnits;
+        if (lo < acc_u + HG * seg_u) {
+          const long long hg = (lo - acc_u) / seg_u;
+          const long long uk = acc_u + hg * seg_u;
+          const long long rel = lo - uk - kSegUnits;
           misc->seq0 = s;
-          misc->hg0 = (int)(rel / nt);
-          misc->off0 = (int)(rel % nt);
+          misc->hg0 = (int)hg;
+          misc->off0 = rel < 0 ? 0 : (int)(rel / kTileUnits);
+          misc->u0 = uk;
           // Every role's walker starts from these, without a load of its own.
           misc->len0 = len;
           misc->len1 = s + 1 < ns ? seq_len_clamped(p, s + 1) : 0;
           break;
         }
-        acc_t += HG * nt;
+        acc_u += HG * seg_u;
       }
     }
   }
@@ -440,9 +469,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = misc->tmem;
-  const int64_t T_total = misc->total;
+  const int64_t U_total = misc->total;
   const int64_t G = misc->grid;
-  Walker walk{misc->lo, misc->hi, misc->seq0, misc->hg0, misc->off0, false, misc->len0, misc->len1};
+  Walker walk{misc->u0, misc->hi, misc->seq0, misc->hg0, misc->off0, false, misc->len0, misc->len1};
 
   if (warp == 0 || warp == 6) {
     // ------------------------------------------------ producers: warp 0 K (+ Q), warp 6 V
@@ -971,7 +1000,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           pa.lsum[g] = lsum[g];
           pa.msel[g] = msel[g];
         }
-        combine_pieces<T, GP, D>(tp, pa, owner_of(pc.seg_start + pc.seg_tiles - 1, T_total, G), hl, dim, kv,
+        combine_pieces<T, GP, D>(tp, pa, owner_of(pc.seg_units + kSegUnits + (int64_t)pc.seg_tiles * kTileUnits - 1, U_total, G), hl, dim, kv,
                                  have_kv, out, abort_flag, row);
       }
 #ifdef PAGEDKV_TRACE
