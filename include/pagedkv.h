@@ -43,6 +43,7 @@ extern "C" {
 /* ---- element types ------------------------------------------------------ */
 #define PAGEDKV_DTYPE_F16   0
 #define PAGEDKV_DTYPE_BF16  1
+#define PAGEDKV_DTYPE_F32   2   /* prefill-write sources only */
 
 /* ---- device error word bits (set by kernels, read by pagedkv_read_error_flags) */
 #define PAGEDKV_EFLAG_BLOCK_ID_RANGE  0x1u  /* a block-table entry >= num_blocks or < 0 */
@@ -142,6 +143,32 @@ int pagedkv_copy_blocks(
     void *const *k_cache_ptrs, void *const *v_cache_ptrs, int32_t num_layers,
     const int64_t *block_mapping, int32_t num_pairs, int64_t block_bytes,
     int64_t num_blocks, void *stream);
+
+/*
+ * Prefill K/V write: a prompt's rows of every layer into whole pool blocks.
+ * Replaces KernelPagedManualDecode._copy_prefill_kv
+ * (engine/kernels/paged_attention_integration.py:278-326: pad to whole blocks,
+ * .to(pool dtype), index_copy_ into each layer's K and V pool). For every
+ * layer l, block i < num_write_blocks, position t < block_size, kv head h:
+ *   pool[l][block_ids[i], t, h, :] = src[l][i * block_size + t, h, :]
+ *                                    if i * block_size + t < num_tokens,
+ *                                  = 0 otherwise (the padded tail),
+ * bit-exact (f32 sources are rounded to nearest even, as torch's .to()).
+ * k_caches / v_caches / k_srcs / v_srcs are HOST arrays of num_layers device
+ * pointers; each source is a [num_tokens, num_kv_heads, head_dim] view with the
+ * given element strides (last dim contiguous), src_dtype = the pool dtype or
+ * PAGEDKV_DTYPE_F32. block_ids is a DEVICE int64 [num_write_blocks] array
+ * (out-of-range ids are skipped and flagged PAGEDKV_EFLAG_BLOCK_ID_RANGE).
+ * One launch per 48 layers, K and V together.
+ */
+int pagedkv_kv_write_prefill(
+    void *const *k_caches, void *const *v_caches,
+    const void *const *k_srcs, const void *const *v_srcs, int32_t num_layers,
+    int64_t k_src_stride_tok, int64_t k_src_stride_head,
+    int64_t v_src_stride_tok, int64_t v_src_stride_head, int32_t src_dtype,
+    const int64_t *block_ids, int32_t num_write_blocks, int32_t num_tokens,
+    int32_t num_kv_heads, int32_t head_dim, int64_t num_blocks, int32_t block_size,
+    int32_t dtype, void *stream);
 
 /*
  * Read (and optionally clear) the device error word of the current device.

@@ -144,6 +144,32 @@ def copy_blocks_ref(
             vc[dst] = vc[src]
 
 
+def prefill_write_ref(
+    k_caches: Sequence[torch.Tensor],
+    v_caches: Sequence[torch.Tensor],
+    k_srcs: Sequence[torch.Tensor],
+    v_srcs: Sequence[torch.Tensor],
+    block_ids: Sequence[int],
+    num_tokens: int,
+) -> None:
+    """In place, restating KernelPagedManualDecode._copy_prefill_kv
+    (paged_attention_integration.py:305-326): the [num_tokens, Hkv, D] source
+    rows are zero-padded to whole blocks (:315-317), converted to the pool
+    dtype (:319-320, torch .to: round to nearest even) and index_copy_'d into
+    blocks ``block_ids`` of every layer's K and V pool (:322-323)."""
+    bs, hkv, d = k_caches[0].shape[1:]
+    nw = len(block_ids)
+    pad = nw * bs - num_tokens
+    ids = torch.tensor(list(block_ids), dtype=torch.long, device=k_caches[0].device)
+    for kc, vc, ks, vs in zip(k_caches, v_caches, k_srcs, v_srcs):
+        k_src, v_src = ks[:num_tokens], vs[:num_tokens]
+        if pad > 0:
+            k_src = torch.nn.functional.pad(k_src, (0, 0, 0, 0, 0, pad))
+            v_src = torch.nn.functional.pad(v_src, (0, 0, 0, 0, 0, pad))
+        kc.index_copy_(0, ids, k_src.reshape(nw, bs, hkv, d).to(kc.dtype))
+        vc.index_copy_(0, ids, v_src.reshape(nw, bs, hkv, d).to(vc.dtype))
+
+
 def time_paged_attention_cpu(
     q: torch.Tensor,
     k_cache: torch.Tensor,

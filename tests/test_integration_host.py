@@ -104,6 +104,8 @@ def test_install_replaces_reference_symbols_and_uninstall_restores():
         assert integ.PagedAttentionContext is integration.PagedAttentionContext
         assert integ.paged_decode_attention_forward is integration.paged_decode_attention_forward
         assert pa.naive_reference_paged_attention.__module__ == "engine.kernels.paged_attention"
+        assert integ.KernelPagedManualDecode._copy_prefill_kv is integration.copy_prefill_kv
     finally:
         integration.uninstall(saved)
+    assert integ.KernelPagedManualDecode._copy_prefill_kv is not integration.copy_prefill_kv
     assert (pa.paged_attention_decode_batched, integ.paged_attention_decode_batched, integ.PagedAttentionContext) == before

@@ -65,6 +65,29 @@ def test_append_and_copy_reject_bad_arguments_without_a_device():
     assert lib.pagedkv_read_error_flags(None, 0, None) == _native.PAGEDKV_ERR_INVALID_ARGUMENT
 
 
+def test_prefill_write_rejects_bad_arguments_without_a_device():
+    lib = _native.lib()
+    f = lib.pagedkv_kv_write_prefill
+    # (pool ptrs, srcs, layers, strides, src dtype, ids, blocks, tokens, hkv, d, nb, bs, dtype, stream)
+    assert f(None, None, None, None, 0, 0, 0, 0, 0, 0, None, 4, 10, 2, 64, 16, 16, 0, None) == 0  # no layers
+    assert f(None, None, None, None, 2, 0, 0, 0, 0, 0, None, 0, 0, 2, 64, 16, 16, 0, None) == 0  # no blocks
+    assert f(None, None, None, None, 2, 0, 0, 0, 0, 1, None, 4, 10, 2, 64, 16, 16, 0, None) == (
+        _native.PAGEDKV_ERR_UNSUPPORTED  # bf16 source into an f16 pool
+    )
+    assert f(None, None, None, None, 2, 0, 0, 0, 0, 0, None, 4, 10, 2, 64, 16, 16, 2, None) == (
+        _native.PAGEDKV_ERR_UNSUPPORTED  # f32 pool
+    )
+    assert f(None, None, None, None, 2, 0, 0, 0, 0, 0, None, 2, 33, 2, 64, 16, 16, 0, None) == (
+        _native.PAGEDKV_ERR_INVALID_ARGUMENT  # more tokens than the blocks hold
+    )
+    assert f(None, None, None, None, 2, 0, 0, 0, 0, 0, None, 2, 20, 2, 60, 16, 16, 0, None) == (
+        _native.PAGEDKV_ERR_INVALID_ARGUMENT  # head_dim not a multiple of 8
+    )
+    assert f(None, None, None, None, 2, 0, 0, 0, 0, 2, None, 2, 20, 2, 64, 16, 16, 0, None) == (
+        _native.PAGEDKV_ERR_INVALID_ARGUMENT  # null pointers
+    )
+
+
 def test_error_flag_descriptions():
     assert _native.describe_error_flags(0) == "none"
     text = _native.describe_error_flags(_native.EFLAG_BLOCK_ID_RANGE | _native.EFLAG_SLOT_RANGE)

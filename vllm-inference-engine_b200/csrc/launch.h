@@ -54,6 +54,23 @@ cudaError_t launch_kv_append(void *k_cache, void *v_cache, const void *k_new, in
                              int32_t num_kv_heads, int32_t head_dim, int64_t num_slots,
                              bool vectorized, unsigned int *err, cudaStream_t stream);
 
+// Prefill write of up to kPrefillMaxLayers layers in one launch (pointer
+// arrays passed by value).
+constexpr int kPrefillMaxLayers = 48;
+struct PrefillParams {
+  void *k_dst[kPrefillMaxLayers];
+  void *v_dst[kPrefillMaxLayers];
+  const void *k_src[kPrefillMaxLayers];
+  const void *v_src[kPrefillMaxLayers];
+  int64_t k_stride_tok, k_stride_head, v_stride_tok, v_stride_head;  // source strides (elements)
+  const int64_t *block_ids;                                           // [num_write_blocks]
+  int64_t num_blocks;
+  int32_t num_layers, num_write_blocks, num_tokens, num_kv_heads, head_dim, block_size;
+};
+
+cudaError_t launch_kv_write_prefill(const PrefillParams &pp, int dtype, int src_dtype, bool vec,
+                                    unsigned int *err, cudaStream_t stream);
+
 cudaError_t launch_copy_blocks(void *const *k_ptrs, void *const *v_ptrs, int32_t num_layers,
                                const int64_t *mapping, int32_t num_pairs, int64_t block_bytes,
                                int64_t num_blocks, unsigned int *err, cudaStream_t stream);

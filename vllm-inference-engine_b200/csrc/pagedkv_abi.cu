@@ -275,6 +275,69 @@ int pagedkv_copy_blocks(void *const *k_cache_ptrs, void *const *v_cache_ptrs, in
   return PAGEDKV_OK;
 }
 
+int pagedkv_kv_write_prefill(void *const *k_caches, void *const *v_caches, const void *const *k_srcs,
+                             const void *const *v_srcs, int32_t num_layers, int64_t k_stride_tok,
+                             int64_t k_stride_head, int64_t v_stride_tok, int64_t v_stride_head,
+                             int32_t src_dtype, const int64_t *block_ids, int32_t num_write_blocks,
+                             int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                             int64_t num_blocks, int32_t block_size, int32_t dtype, void *stream) {
+  if (num_layers < 0 || num_write_blocks < 0 || num_tokens < 0)
+    return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "num_layers, num_write_blocks, num_tokens must be >= 0");
+  if (num_layers == 0 || num_write_blocks == 0) return PAGEDKV_OK;
+  if (dtype != PAGEDKV_DTYPE_F16 && dtype != PAGEDKV_DTYPE_BF16)
+    return fail(PAGEDKV_ERR_UNSUPPORTED, "pool dtype %d not supported (0=f16, 1=bf16)", dtype);
+  if (src_dtype != dtype && src_dtype != PAGEDKV_DTYPE_F32)
+    return fail(PAGEDKV_ERR_UNSUPPORTED, "source dtype %d must equal the pool dtype %d or be f32 (2)",
+                src_dtype, dtype);
+  if (num_kv_heads <= 0 || head_dim <= 0 || (head_dim % 8) != 0 || block_size <= 0 || num_blocks <= 0)
+    return fail(PAGEDKV_ERR_INVALID_ARGUMENT,
+                "num_kv_heads, block_size, num_blocks must be > 0 and head_dim a positive multiple of 8");
+  if ((int64_t)num_tokens > (int64_t)num_write_blocks * block_size)
+    return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "num_tokens (%d) exceeds num_write_blocks * block_size", num_tokens);
+  if (!k_caches || !v_caches || !k_srcs || !v_srcs || !block_ids)
+    return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "null pointer");
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc != PAGEDKV_OK) return rc;
+  // Vector loads need every 8-element source chunk aligned: strides in whole chunks.
+  bool vec = (k_stride_tok % 8) == 0 && (k_stride_head % 8) == 0 && (v_stride_tok % 8) == 0 &&
+             (v_stride_head % 8) == 0;
+  const size_t src_align = src_dtype == PAGEDKV_DTYPE_F32 ? 32 : 16;
+  for (int32_t l = 0; l < num_layers; ++l) {
+    if (!k_caches[l] || !v_caches[l] || !k_srcs[l] || !v_srcs[l])
+      return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "null pointer for layer %d", l);
+    if (!aligned16(k_caches[l]) || !aligned16(v_caches[l]))
+      return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "pool of layer %d is not 16-byte aligned", l);
+    if (reinterpret_cast<uintptr_t>(k_srcs[l]) % src_align || reinterpret_cast<uintptr_t>(v_srcs[l]) % src_align)
+      vec = false;
+  }
+  PrefillParams pp{};
+  pp.k_stride_tok = k_stride_tok;
+  pp.k_stride_head = k_stride_head;
+  pp.v_stride_tok = v_stride_tok;
+  pp.v_stride_head = v_stride_head;
+  pp.block_ids = block_ids;
+  pp.num_blocks = num_blocks;
+  pp.num_write_blocks = num_write_blocks;
+  pp.num_tokens = num_tokens;
+  pp.num_kv_heads = num_kv_heads;
+  pp.head_dim = head_dim;
+  pp.block_size = block_size;
+  for (int32_t l0 = 0; l0 < num_layers; l0 += kPrefillMaxLayers) {
+    const int32_t n = num_layers - l0 < kPrefillMaxLayers ? num_layers - l0 : kPrefillMaxLayers;
+    pp.num_layers = n;
+    for (int32_t i = 0; i < n; ++i) {
+      pp.k_dst[i] = k_caches[l0 + i];
+      pp.v_dst[i] = v_caches[l0 + i];
+      pp.k_src[i] = k_srcs[l0 + i];
+      pp.v_src[i] = v_srcs[l0 + i];
+    }
+    cudaError_t e = launch_kv_write_prefill(pp, dtype, src_dtype, vec, di.err, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "kv_write_prefill launch");
+  }
+  return PAGEDKV_OK;
+}
+
 int pagedkv_read_error_flags(uint32_t *flags_out, int32_t clear, void *stream) {
   if (!flags_out) return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "flags_out is null");
   DeviceInfo di;

@@ -9,6 +9,7 @@ place (:func:`pagedkv.integration.install`).
 from .paged_attention import (
     copy_blocks,
     kv_append,
+    kv_write_prefill,
     last_decode_launch_info,
     pad_block_tables,
     paged_attention_decode,
@@ -21,6 +22,7 @@ from .paged_attention import (
 __all__ = [
     "copy_blocks",
     "kv_append",
+    "kv_write_prefill",
     "last_decode_launch_info",
     "pad_block_tables",
     "paged_attention_decode",

@@ -20,6 +20,7 @@ PAGEDKV_ERR_WORKSPACE = 4
 
 DTYPE_F16 = 0
 DTYPE_BF16 = 1
+DTYPE_F32 = 2  # prefill-write sources only
 
 EFLAG_BLOCK_ID_RANGE = 0x1
 EFLAG_SLOT_RANGE = 0x2
@@ -80,6 +81,17 @@ _SIGNATURES = [
         "pagedkv_copy_blocks",
         ctypes.c_int,
         [_c_vp, _c_vp, _c_i32, _c_vp, _c_i32, _c_i64, _c_i64, _c_vp],
+    ),
+    (
+        "pagedkv_kv_write_prefill",
+        ctypes.c_int,
+        [
+            _c_vp, _c_vp, _c_vp, _c_vp, _c_i32,     # k/v pool pointer arrays, k/v source pointer arrays, layers
+            _c_i64, _c_i64, _c_i64, _c_i64, _c_i32,  # k/v source strides, source dtype
+            _c_vp, _c_i32, _c_i32,                  # block_ids, blocks to write, tokens
+            _c_i32, _c_i32, _c_i64, _c_i32, _c_i32,  # kv heads, head_dim, num_blocks, block_size, dtype
+            _c_vp,
+        ],
     ),
     (
         "pagedkv_decode_attention_noalloc",

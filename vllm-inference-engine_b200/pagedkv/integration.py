@@ -32,6 +32,7 @@ import torch
 from .paged_attention import (
     copy_blocks,
     kv_append,
+    kv_write_prefill,
     pad_block_tables,
     paged_attention_decode,
     paged_attention_decode_batched,
@@ -247,6 +248,47 @@ def copy_on_write(pool: Any, pairs: Sequence[Tuple[int, int]]) -> None:
     copy_blocks(pool.k_cache, pool.v_cache, mapping)
 
 
+def _layer_kv(pkv: Any, layer: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(keys, values) [batch, kv_heads, tokens, head_dim] of one layer of a
+    prefill cache, in either layout the reference reads (integration.py:308-313)."""
+    if hasattr(pkv, "layers"):
+        return pkv.layers[layer].keys, pkv.layers[layer].values
+    return pkv[layer][0], pkv[layer][1]
+
+
+def copy_prefill_kv(self: Any, pkv: Any, block_table: Any, prompt_len: int, skip_blocks: int = 0) -> None:
+    """Drop-in for ``KernelPagedManualDecode._copy_prefill_kv``
+    (integration.py:278-326): write the prompt's K/V from token
+    ``skip_blocks * block_size`` on into blocks ``[skip_blocks,
+    ceil(prompt_len / block_size))`` of the sequence's table, zero-padding the
+    last block's tail, for every layer in ONE launch (the reference pads and
+    runs two ``index_copy_`` per layer). Blocks before ``skip_blocks`` (prefix
+    cache hits) are not touched; nothing is allocated here."""
+    bs = self.block_size
+    start_token = skip_blocks * bs
+    if start_token >= prompt_len:
+        return
+    total_blocks = (prompt_len + bs - 1) // bs
+    blocks_to_write = total_blocks - skip_blocks
+    if blocks_to_write <= 0:
+        return
+    k_caches, v_caches = self.pool.k_cache, self.pool.v_cache
+    dev = k_caches[0].device
+    ids = torch.tensor(block_table.physical_block_ids[skip_blocks:total_blocks], dtype=torch.int64).to(dev)
+    k_srcs, v_srcs = [], []
+    for layer in range(len(k_caches)):
+        keys, values = _layer_kv(pkv, layer)
+        k = keys[0, :, start_token:prompt_len, :].permute(1, 0, 2)
+        v = values[0, :, start_token:prompt_len, :].permute(1, 0, 2)
+        if k.dtype not in (k_caches[0].dtype, torch.float32):
+            k, v = k.to(k_caches[0].dtype), v.to(k_caches[0].dtype)
+        if k.stride(2) != 1 or v.stride() != k.stride():
+            k, v = k.contiguous(), v.contiguous()
+        k_srcs.append(k)
+        v_srcs.append(v)
+    kv_write_prefill(k_srcs, v_srcs, k_caches, v_caches, ids, prompt_len - start_token)
+
+
 _INSTALL_NAMES_KERNELS = (
     "paged_attention_decode_batched",
     "paged_attention_decode_v1",
@@ -288,6 +330,12 @@ def install(paged_attention_module: Any = None, integration_module: Any = None) 
             if hasattr(mod, name):
                 saved[(mod, name)] = getattr(mod, name)
                 setattr(mod, name, fn)
+    # The runner's prefill write (a method, patched on the class).
+    runner_cls = getattr(integration_module, "KernelPagedManualDecode", None)
+    if runner_cls is not None and hasattr(runner_cls, "_copy_prefill_kv"):
+        saved[(runner_cls, "_copy_prefill_kv")] = runner_cls.__dict__.get(
+            "_copy_prefill_kv", getattr(runner_cls, "_copy_prefill_kv"))
+        setattr(runner_cls, "_copy_prefill_kv", copy_prefill_kv)
     return saved
 
 

@@ -25,6 +25,7 @@ be strided views (last dimension contiguous).
 """
 from __future__ import annotations
 
+import ctypes
 import os
 from typing import Any, Sequence
 
@@ -404,6 +405,64 @@ def copy_blocks(
         )
     _native.check(rc, "pagedkv_copy_blocks")
     _debug_check(dev, "copy_blocks")
+
+
+def kv_write_prefill(
+    k_srcs: Sequence[torch.Tensor],
+    v_srcs: Sequence[torch.Tensor],
+    k_caches: Sequence[torch.Tensor],
+    v_caches: Sequence[torch.Tensor],
+    block_ids: torch.Tensor,  # [num_write_blocks] int64, on the pools' device
+    num_tokens: int,
+) -> None:
+    """Prefill K/V write into whole blocks, every layer in one launch.
+
+    For layer l, block i and position t: ``k_caches[l][block_ids[i], t] =
+    k_srcs[l][i * block_size + t]`` while that index is below ``num_tokens``,
+    else zeros (the padded tail of the last block); the same for V. Sources are
+    ``[num_tokens, num_kv_heads, head_dim]`` views (any token / head strides,
+    last dim contiguous) in the pool dtype or float32 (rounded to nearest even,
+    as ``.to()``). Restates ``_copy_prefill_kv``
+    (paged_attention_integration.py:278-326: pad + index_copy_ per layer).
+    """
+    nl = len(k_caches)
+    assert nl > 0 and len(v_caches) == nl and len(k_srcs) == nl and len(v_srcs) == nl
+    ref = k_caches[0]
+    assert ref.is_cuda and ref.dim() == 4, "pools must be CUDA [num_blocks, block_size, kv_heads, head_dim]"
+    assert ref.dtype in (torch.float16, torch.bfloat16), "pool dtype must be float16 or bfloat16"
+    for t in list(k_caches) + list(v_caches):
+        assert t.shape == ref.shape and t.dtype == ref.dtype and t.is_contiguous() and t.device == ref.device
+    nb, bs, hkv, d = ref.shape
+    src_dtype = k_srcs[0].dtype
+    assert src_dtype in (ref.dtype, torch.float32), "source dtype must be the pool dtype or float32"
+    ks0, vs0 = k_srcs[0], v_srcs[0]
+    for t, t0 in [(t, ks0) for t in k_srcs] + [(t, vs0) for t in v_srcs]:
+        assert t.is_cuda and t.device == ref.device and t.dtype == src_dtype
+        assert t.dim() == 3 and t.shape[1:] == (hkv, d) and t.shape[0] >= num_tokens
+        assert t.stride(2) == 1 and t.stride()[:2] == t0.stride()[:2], "sources share one layout, last dim contiguous"
+    assert block_ids.is_cuda and block_ids.device == ref.device and block_ids.dtype == torch.int64 and block_ids.dim() == 1
+    nw = block_ids.shape[0]
+    assert 0 <= num_tokens <= nw * bs
+    if nw == 0:
+        return
+    ids = block_ids if block_ids.is_contiguous() else block_ids.contiguous()
+    arr = ctypes.c_void_p * nl
+    kc = arr(*[t.data_ptr() for t in k_caches])
+    vc = arr(*[t.data_ptr() for t in v_caches])
+    ksrc = arr(*[t.data_ptr() for t in k_srcs])
+    vsrc = arr(*[t.data_ptr() for t in v_srcs])
+    sd = _native.DTYPE_F32 if src_dtype == torch.float32 else _DTYPES[ref.dtype]
+    dev = ref.device
+    guard = _device_guard(dev)
+    with guard if guard is not None else _NullCtx():
+        rc = _native.lib().pagedkv_kv_write_prefill(
+            kc, vc, ksrc, vsrc, nl,
+            ks0.stride(0), ks0.stride(1), vs0.stride(0), vs0.stride(1), sd,
+            ids.data_ptr(), nw, int(num_tokens), hkv, d, nb, bs, _DTYPES[ref.dtype],
+            _stream_handle(dev),
+        )
+    _native.check(rc, "pagedkv_kv_write_prefill")
+    _debug_check(dev, "kv_write_prefill")
 
 
 def last_decode_launch_info() -> tuple[int, str]:
