@@ -145,6 +145,31 @@ int pagedkv_copy_blocks(
     int64_t num_blocks, void *stream);
 
 /*
+ * Fused rotary embedding + KV append for a decode step. Replaces the
+ * apply_rotary_pos_emb call (engine/kernels/paged_attention_integration.py:
+ * 108-109, transformers' x * cos + rotate_half(x) * sin with
+ * rotate_half(x) = cat(-x[D/2:], x[:D/2])) plus the append of :150-160.
+ * For token t: q_out[t, h] = rope(q[t, h]) for every query head;
+ * k_cache[slot] = rope(k_new[t]), v_cache[slot] = v_new[t] with
+ * slot = slot_mapping[t] (negative = skip), rounded exactly as the tensor ops
+ * (each product and the sum rounded to the dtype), i.e. bit-identical to the
+ * reference's result. cos / sin: [num_tokens, head_dim] rows (row stride
+ * cos_sin_stride_tok, last dim contiguous) in the same dtype. All strides are in
+ * elements with a contiguous last dim; head_dim a multiple of 16. q_out may
+ * alias q. One launch.
+ */
+int pagedkv_kv_append_rope(
+    void *q_out, int64_t q_out_stride_tok, int64_t q_out_stride_head,
+    const void *q, int64_t q_stride_tok, int64_t q_stride_head, int32_t num_q_heads,
+    void *k_cache, void *v_cache,
+    const void *k_new, int64_t k_new_stride_tok, int64_t k_new_stride_head,
+    const void *v_new, int64_t v_new_stride_tok, int64_t v_new_stride_head,
+    const void *cos, const void *sin, int64_t cos_sin_stride_tok,
+    const int64_t *slot_mapping, int32_t num_tokens, int32_t num_kv_heads,
+    int32_t head_dim, int64_t num_blocks, int32_t block_size, int32_t dtype,
+    void *stream);
+
+/*
  * Prefill K/V write: a prompt's rows of every layer into whole pool blocks.
  * Replaces KernelPagedManualDecode._copy_prefill_kv
  * (engine/kernels/paged_attention_integration.py:278-326: pad to whole blocks,

@@ -144,6 +144,17 @@ def copy_blocks_ref(
             vc[dst] = vc[src]
 
 
+def rope_ref(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Rotary embedding as transformers' apply_rotary_pos_emb computes it for
+    one decode token (used at paged_attention_integration.py:108-109):
+    ``x * cos + rotate_half(x) * sin`` with rotate_half(x) = cat(-x2, x1), as
+    16-bit tensor ops (each product and the sum rounded to the dtype).
+    x: [tokens, heads, D]; cos / sin: [tokens, D]."""
+    half = x.shape[-1] // 2
+    rot = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+    return (x * cos[:, None, :]) + (rot * sin[:, None, :])
+
+
 def prefill_write_ref(
     k_caches: Sequence[torch.Tensor],
     v_caches: Sequence[torch.Tensor],

@@ -65,6 +65,17 @@ def test_append_and_copy_reject_bad_arguments_without_a_device():
     assert lib.pagedkv_read_error_flags(None, 0, None) == _native.PAGEDKV_ERR_INVALID_ARGUMENT
 
 
+def test_append_rope_rejects_bad_arguments_without_a_device():
+    lib = _native.lib()
+    f = lib.pagedkv_kv_append_rope
+    args = [None, 0, 0, None, 0, 0, 14, None, None, None, 0, 0, None, 0, 0, None, None, 0, None]
+    assert f(*args, 0, 2, 64, 16, 16, 0, None) == 0  # no tokens
+    assert f(*args, 4, 2, 64, 16, 16, 3, None) == _native.PAGEDKV_ERR_UNSUPPORTED  # dtype
+    assert f(*args, 4, 2, 72, 16, 16, 0, None) == _native.PAGEDKV_ERR_UNSUPPORTED  # head_dim % 16
+    assert f(*args, 4, 2, 64, 16, 16, 0, None) == _native.PAGEDKV_ERR_INVALID_ARGUMENT  # null pointers
+    assert f(*args, -1, 2, 64, 16, 16, 0, None) == _native.PAGEDKV_ERR_INVALID_ARGUMENT
+
+
 def test_prefill_write_rejects_bad_arguments_without_a_device():
     lib = _native.lib()
     f = lib.pagedkv_kv_write_prefill

@@ -71,6 +71,27 @@ struct PrefillParams {
 cudaError_t launch_kv_write_prefill(const PrefillParams &pp, int dtype, int src_dtype, bool vec,
                                     unsigned int *err, cudaStream_t stream);
 
+// Fused rotary embedding + KV append (strides in elements).
+struct RopeParams {
+  void *q_out;
+  int64_t qo_st, qo_sh;
+  const void *q;
+  int64_t q_st, q_sh;
+  void *k_cache, *v_cache;
+  const void *k;
+  int64_t k_st, k_sh;
+  const void *v;
+  int64_t v_st, v_sh;
+  const void *cos, *sin;  // [num_tokens, head_dim] rows
+  int64_t cs_st;
+  const int64_t *slots;
+  int64_t num_slots;
+  int32_t num_tokens, hq, hkv, head_dim;
+};
+
+cudaError_t launch_kv_append_rope(const RopeParams &rp, int dtype, bool vec, unsigned int *err,
+                                  cudaStream_t stream);
+
 cudaError_t launch_copy_blocks(void *const *k_ptrs, void *const *v_ptrs, int32_t num_layers,
                                const int64_t *mapping, int32_t num_pairs, int64_t block_bytes,
                                int64_t num_blocks, unsigned int *err, cudaStream_t stream);

@@ -275,6 +275,62 @@ int pagedkv_copy_blocks(void *const *k_cache_ptrs, void *const *v_cache_ptrs, in
   return PAGEDKV_OK;
 }
 
+int pagedkv_kv_append_rope(void *q_out, int64_t q_out_stride_tok, int64_t q_out_stride_head, const void *q,
+                           int64_t q_stride_tok, int64_t q_stride_head, int32_t num_q_heads, void *k_cache,
+                           void *v_cache, const void *k_new, int64_t k_new_stride_tok,
+                           int64_t k_new_stride_head, const void *v_new, int64_t v_new_stride_tok,
+                           int64_t v_new_stride_head, const void *cos, const void *sin,
+                           int64_t cos_sin_stride_tok, const int64_t *slot_mapping, int32_t num_tokens,
+                           int32_t num_kv_heads, int32_t head_dim, int64_t num_blocks, int32_t block_size,
+                           int32_t dtype, void *stream) {
+  if (num_tokens < 0) return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "num_tokens must be >= 0");
+  if (num_tokens == 0) return PAGEDKV_OK;
+  if (dtype != PAGEDKV_DTYPE_F16 && dtype != PAGEDKV_DTYPE_BF16)
+    return fail(PAGEDKV_ERR_UNSUPPORTED, "dtype %d not supported (0=f16, 1=bf16)", dtype);
+  if (num_q_heads <= 0 || num_kv_heads <= 0 || block_size <= 0 || num_blocks <= 0)
+    return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "num_q_heads, num_kv_heads, block_size, num_blocks must be > 0");
+  if (head_dim <= 0 || (head_dim % 16) != 0)
+    return fail(PAGEDKV_ERR_UNSUPPORTED, "head_dim (%d) must be a positive multiple of 16", head_dim);
+  if (!q_out || !q || !k_cache || !v_cache || !k_new || !v_new || !cos || !sin || !slot_mapping)
+    return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "null pointer");
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc != PAGEDKV_OK) return rc;
+  const int64_t strides[] = {q_out_stride_tok, q_out_stride_head, q_stride_tok, q_stride_head,
+                             k_new_stride_tok, k_new_stride_head, v_new_stride_tok, v_new_stride_head,
+                             cos_sin_stride_tok};
+  bool vec = aligned16(q_out) && aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(k_new) &&
+             aligned16(v_new) && aligned16(cos) && aligned16(sin);
+  for (int64_t st : strides) vec = vec && (st % 8) == 0;
+  RopeParams rp{};
+  rp.q_out = q_out;
+  rp.qo_st = q_out_stride_tok;
+  rp.qo_sh = q_out_stride_head;
+  rp.q = q;
+  rp.q_st = q_stride_tok;
+  rp.q_sh = q_stride_head;
+  rp.k_cache = k_cache;
+  rp.v_cache = v_cache;
+  rp.k = k_new;
+  rp.k_st = k_new_stride_tok;
+  rp.k_sh = k_new_stride_head;
+  rp.v = v_new;
+  rp.v_st = v_new_stride_tok;
+  rp.v_sh = v_new_stride_head;
+  rp.cos = cos;
+  rp.sin = sin;
+  rp.cs_st = cos_sin_stride_tok;
+  rp.slots = slot_mapping;
+  rp.num_slots = num_blocks * block_size;
+  rp.num_tokens = num_tokens;
+  rp.hq = num_q_heads;
+  rp.hkv = num_kv_heads;
+  rp.head_dim = head_dim;
+  cudaError_t e = launch_kv_append_rope(rp, dtype, vec, di.err, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "kv_append_rope launch");
+  return PAGEDKV_OK;
+}
+
 int pagedkv_kv_write_prefill(void *const *k_caches, void *const *v_caches, const void *const *k_srcs,
                              const void *const *v_srcs, int32_t num_layers, int64_t k_stride_tok,
                              int64_t k_stride_head, int64_t v_stride_tok, int64_t v_stride_head,

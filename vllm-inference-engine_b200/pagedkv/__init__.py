@@ -9,6 +9,7 @@ place (:func:`pagedkv.integration.install`).
 from .paged_attention import (
     copy_blocks,
     kv_append,
+    kv_append_rope,
     kv_write_prefill,
     last_decode_launch_info,
     pad_block_tables,
@@ -22,6 +23,7 @@ from .paged_attention import (
 __all__ = [
     "copy_blocks",
     "kv_append",
+    "kv_append_rope",
     "kv_write_prefill",
     "last_decode_launch_info",
     "pad_block_tables",

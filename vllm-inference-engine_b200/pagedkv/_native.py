@@ -83,6 +83,20 @@ _SIGNATURES = [
         [_c_vp, _c_vp, _c_i32, _c_vp, _c_i32, _c_i64, _c_i64, _c_vp],
     ),
     (
+        "pagedkv_kv_append_rope",
+        ctypes.c_int,
+        [
+            _c_vp, _c_i64, _c_i64,                  # q_out, strides
+            _c_vp, _c_i64, _c_i64, _c_i32,          # q, strides, num_q_heads
+            _c_vp, _c_vp,                           # k_cache, v_cache
+            _c_vp, _c_i64, _c_i64,                  # k_new, strides
+            _c_vp, _c_i64, _c_i64,                  # v_new, strides
+            _c_vp, _c_vp, _c_i64,                   # cos, sin, row stride
+            _c_vp, _c_i32, _c_i32, _c_i32, _c_i64, _c_i32, _c_i32,
+            _c_vp,
+        ],
+    ),
+    (
         "pagedkv_kv_write_prefill",
         ctypes.c_int,
         [

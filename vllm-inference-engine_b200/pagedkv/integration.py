@@ -31,7 +31,7 @@ import torch
 
 from .paged_attention import (
     copy_blocks,
-    kv_append,
+    kv_append_rope,
     kv_write_prefill,
     pad_block_tables,
     paged_attention_decode,
@@ -139,8 +139,8 @@ def paged_decode_attention_forward(
     **kwargs: Any,
 ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
     """Decode-step replacement for ``Qwen2Attention.forward`` (reference
-    integration.py:65-176): projections, RoPE, KV append through the slot
-    mapping (one launch per layer), batched paged attention, o_proj."""
+    integration.py:65-176): projections, RoPE fused with the KV append through
+    the slot mapping (one launch per layer), batched paged attention, o_proj."""
     ctx = getattr(self, "_paged_attention_context", None)
     if ctx is None or not ctx.is_decode:
         orig_forward = getattr(self, "_orig_attention_forward", None)
@@ -154,25 +154,29 @@ def paged_decode_attention_forward(
             )
         raise RuntimeError("No fallback forward method found on attention module.")
 
-    from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
-
     layer_idx = self.layer_idx
     input_shape = hidden_states.shape[:-1]
     hidden_shape = (*input_shape, -1, self.head_dim)
-    query_states = self.q_proj(hidden_states).view(hidden_shape).transpose(1, 2)
-    key_states = self.k_proj(hidden_states).view(hidden_shape).transpose(1, 2)
-    value_states = self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
-    cos, sin = position_embeddings
-    query_states, key_states = apply_rotary_pos_emb(query_states, key_states, cos, sin)
+    # [B, 1, H * D] -> [B, H, D] views (one decode token per sequence)
+    query_states = self.q_proj(hidden_states).view(hidden_shape)[:, 0]
+    key_states = self.k_proj(hidden_states).view(hidden_shape)[:, 0]
+    value_states = self.v_proj(hidden_states).view(hidden_shape)[:, 0]
+    cos, sin = position_embeddings  # [B, 1, D]
     scale = self.scaling if hasattr(self, "scaling") else 1.0 / math.sqrt(self.head_dim)
 
     pool = ctx.pool
     k_cache = pool.k_cache[layer_idx]
     v_cache = pool.v_cache[layer_idx]
-    # [B, Hkv, 1, D] -> [B, Hkv, D] (views; the append takes strides)
-    kv_append(key_states.squeeze(2), value_states.squeeze(2), k_cache, v_cache, ctx.slot_mapping)
+    # RoPE on q and k fused with the append of k and v through the slot
+    # mapping: one launch instead of the rotary tensor ops plus the append.
+    bsz = query_states.shape[0]
+    cos2 = cos.reshape(-1, cos.shape[-1])  # [B, 1, D] (or a broadcast [1, 1, D]) -> rows
+    sin2 = sin.reshape(-1, sin.shape[-1])
+    if cos2.shape[0] != bsz:
+        cos2, sin2 = cos2.expand(bsz, -1), sin2.expand(bsz, -1)
+    q_rot = kv_append_rope(query_states, key_states, value_states, cos2, sin2, k_cache, v_cache, ctx.slot_mapping)
     attn_output = paged_attention_decode_batched(
-        q=query_states.squeeze(2),
+        q=q_rot,
         k_cache=k_cache,
         v_cache=v_cache,
         block_tables=ctx.padded_block_tables,

@@ -407,6 +407,71 @@ def copy_blocks(
     _debug_check(dev, "copy_blocks")
 
 
+def kv_append_rope(
+    q: torch.Tensor,             # [num_tokens, num_q_heads, head_dim]
+    k_new: torch.Tensor,         # [num_tokens, num_kv_heads, head_dim]
+    v_new: torch.Tensor,         # [num_tokens, num_kv_heads, head_dim]
+    cos: torch.Tensor,           # [num_tokens, head_dim] (or [num_tokens, 1, head_dim])
+    sin: torch.Tensor,
+    k_cache: torch.Tensor,       # [num_blocks, block_size, num_kv_heads, head_dim]
+    v_cache: torch.Tensor,
+    slot_mapping: torch.Tensor,  # [num_tokens] int64
+    q_out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Rotary embedding of q and k fused with the KV append, in one launch.
+
+    Returns ``rope(q)`` (in ``q_out`` when given; it may be ``q`` itself) and
+    writes ``rope(k_new)`` / ``v_new`` into the pool slots, with rope(x) =
+    ``x * cos + rotate_half(x) * sin`` rounded exactly as transformers'
+    ``apply_rotary_pos_emb`` tensor ops (the reference decode forward,
+    paged_attention_integration.py:108-109, then the append of :150-160).
+    """
+    for t in (q, k_new, v_new, cos, sin, k_cache, v_cache, slot_mapping):
+        assert t.is_cuda and t.device == k_cache.device
+    dt = k_cache.dtype
+    assert dt in _DTYPES and v_cache.dtype == dt
+    assert q.dtype == dt and k_new.dtype == dt and v_new.dtype == dt and cos.dtype == dt and sin.dtype == dt
+    assert slot_mapping.dtype == torch.int64
+    assert k_cache.is_contiguous() and v_cache.is_contiguous() and v_cache.shape == k_cache.shape
+    num_blocks, block_size, hkv, d = k_cache.shape
+    assert d % 16 == 0, "head_dim must be a multiple of 16"
+    q3 = q if q.dim() == 3 else q.reshape(q.shape[0], -1, d)
+    k3 = k_new.reshape(-1, hkv, d)
+    v3 = v_new.reshape(-1, hkv, d)
+    n, hq = q3.shape[0], q3.shape[1]
+    c2 = cos.reshape(n, d) if cos.dim() != 2 else cos
+    s2 = sin.reshape(n, d) if sin.dim() != 2 else sin
+    assert k3.shape[0] == n and v3.shape[0] == n and slot_mapping.numel() == n and c2.shape == (n, d)
+    if q_out is None:
+        q_out = torch.empty((n, hq, d), dtype=dt, device=k_cache.device)
+    assert q_out.shape == (n, hq, d) and q_out.dtype == dt and q_out.stride(-1) == 1
+    if n == 0:
+        return q_out
+    fix = lambda t: t if t.stride(-1) == 1 else t.contiguous()
+    q3, k3, v3 = fix(q3), fix(k3), fix(v3)
+    if c2.stride() != s2.stride() or c2.stride(-1) != 1:
+        c2, s2 = c2.contiguous(), s2.contiguous()
+    slots = slot_mapping.reshape(-1)
+    if not slots.is_contiguous():
+        slots = slots.contiguous()
+    dev = k_cache.device
+    guard = _device_guard(dev)
+    with guard if guard is not None else _NullCtx():
+        rc = _native.lib().pagedkv_kv_append_rope(
+            q_out.data_ptr(), q_out.stride(0), q_out.stride(1),
+            q3.data_ptr(), q3.stride(0), q3.stride(1), hq,
+            k_cache.data_ptr(), v_cache.data_ptr(),
+            k3.data_ptr(), k3.stride(0), k3.stride(1),
+            v3.data_ptr(), v3.stride(0), v3.stride(1),
+            c2.data_ptr(), s2.data_ptr(), c2.stride(0),
+            slots.data_ptr(), n, hkv, d, num_blocks, block_size, _DTYPES[dt],
+            _stream_handle(dev),
+        )
+    _native.check(rc, "pagedkv_kv_append_rope")
+    _debug_check(dev, "kv_append_rope")
+    return q_out
+
+
 def kv_write_prefill(
     k_srcs: Sequence[torch.Tensor],
     v_srcs: Sequence[torch.Tensor],
