@@ -680,13 +680,131 @@ def run_ours(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---- config 5: full-model decode under continuous batching ------------------
+def run_model(args) -> None:
+    """Config 5: a random-init Qwen2.5-0.5B-architecture model (24 layers, 896
+    hidden, 14/2 heads, MLP 4864, vocab 151936, fp16) served by the continuous-
+    batching decode runner over a seeded Poisson trace (per GPU: ``--requests``
+    at ``--rate`` req/s, prompts U[64, 1024] random ids, 128 output tokens,
+    greedy). Reports decode tokens/s (all GPUs) and latency figures."""
+    import numpy as np
+    from pagedkv.decode_runner import PagedDecodeRunner, random_qwen2
+
+    dist, rank, world, local = _dist_setup(args)
+    dev = torch.device("cuda", local)
+    model = random_qwen2(device=dev, seed=0)
+    block_size = 16
+    block_bytes = 2 * model.config.num_hidden_layers * block_size * model.config.num_key_value_heads * 64 * 2
+    num_blocks = min(int(args.kv_budget_gb * 1e9) // block_bytes, (2**31 - 1) // block_size)
+    runner = PagedDecodeRunner(model, num_blocks=num_blocks, block_size=block_size, max_batch=256,
+                               max_seq_len=1024 + 128)
+    rng = np.random.default_rng(5000 + rank)
+    n_req = args.requests
+    arrivals = np.cumsum(rng.exponential(1.0 / args.rate, n_req))
+    prompt_lens = rng.integers(64, 1025, n_req)
+    vocab = model.config.vocab_size
+    prompts = [rng.integers(0, vocab, int(L)).tolist() for L in prompt_lens]
+    out_tokens = 128
+
+    # warm-up: graphs for every bucket and one prefill, outside the timed trace
+    runner.warm_prefill(1024)
+    warm = [runner.prefill(prompts[i % n_req][:64], 2) for i in range(2)]
+    for b in (1, 2, 4, 8, 16, 32, 64, 128, 256):
+        runner._graph_for(b)
+    runner.decode_step(warm)
+    for s_ in warm:
+        runner.release(s_)
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+
+    waiting = list(range(n_req))
+    running = []
+    ttft, finish, decode_time, decode_steps, prefill_time = [], [], 0.0, 0, 0.0
+    t0 = time.perf_counter()
+    while waiting or running:
+        now = time.perf_counter() - t0
+        admitted = 0
+        while (waiting and arrivals[waiting[0]] <= now and len(running) < runner.max_batch
+               and runner.can_admit(int(prompt_lens[waiting[0]]), out_tokens)):
+            i = waiting.pop(0)
+            tp = time.perf_counter()
+            seq = runner.prefill(prompts[i], out_tokens)
+            torch.cuda.synchronize(dev)
+            prefill_time += time.perf_counter() - tp
+            seq.arrival = arrivals[i]
+            ttft.append(time.perf_counter() - t0 - arrivals[i])
+            running.append(seq)
+            admitted += 1
+            if admitted >= 8:  # keep decoding between bursts of arrivals
+                break
+        if running:
+            td = time.perf_counter()
+            runner.decode_step(running)
+            decode_time += time.perf_counter() - td
+            decode_steps += 1
+            still = []
+            for s_ in running:
+                if s_.done:
+                    finish.append(time.perf_counter() - t0 - s_.arrival)
+                    runner.release(s_)
+                else:
+                    still.append(s_)
+            running = still
+        elif waiting:
+            time.sleep(max(0.0, min(0.01, arrivals[waiting[0]] - (time.perf_counter() - t0))))
+    elapsed = time.perf_counter() - t0
+    gen = n_req * out_tokens
+    elapsed_max = _max_over_ranks(dist, elapsed, dev)
+    gen_all = _sum_over_ranks(dist, float(gen), dev)
+    dec_tok = n_req * (out_tokens - 1)  # the first token of each request comes from its prefill
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": "decode tokens/s",
+        "value": round(gen_all / elapsed_max, 1),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic",
+        "config": {
+            "workload": "cfg5: random-init Qwen2.5-0.5B architecture (24 layers, hidden 896, 14q/2kv, head_dim 64, "
+                        "MLP 4864, vocab 151936, tied embeddings, fp16), continuous batching over a seeded Poisson "
+                        f"trace per GPU: {n_req} requests at {args.rate} req/s, prompts U[64,1024] random ids, "
+                        f"{out_tokens} output tokens, greedy",
+            "kv_budget_gb": args.kv_budget_gb,
+            "num_blocks": num_blocks,
+            "parallelism": f"dp{world}: one runner, pool and trace per GPU",
+        },
+        "elapsed_s": round(elapsed_max, 3),
+        "generated_tokens": int(gen_all),
+        "decode_only_tokens_per_s": round(dec_tok / decode_time, 1) if decode_time > 0 else None,
+        "decode_steps": decode_steps,
+        "mean_decode_step_ms": round(1e3 * decode_time / max(1, decode_steps), 3),
+        "prefill_s": round(prefill_time, 3),
+        "ttft_ms_p50": round(1e3 * float(np.median(ttft)), 2),
+        "request_latency_s_p50": round(float(np.median(finish)), 3),
+        "timing": "wall clock of the trace replay on rank 0 (max over ranks); decode steps are CUDA-graph replays",
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg4-cow"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg4-cow", "cfg5"], default="cfg2")
+    ap.add_argument("--requests", type=int, default=2000, help="cfg5: requests per GPU")
+    ap.add_argument("--rate", type=float, default=32.0, help="cfg5: Poisson arrival rate per GPU (req/s)")
+    ap.add_argument("--kv-budget-gb", type=float, default=60.0, help="cfg5: KV pool budget per GPU")
     ap.add_argument("--gqa", type=int, default=7, help="GQA group for --workload cfg3 (1, 2, 4 or 7)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -695,6 +813,8 @@ def main() -> None:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference_arm(args)
+    elif args.workload == "cfg5":
+        run_model(args)
     else:
         run_ours(args)
 
