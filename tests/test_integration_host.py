@@ -9,7 +9,7 @@ import torch
 
 import cases
 from oracle import paged_ref
-from pagedkv import integration
+from pagedkv import integration, prefix_index
 
 REFERENCE = Path("/root/reference")
 
@@ -105,7 +105,13 @@ def test_install_replaces_reference_symbols_and_uninstall_restores():
         assert integ.paged_decode_attention_forward is integration.paged_decode_attention_forward
         assert pa.naive_reference_paged_attention.__module__ == "engine.kernels.paged_attention"
         assert integ.KernelPagedManualDecode._copy_prefill_kv is integration.copy_prefill_kv
+        from engine.memory.block_allocator import BlockAllocator
+
+        assert BlockAllocator.lookup_prefix is prefix_index.lookup_prefix
     finally:
         integration.uninstall(saved)
     assert integ.KernelPagedManualDecode._copy_prefill_kv is not integration.copy_prefill_kv
+    from engine.memory.block_allocator import BlockAllocator
+
+    assert BlockAllocator.lookup_prefix is not prefix_index.lookup_prefix
     assert (pa.paged_attention_decode_batched, integ.paged_attention_decode_batched, integ.PagedAttentionContext) == before

@@ -29,6 +29,7 @@ from typing import Any, Callable, Iterable, List, Optional, Sequence, Tuple, Uni
 
 import torch
 
+from . import prefix_index
 from .paged_attention import (
     copy_blocks,
     kv_append_rope,
@@ -302,13 +303,16 @@ _INSTALL_NAMES_KERNELS = (
 )
 
 
-def install(paged_attention_module: Any = None, integration_module: Any = None) -> dict:
+def install(paged_attention_module: Any = None, integration_module: Any = None,
+            allocator_module: Any = None) -> dict:
     """Install the B200 path into the reference's modules.
 
-    ``paged_attention_module`` defaults to ``engine.kernels.paged_attention``
-    and ``integration_module`` to ``engine.kernels.paged_attention_integration``
-    (imported if not given). Returns the replaced symbols for :func:`uninstall`.
-    The reference's ``naive_reference_paged_attention`` is left untouched.
+    ``paged_attention_module`` defaults to ``engine.kernels.paged_attention``,
+    ``integration_module`` to ``engine.kernels.paged_attention_integration`` and
+    ``allocator_module`` to ``engine.memory.block_allocator`` (imported if not
+    given; the allocator is skipped when it cannot be imported). Returns the
+    replaced symbols for :func:`uninstall`. The reference's
+    ``naive_reference_paged_attention`` is left untouched.
     """
     if paged_attention_module is None:
         import importlib
@@ -340,10 +344,25 @@ def install(paged_attention_module: Any = None, integration_module: Any = None) 
         saved[(runner_cls, "_copy_prefill_kv")] = runner_cls.__dict__.get(
             "_copy_prefill_kv", getattr(runner_cls, "_copy_prefill_kv"))
         setattr(runner_cls, "_copy_prefill_kv", copy_prefill_kv)
+    # The allocator's prefix lookup: a per-parent index instead of a full scan
+    # of the cache per block (block_allocator.py:231-252).
+    if allocator_module is None:
+        try:
+            import importlib
+
+            allocator_module = importlib.import_module("engine.memory.block_allocator")
+        except ImportError:
+            allocator_module = None
+    alloc_cls = getattr(allocator_module, "BlockAllocator", None)
+    if alloc_cls is not None and "lookup_prefix" in alloc_cls.__dict__:
+        saved[("prefix_index", alloc_cls)] = prefix_index.install(alloc_cls)
     return saved
 
 
 def uninstall(saved: dict) -> None:
     """Undo :func:`install`."""
     for (mod, name), fn in saved.items():
-        setattr(mod, name, fn)
+        if mod == "prefix_index":
+            prefix_index.uninstall(fn)
+        else:
+            setattr(mod, name, fn)
