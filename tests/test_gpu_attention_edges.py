@@ -81,3 +81,14 @@ def test_back_to_back_launches_of_changing_shapes(cuda_ready):
         out = pagedkv.paged_attention_decode_batched(q, k, v, tables, lens, 0.125)
         torch.testing.assert_close(out.float().cpu(), refs[i], atol=ATOL, rtol=RTOL)
     assert pagedkv.read_error_flags(dev) == 0
+
+
+@pytest.mark.parametrize("d,g", [(128, 17), (128, 24), (128, 32), (32, 1), (32, 5), (32, 8), (64, 16)])
+def test_wide_groups_and_head_dim_32_on_tensor_cores(cuda_ready, d, g):
+    """GQA groups up to 32 at head_dim 128 (one kv head per tile, 32 query
+    columns) and head_dim 32 (four kv heads per tile, block-diagonal Q)."""
+    hkv = 3 if d == 32 else 2  # head_dim 32: a group of four kv heads, the last one partly empty
+    lens = [1, 100, 128, 129, 1500]
+    q, k, v, tables, lists, lens_t = _random_case(d * 100 + g, len(lens), g * hkv, hkv, d, 16, lens, q_scale=4.0)
+    _check_vs_oracle(cuda_ready, q, k, v, tables, lists, lens_t, 1 / math.sqrt(d))
+    assert pagedkv.last_decode_launch_info()[1] == "tc"

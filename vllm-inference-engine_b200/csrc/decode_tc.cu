@@ -537,8 +537,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         const int n = rem >> 3, ch = rem & 7;
         const int hl = n / GP, g = n - hl * GP;
         const int kv = q.hg * H + hl;
-        const bool in = hl < H && g < p.group && kv < p.hkv && (H == 1 || xh == hl);
-        const int d = (H == 1 ? xh * 64 : 0) + ch * 8;
+        // Element e of the 128-wide row belongs to kv head e / D of the group:
+        // query column n (head hl) is nonzero only on its own head's D elements.
+        const int e = xh * 64 + ch * 8;
+        const bool in = hl < H && g < p.group && kv < p.hkv && e / D == hl;
+        const int d = e - hl * D;
         const T *src = reinterpret_cast<const T *>(p.q) +
                        (in ? (int64_t)q.seq * p.q_ss + (int64_t)(kv * p.group + g) * p.q_sh + d : 0);
         const uint32_t addr = qbuf + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
@@ -884,8 +887,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     // ---------------------------------------- correction / epilogue: O -> output
     const int q4 = warp & 3;         // TMEM lane quarter of this warp
     const int row = q4 * 32 + lane;  // TMEM lane: (kv head, dim) row of O
-    const int hl = H == 2 ? (row >> 6) : 0;
-    const int dim = H == 2 ? (row & 63) : row;
+    const int hl = row / D;   // kv head of the group this O row belongs to
+    const int dim = row % D;
     const uint32_t tl = tmem + ((uint32_t)(q4 * 32) << 16);
     const int HQS = H * p.group;  // query heads per segment
     uint32_t gt = 0, pi = 0;
@@ -1057,6 +1060,7 @@ TcPlan make_plan(int32_t num_seqs, int32_t hq, int32_t hkv, int32_t head_dim, in
   pl.H = 128 / head_dim;
   const int G = hq / hkv;
   pl.GP = round_up(G, 8);
+  if (pl.H == 1 && pl.GP > 16) pl.GP = 32;  // one kv head per tile: columns 17..32 share the N = 32 variant
   pl.N = round_up(pl.H * pl.GP, 16);
   pl.stages = pl.N <= 16 ? 3 : 2;
   pl.head_groups = (hkv + pl.H - 1) / pl.H;
@@ -1187,6 +1191,8 @@ cudaError_t dispatch_tc(const TcPlan &pl, const CUtensorMap &mk, const CUtensorM
   if (pl.H == 2 && pl.GP == 16) return launch_tc<T, 2, 16, 32, 2, 2>(mk, mv, tp, pl.grid, stream);
   if (pl.H == 1 && pl.GP == 8) return launch_tc<T, 1, 8, 16, 3, 3>(mk, mv, tp, pl.grid, stream);
   if (pl.H == 1 && pl.GP == 16) return launch_tc<T, 1, 16, 16, 3, 3>(mk, mv, tp, pl.grid, stream);
+  if (pl.H == 1 && pl.GP == 32) return launch_tc<T, 1, 32, 32, 2, 2>(mk, mv, tp, pl.grid, stream);
+  if (pl.H == 4 && pl.GP == 8) return launch_tc<T, 4, 8, 32, 2, 2>(mk, mv, tp, pl.grid, stream);
   return cudaErrorInvalidValue;
 }
 
@@ -1202,10 +1208,20 @@ extern "C" int pagedkv_trace_read(unsigned long long *host, size_t count) {
 bool tc_eligible(int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size) {
   if (num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return false;
   const int G = num_q_heads / num_kv_heads;
-  if (head_dim != 64 && head_dim != 128) return false;
-  // Every group size 1..16: the pipeline is bound by HBM, not by the MMA
-  // shape, and measured 1.1-2.7x faster than the CUDA-core kernel at G = 1, 2.
-  if (G < 1 || G > 16) return false;
+  // A tile row is 128 elements: 128 / head_dim kv heads side by side, and their
+  // query columns (padded groups) must fit the N <= 32 MMA width. Every such
+  // group size runs here: the pipeline is bound by HBM, not by the MMA shape
+  // (measured 1.1-2.7x faster than the CUDA-core kernel at G = 1, 2).
+  if (G < 1) return false;
+  if (head_dim == 128) {
+    if (G > 32) return false;
+  } else if (head_dim == 64) {
+    if (G > 16) return false;
+  } else if (head_dim == 32) {
+    if (G > 8) return false;
+  } else {
+    return false;
+  }
   if (block_size < 8 || block_size > 128 || (block_size & (block_size - 1)) != 0) return false;
   return true;
 }
