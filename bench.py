@@ -9,7 +9,7 @@ the KV append of 256 new tokens through a slot mapping, then batched decode
 attention over all 256 contexts (which include the appended token).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload cfg2|cfg3|cfg4|cfg4-cow] [--gqa G]
+                  [--workload cfg2|cfg3|cfg4|cfg4-cow|cfg5|ops] [--gqa G]
 
 Extra workloads (not the headline): ``cfg3`` = BASELINE config 3 (head_dim
 128, 8 kv heads, GQA G, 128 sequences with log-uniform lengths 16..8192,
@@ -596,7 +596,60 @@ def run_ours(args) -> None:
     for _ in range(max(3, args.warmup)):
         e2e_step()
     torch.cuda.synchronize(dev)
-    e2e_ms = _max_over_ranks(dist, timed(e2e_step, args.steps), dev) / args.steps
+    serial_ms = _max_over_ranks(dist, timed(e2e_step, args.steps), dev) / args.steps
+    serial_out = h_out.clone()
+
+    # Pipelined: the same calls and copies, with step i+1's inputs copied on a
+    # side stream into the other of two device buffers while step i computes,
+    # and step i's output read back on a second side stream (the two copy
+    # engines run in parallel with the SMs). Every step still moves all of its
+    # inputs host->device and its output device->host inside the timed region.
+    d_in2 = [d_in, torch.empty_like(d_in)]
+    views2 = [views, [d_in2[1][o : o + sz].view(t.dtype).view(t.shape) for t, o, sz in zip(parts, offs, sizes)]]
+    h_out2 = [h_out, torch.empty_like(h_out).pin_memory()]
+    s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    free = [torch.cuda.Event(), torch.cuda.Event()]
+    ready = [torch.cuda.Event(), torch.cuda.Event()]
+    it = [0]
+
+    def e2e_pipelined_step():
+        i = it[0] % 2
+        it[0] += 1
+        s_h2d.wait_event(free[i])  # the step that last read this buffer is done
+        torch.cuda.set_stream(s_h2d)
+        d_in2[i].copy_(h_in, non_blocking=True)
+        torch.cuda.set_stream(stream)
+        ready[i].record(s_h2d)
+        stream.wait_event(ready[i])
+        dq, dk, dv, ds, dt, dl = views2[i]
+        if pairs is not None:
+            pagedkv.copy_blocks([kc], [vc], pairs)
+        pagedkv.kv_append(dk, dv, kc, vc, ds)
+        o = pagedkv.paged_attention_decode_batched(dq, kc, vc, dt, dl, scale)
+        free[i].record(stream)
+        s_d2h.wait_event(free[i])
+        torch.cuda.set_stream(s_d2h)
+        h_out2[i].copy_(o, non_blocking=True)
+        torch.cuda.set_stream(stream)
+        o.record_stream(s_d2h)
+
+    def e2e_pipelined(n):
+        # the side streams start after the region's opening event and the
+        # launch stream waits for both before its closing event
+        s_h2d.wait_stream(stream)
+        s_d2h.wait_stream(stream)
+        for _ in range(n):
+            e2e_pipelined_step()
+        stream.wait_stream(s_h2d)
+        stream.wait_stream(s_d2h)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            e2e_pipelined_step()
+        stream.wait_stream(s_d2h)
+    torch.cuda.synchronize(dev)
+    e2e_ms = _max_over_ranks(dist, timed(lambda: e2e_pipelined(args.steps), 1), dev) / args.steps
+    pipe_match = bool(torch.equal(h_out2[(it[0] - 1) % 2], serial_out))
     e2e_value = world * step_bytes / (e2e_ms * 1e-3) / 1e9
 
     cpu = None
@@ -672,6 +725,10 @@ def run_ours(args) -> None:
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
             "api": "pagedkv public API; step inputs staged in one pinned buffer, one H2D and one D2H copy per step",
+            "overlap": "step i+1's H2D and step i-1's D2H run on side streams (double-buffered) while step i computes",
+            "serial_ms_per_step": round(serial_ms, 5),
+            "serial_value": round(world * step_bytes / (serial_ms * 1e-3) / 1e9, 2),
+            "pipelined_output_matches_serial": pipe_match,
         },
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
@@ -795,13 +852,123 @@ def run_model(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---- the pool-write kernels on their own -------------------------------------
+def run_ops(args) -> None:
+    """The four pool-write kernels (decode append, fused RoPE + append,
+    copy-on-write block copy, prefill write), each timed at the size one decode
+    layer-step gives it (latency-bound: microseconds) and at a bulk size whose
+    traffic exceeds L2 (bandwidth-bound: GB/s against the measured HBM peak).
+    CUDA-graph replay of one launch, K replays between CUDA events."""
+    import pagedkv
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("--workload ops runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(7)
+    stream = torch.cuda.current_stream(dev)
+    pp = ROOT / "MEASURED_PEAKS.json"
+    peak = float(json.loads(pp.read_text()).get("hbm_gbs", 6650.0)) if pp.exists() else 6650.0
+
+    def rnd(*shape):
+        return torch.randn(shape, generator=g, device=dev, dtype=torch.float16)
+
+    def distinct_slots(n, num_blocks, bs):
+        return torch.randperm(num_blocks * bs, generator=g, device=dev)[:n].contiguous()
+
+    def time_graph(fn, steps):
+        fn()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        del graph
+        return a.elapsed_time(b) / steps * 1e3  # us
+
+    results = {}
+
+    def record(name, us, nbytes, shape):
+        gbs = nbytes / (us * 1e-6) / 1e9
+        results[name] = {"us": round(us, 3), "bytes": int(nbytes), "GB/s": round(gbs, 1),
+                         "frac_of_measured_hbm": round(gbs / peak, 4), "shape": shape}
+
+    steps = min(args.steps, 500)
+    # decode append (paged_attention_integration.py:150-160) at config 2 and in bulk
+    for tag, n, hkv, d, nb in (("decode", 256, 2, 64, 40960), ("bulk", 65536, 8, 128, 8192)):
+        kc, vc = rnd(nb, 16, hkv, d), rnd(nb, 16, hkv, d)
+        kn, vn = rnd(n, hkv, d), rnd(n, hkv, d)
+        sl = distinct_slots(n, nb, 16)
+        us = time_graph(lambda: pagedkv.kv_append(kn, vn, kc, vc, sl), steps)
+        record(f"kv_append_{tag}", us, n * hkv * d * 2 * 2 * 2 + n * 8, f"{n} tokens x {hkv}x{d}")
+        del kc, vc, kn, vn
+    # fused RoPE + append at the Qwen2.5-0.5B attention shape (14 q / 2 kv heads, head_dim 64)
+    for tag, n, nb in (("decode", 256, 40960), ("bulk", 262144, 40960)):
+        hq, hkv, d = 14, 2, 64
+        kc, vc = rnd(nb, 16, hkv, d), rnd(nb, 16, hkv, d)
+        q, kn, vn = rnd(n, hq, d), rnd(n, hkv, d), rnd(n, hkv, d)
+        cos, sin = rnd(n, d), rnd(n, d)
+        qo = torch.empty_like(q)
+        sl = distinct_slots(n, nb, 16)
+        us = time_graph(lambda: pagedkv.kv_append_rope(q, kn, vn, cos, sin, kc, vc, sl, q_out=qo), steps)
+        nbytes = n * d * 2 * (2 * hq + 4 * hkv + 2) + n * 8
+        record(f"kv_append_rope_{tag}", us, nbytes, f"{n} tokens x {hq}q/{hkv}kv x {d}")
+        del kc, vc, q, kn, vn, cos, sin, qo
+    # copy-on-write over 24 layers (config-4 block: 16 x 2 x 64 fp16 = 4 KiB for K and for V)
+    for tag, pairs_n, nb in (("decode", 512, 1024), ("bulk", 8192, 16384)):
+        layers = 24
+        kcs = [rnd(nb, 16, 2, 64) for _ in range(layers)]
+        vcs = [rnd(nb, 16, 2, 64) for _ in range(layers)]
+        perm = torch.randperm(nb, generator=g, device=dev)
+        mapping = torch.stack([perm[:pairs_n], perm[pairs_n : 2 * pairs_n]], dim=1).contiguous()
+        us = time_graph(lambda: pagedkv.copy_blocks(kcs, vcs, mapping), steps)
+        block = 16 * 2 * 64 * 2
+        record(f"copy_blocks_{tag}", us, layers * pairs_n * block * 2 * 2 + pairs_n * 16,
+               f"{pairs_n} pairs x {layers} layers x 2 x {block} B")
+        del kcs, vcs
+    # prefill write of one prompt into every layer's pool (fp16 sources)
+    for tag, ntok in (("prompt", 1000), ("bulk", 65536)):
+        layers, hkv, d, bs = 24, 2, 64, 16
+        nw = (ntok + bs - 1) // bs
+        nb = nw + 64
+        kcs = [rnd(nb, bs, hkv, d) for _ in range(layers)]
+        vcs = [rnd(nb, bs, hkv, d) for _ in range(layers)]
+        ks = [rnd(ntok, hkv, d) for _ in range(layers)]
+        vs = [rnd(ntok, hkv, d) for _ in range(layers)]
+        ids = torch.randperm(nb, generator=g, device=dev)[:nw].contiguous()
+        us = time_graph(lambda: pagedkv.kv_write_prefill(ks, vs, kcs, vcs, ids, ntok), min(steps, 200))
+        nbytes = layers * 2 * (ntok * hkv * d * 2 + nw * bs * hkv * d * 2)
+        record(f"kv_write_prefill_{tag}", us, nbytes, f"{ntok}-token prompt x {layers} layers, {hkv}x{d}")
+        del kcs, vcs, ks, vs
+    line = {
+        "metric": "pool-write kernels: us per launch and GB/s",
+        "workload": "ops",
+        "n_gpus": 1,
+        "steps": steps,
+        "warmup": args.warmup,
+        "peak_hbm_gbs": peak,
+        "timing": "CUDA-graph replay of one launch, CUDA events on the launch stream; bulk sizes exceed L2",
+        "data": "synthetic",
+        "ops": results,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg4-cow", "cfg5"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg4-cow", "cfg5", "ops"], default="cfg2")
     ap.add_argument("--requests", type=int, default=2000, help="cfg5: requests per GPU")
     ap.add_argument("--rate", type=float, default=32.0, help="cfg5: Poisson arrival rate per GPU (req/s)")
     ap.add_argument("--kv-budget-gb", type=float, default=60.0, help="cfg5: KV pool budget per GPU")
@@ -815,6 +982,8 @@ def main() -> None:
         run_reference_arm(args)
     elif args.workload == "cfg5":
         run_model(args)
+    elif args.workload == "ops":
+        run_ops(args)
     else:
         run_ours(args)
 

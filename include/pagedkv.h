@@ -134,7 +134,8 @@ int pagedkv_kv_append(
  * pair p and layer l,
  *   k_cache[l][block_mapping[2p + 1]] = k_cache[l][block_mapping[2p]]
  * and the same for V, bit-exact. k_cache_ptrs / v_cache_ptrs are DEVICE arrays
- * of num_layers pool base pointers; block_mapping is a device int64 [num_pairs, 2]
+ * of num_layers pool base pointers (16-byte aligned, as every allocation of the
+ * CUDA caching allocators is); block_mapping is a device int64 [num_pairs, 2]
  * (src, dst) array. Destinations must be distinct and must not appear as a
  * source in the same call. block_bytes = block_size * num_kv_heads * head_dim
  * * element size. One launch covers all layers, K and V.

@@ -98,6 +98,31 @@ def test_copy_blocks_all_layers_vs_oracle(cuda_ready, dtype):
         assert np.array_equal(_bits(a), b)
 
 
+@pytest.mark.parametrize(
+    "layers,nb,bs,hkv,d,pairs",
+    [
+        (3, 32, 3, 1, 8, 7),            # 48-byte blocks: 3 chunks, most lanes idle
+        (2, 24, 64, 8, 128, 9),         # 128 KiB blocks: many unrolled rounds per warp
+        (1, 8192, 16, 2, 64, 4000),     # more (pair, layer) units than the grid's warps
+        (48, 1280, 16, 2, 64, 600),     # 28 800 units over 48 layers
+    ],
+)
+def test_copy_blocks_shapes_and_grid_stride(cuda_ready, layers, nb, bs, hkv, d, pairs):
+    g = torch.Generator().manual_seed(layers * 1000 + pairs)
+    ks = [torch.randn(nb, bs, hkv, d, generator=g).half() for _ in range(layers)]
+    vs = [torch.randn(nb, bs, hkv, d, generator=g).half() for _ in range(layers)]
+    perm = torch.randperm(nb, generator=g)
+    mapping = torch.stack([perm[:pairs], perm[pairs : 2 * pairs]], dim=1).contiguous()
+    kd = [t.to(cuda_ready) for t in ks]
+    vd = [t.to(cuda_ready) for t in vs]
+    pagedkv.copy_blocks(kd, vd, mapping.to(cuda_ready))
+    kr = [_bits(t).copy() for t in ks]
+    vr = [_bits(t).copy() for t in vs]
+    paged_ref.copy_blocks_ref(kr, vr, mapping.numpy())
+    for a, b in zip(kd + vd, kr + vr):
+        assert np.array_equal(_bits(a), b)
+
+
 def test_copy_blocks_out_of_range_flagged(cuda_ready):
     kc = [torch.zeros(4, 16, 2, 64, dtype=torch.float16, device=cuda_ready)]
     vc = [torch.zeros(4, 16, 2, 64, dtype=torch.float16, device=cuda_ready)]

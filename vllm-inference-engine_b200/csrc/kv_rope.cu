@@ -47,7 +47,9 @@ __device__ __forceinline__ float rope_elem(float a, float c, float b, float s) {
   return p1 + p2;  // rounded to T by the store
 }
 
-template <typename T, bool VEC>
+// I is the flat work index type: 32-bit whenever the launch has fewer than
+// 2^32 items (the divisions below are then the cheap 32-bit ones), else 64-bit.
+template <typename T, bool VEC, typename I>
 __global__ void __launch_bounds__(256)
 kv_append_rope_kernel(const RopeParams rp, unsigned int *err) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -55,13 +57,13 @@ kv_append_rope_kernel(const RopeParams rp, unsigned int *err) {
   const int half = rp.head_dim >> 1;
   const int cph = half >> 3;                          // chunk pairs per row
   const int rows_per_tok = rp.hq + 2 * rp.hkv;        // q rows, k rows, v rows
-  const int64_t total = (int64_t)rp.num_tokens * rows_per_tok * cph;
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t tr = idx / cph;
-    const int c = (int)(idx - tr * cph);
-    const int tok = (int)(tr / rows_per_tok);
-    const int r = (int)(tr - (int64_t)tok * rows_per_tok);
+  const I per_tok = (I)rows_per_tok * cph;
+  const I total = (I)rp.num_tokens * per_tok;
+  for (I idx = (I)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (I)gridDim.x * blockDim.x) {
+    const int tok = (int)(idx / per_tok);
+    const int rem = (int)(idx - (I)tok * per_tok);
+    const int r = rem / cph;
+    const int c = rem - r * cph;
     const int lo = c * 8, hi = half + c * 8;
     const T *src;
     T *dst;
@@ -127,8 +129,14 @@ cudaError_t launch_typed(const RopeParams &rp, bool vec, unsigned int *err, cuda
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (vec) return cudaLaunchKernelEx(&cfg, kv_append_rope_kernel<T, true>, rp, err);
-  return cudaLaunchKernelEx(&cfg, kv_append_rope_kernel<T, false>, rp, err);
+  // total + gridDim * blockDim must not wrap the 32-bit index
+  const bool narrow = total + (int64_t)cfg.gridDim.x * threads < (int64_t(1) << 32);
+  if (narrow) {
+    if (vec) return cudaLaunchKernelEx(&cfg, kv_append_rope_kernel<T, true, uint32_t>, rp, err);
+    return cudaLaunchKernelEx(&cfg, kv_append_rope_kernel<T, false, uint32_t>, rp, err);
+  }
+  if (vec) return cudaLaunchKernelEx(&cfg, kv_append_rope_kernel<T, true, int64_t>, rp, err);
+  return cudaLaunchKernelEx(&cfg, kv_append_rope_kernel<T, false, int64_t>, rp, err);
 }
 
 }  // namespace

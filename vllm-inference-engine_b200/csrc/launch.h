@@ -94,6 +94,6 @@ cudaError_t launch_kv_append_rope(const RopeParams &rp, int dtype, bool vec, uns
 
 cudaError_t launch_copy_blocks(void *const *k_ptrs, void *const *v_ptrs, int32_t num_layers,
                                const int64_t *mapping, int32_t num_pairs, int64_t block_bytes,
-                               int64_t num_blocks, unsigned int *err, cudaStream_t stream);
+                               int64_t num_blocks, int num_sms, unsigned int *err, cudaStream_t stream);
 
 }  // namespace pagedkv

@@ -269,7 +269,7 @@ int pagedkv_copy_blocks(void *const *k_cache_ptrs, void *const *v_cache_ptrs, in
   int rc = device_info(&di);
   if (rc != PAGEDKV_OK) return rc;
   cudaError_t e = launch_copy_blocks(k_cache_ptrs, v_cache_ptrs, num_layers, block_mapping,
-                                     num_pairs, block_bytes, num_blocks, di.err,
+                                     num_pairs, block_bytes, num_blocks, di.num_sms, di.err,
                                      static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "copy_blocks launch");
   return PAGEDKV_OK;

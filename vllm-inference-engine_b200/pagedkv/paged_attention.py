@@ -44,10 +44,9 @@ _ws_sizes: dict[tuple, int] = {}
 _retired_workspaces: list[torch.Tensor] = []
 
 
-def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
+def _workspace(idx: int, nbytes: int) -> torch.Tensor | None:
     if nbytes == 0:
         return None
-    idx = device.index if device.index is not None else torch.cuda.current_device()
     buf = _workspaces.get(idx)
     if buf is None or buf.numel() < nbytes:
         if buf is not None:
@@ -56,13 +55,33 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
         size = max(nbytes, 1 << 20)
         # zero-filled once: the first 8 KiB are completion flags the kernels
         # expect at zero and leave at zero
-        buf = torch.zeros(size, dtype=torch.uint8, device=device)
+        buf = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
         _workspaces[idx] = buf
     return buf
 
 
-def _stream_handle(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+# The current stream's raw handle without building a torch Stream object
+# (about 10x cheaper per call); torch builds without the binding use the
+# public route.
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream_handle(device: torch.device | int) -> int:
+    idx = device if isinstance(device, int) else device.index
+    if idx is None:
+        idx = torch.cuda.current_device()
+    if _raw_stream is not None:
+        return _raw_stream(idx)
+    return torch.cuda.current_stream(idx).cuda_stream
+
+
+def _launch(idx: int, fn, *args) -> int:
+    """Call the C entry ``fn(*args, stream)`` with device ``idx`` current and
+    its current torch stream as the last argument."""
+    if torch.cuda.current_device() == idx:
+        return fn(*args, _stream_handle(idx))
+    with torch.cuda.device(idx):
+        return fn(*args, _stream_handle(idx))
 
 
 def _aligned(t: torch.Tensor) -> bool:
@@ -70,7 +89,8 @@ def _aligned(t: torch.Tensor) -> bool:
 
 
 def _qo_ok(t: torch.Tensor) -> bool:
-    return t.stride(-1) == 1 and _aligned(t) and t.stride(0) % 8 == 0 and t.stride(1) % 8 == 0
+    s0, s1, s2 = t.stride()
+    return s2 == 1 and s0 % 8 == 0 and s1 % 8 == 0 and t.data_ptr() % 16 == 0
 
 
 def _device_guard(device: torch.device):
@@ -115,9 +135,10 @@ def _decode_into(
 ) -> None:
     """Launch decode attention writing into ``out`` ([N, Hq, D])."""
     assert k_cache.is_contiguous() and v_cache.is_contiguous(), "KV pool tensors must be contiguous"
-    assert v_cache.shape == k_cache.shape, "k_cache and v_cache must have the same shape"
+    kshape = k_cache.shape
+    assert v_cache.shape == kshape, "k_cache and v_cache must have the same shape"
     num_seqs, num_q_heads, head_dim = q.shape
-    num_blocks, block_size, num_kv_heads, _ = k_cache.shape
+    num_blocks, block_size, num_kv_heads, _ = kshape
     if num_seqs == 0:
         return
     if block_tables.stride(-1) != 1:
@@ -128,35 +149,35 @@ def _decode_into(
     oo = out if _qo_ok(out) else torch.empty(q.shape, dtype=q.dtype, device=q.device)
     dtype = _DTYPES[q.dtype]
     max_blocks = block_tables.shape[1]
+    idx = q.get_device()
     lib = _native.lib()
-    dev = q.device
-    guard = _device_guard(dev)
-    ctx = guard if guard is not None else _NullCtx()
-    with ctx:
-        key = (dev.index, num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks, dtype)
-        nbytes = _ws_sizes.get(key)
-        if nbytes is None:
-            nbytes = lib.pagedkv_decode_attention_workspace_size(
-                num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks, dtype
-            )
-            _ws_sizes[key] = nbytes
-        ws = _workspace(dev, nbytes)
-        rc = lib.pagedkv_decode_attention(
-            oo.data_ptr(), oo.stride(0), oo.stride(1),
-            qq.data_ptr(), qq.stride(0), qq.stride(1),
-            k_cache.data_ptr(), v_cache.data_ptr(),
-            block_tables.data_ptr(), block_tables.stride(0),
-            seq_lens.data_ptr() if seq_lens is not None else None, int(uniform_seq_len),
-            num_seqs, num_q_heads, num_kv_heads, head_dim,
-            num_blocks, block_size, max_blocks,
-            float(scale), dtype,
-            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
-            _stream_handle(dev),
+    key = (idx, num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks, dtype)
+    nbytes = _ws_sizes.get(key)
+    if nbytes is None:
+        nbytes = lib.pagedkv_decode_attention_workspace_size(
+            num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks, dtype
         )
-    _native.check(rc, "pagedkv_decode_attention")
+        _ws_sizes[key] = nbytes
+    ws = _workspace(idx, nbytes)
+    qs, os_ = qq.stride(), oo.stride()
+    rc = _launch(
+        idx, lib.pagedkv_decode_attention,
+        oo.data_ptr(), os_[0], os_[1],
+        qq.data_ptr(), qs[0], qs[1],
+        k_cache.data_ptr(), v_cache.data_ptr(),
+        block_tables.data_ptr(), block_tables.stride(0),
+        seq_lens.data_ptr() if seq_lens is not None else None, int(uniform_seq_len),
+        num_seqs, num_q_heads, num_kv_heads, head_dim,
+        num_blocks, block_size, max_blocks,
+        float(scale), dtype,
+        ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+    )
+    if rc:
+        _native.check(rc, "pagedkv_decode_attention")
     if oo is not out:
         out.copy_(oo)
-    _debug_check(dev, "paged decode attention")
+    if _DEBUG:
+        _debug_check(q.device, "paged decode attention")
 
 
 class _NullCtx:
@@ -323,34 +344,37 @@ def kv_append(
     assert k_cache.is_contiguous() and v_cache.is_contiguous(), "KV pool tensors must be contiguous"
     assert v_cache.shape == k_cache.shape
     num_blocks, block_size, num_kv_heads, head_dim = k_cache.shape
-    k3 = k_new.reshape(-1, num_kv_heads, head_dim)
-    v3 = v_new.reshape(-1, num_kv_heads, head_dim)
+    row = (num_kv_heads, head_dim)
+    k3 = k_new if k_new.dim() == 3 and k_new.shape[1:] == row else k_new.reshape(-1, num_kv_heads, head_dim)
+    v3 = v_new if v_new.dim() == 3 and v_new.shape[1:] == row else v_new.reshape(-1, num_kv_heads, head_dim)
     num_tokens = k3.shape[0]
     assert v3.shape[0] == num_tokens and slot_mapping.numel() == num_tokens, (
         f"k_new/v_new/slot_mapping disagree on the token count ({num_tokens}, {v3.shape[0]}, {slot_mapping.numel()})"
     )
     if num_tokens == 0:
         return
-    if k3.stride(-1) != 1:
+    ks, vs = k3.stride(), v3.stride()
+    if ks[2] != 1:
         k3 = k3.contiguous()
-    if v3.stride(-1) != 1:
+        ks = k3.stride()
+    if vs[2] != 1:
         v3 = v3.contiguous()
-    slots = slot_mapping.reshape(-1)
+        vs = v3.stride()
+    slots = slot_mapping if slot_mapping.dim() == 1 else slot_mapping.reshape(-1)
     if not slots.is_contiguous():
         slots = slots.contiguous()
-    dev = k_cache.device
-    guard = _device_guard(dev)
-    with guard if guard is not None else _NullCtx():
-        rc = _native.lib().pagedkv_kv_append(
-            k_cache.data_ptr(), v_cache.data_ptr(),
-            k3.data_ptr(), k3.stride(0), k3.stride(1),
-            v3.data_ptr(), v3.stride(0), v3.stride(1),
-            slots.data_ptr(), num_tokens, num_kv_heads, head_dim,
-            num_blocks, block_size, _DTYPES[k_cache.dtype],
-            _stream_handle(dev),
-        )
-    _native.check(rc, "pagedkv_kv_append")
-    _debug_check(dev, "kv_append")
+    rc = _launch(
+        k_cache.get_device(), _native.lib().pagedkv_kv_append,
+        k_cache.data_ptr(), v_cache.data_ptr(),
+        k3.data_ptr(), ks[0], ks[1],
+        v3.data_ptr(), vs[0], vs[1],
+        slots.data_ptr(), num_tokens, num_kv_heads, head_dim,
+        num_blocks, block_size, _DTYPES[k_cache.dtype],
+    )
+    if rc:
+        _native.check(rc, "pagedkv_kv_append")
+    if _DEBUG:
+        _debug_check(k_cache.device, "kv_append")
 
 
 # Device arrays of per-layer pool base pointers, keyed by the pointer tuple.
@@ -390,21 +414,22 @@ def copy_blocks(
     assert block_mapping.dtype == torch.int64 and block_mapping.dim() == 2 and block_mapping.shape[1] == 2
     for t in list(k_caches) + list(v_caches):
         assert t.shape == ref.shape and t.dtype == ref.dtype and t.is_contiguous() and t.device == ref.device
+        assert t.data_ptr() % 16 == 0, "pool tensors must start on a 16-byte boundary"
     num_pairs = block_mapping.shape[0]
     if num_pairs == 0:
         return
     mapping = block_mapping if block_mapping.is_contiguous() else block_mapping.contiguous()
     kp, vp = _pointer_tables(k_caches, v_caches)
     block_bytes = ref[0].numel() * ref.element_size()
-    dev = ref.device
-    guard = _device_guard(dev)
-    with guard if guard is not None else _NullCtx():
-        rc = _native.lib().pagedkv_copy_blocks(
-            kp.data_ptr(), vp.data_ptr(), len(k_caches), mapping.data_ptr(), num_pairs,
-            block_bytes, ref.shape[0], _stream_handle(dev),
-        )
-    _native.check(rc, "pagedkv_copy_blocks")
-    _debug_check(dev, "copy_blocks")
+    rc = _launch(
+        ref.get_device(), _native.lib().pagedkv_copy_blocks,
+        kp.data_ptr(), vp.data_ptr(), len(k_caches), mapping.data_ptr(), num_pairs,
+        block_bytes, ref.shape[0],
+    )
+    if rc:
+        _native.check(rc, "pagedkv_copy_blocks")
+    if _DEBUG:
+        _debug_check(ref.device, "copy_blocks")
 
 
 def kv_append_rope(
@@ -436,8 +461,9 @@ def kv_append_rope(
     num_blocks, block_size, hkv, d = k_cache.shape
     assert d % 16 == 0, "head_dim must be a multiple of 16"
     q3 = q if q.dim() == 3 else q.reshape(q.shape[0], -1, d)
-    k3 = k_new.reshape(-1, hkv, d)
-    v3 = v_new.reshape(-1, hkv, d)
+    row = (hkv, d)
+    k3 = k_new if k_new.dim() == 3 and k_new.shape[1:] == row else k_new.reshape(-1, hkv, d)
+    v3 = v_new if v_new.dim() == 3 and v_new.shape[1:] == row else v_new.reshape(-1, hkv, d)
     n, hq = q3.shape[0], q3.shape[1]
     c2 = cos.reshape(n, d) if cos.dim() != 2 else cos
     s2 = sin.reshape(n, d) if sin.dim() != 2 else sin
@@ -451,24 +477,24 @@ def kv_append_rope(
     q3, k3, v3 = fix(q3), fix(k3), fix(v3)
     if c2.stride() != s2.stride() or c2.stride(-1) != 1:
         c2, s2 = c2.contiguous(), s2.contiguous()
-    slots = slot_mapping.reshape(-1)
+    slots = slot_mapping if slot_mapping.dim() == 1 else slot_mapping.reshape(-1)
     if not slots.is_contiguous():
         slots = slots.contiguous()
-    dev = k_cache.device
-    guard = _device_guard(dev)
-    with guard if guard is not None else _NullCtx():
-        rc = _native.lib().pagedkv_kv_append_rope(
-            q_out.data_ptr(), q_out.stride(0), q_out.stride(1),
-            q3.data_ptr(), q3.stride(0), q3.stride(1), hq,
-            k_cache.data_ptr(), v_cache.data_ptr(),
-            k3.data_ptr(), k3.stride(0), k3.stride(1),
-            v3.data_ptr(), v3.stride(0), v3.stride(1),
-            c2.data_ptr(), s2.data_ptr(), c2.stride(0),
-            slots.data_ptr(), n, hkv, d, num_blocks, block_size, _DTYPES[dt],
-            _stream_handle(dev),
-        )
-    _native.check(rc, "pagedkv_kv_append_rope")
-    _debug_check(dev, "kv_append_rope")
+    qos, qs, ks, vs = q_out.stride(), q3.stride(), k3.stride(), v3.stride()
+    rc = _launch(
+        k_cache.get_device(), _native.lib().pagedkv_kv_append_rope,
+        q_out.data_ptr(), qos[0], qos[1],
+        q3.data_ptr(), qs[0], qs[1], hq,
+        k_cache.data_ptr(), v_cache.data_ptr(),
+        k3.data_ptr(), ks[0], ks[1],
+        v3.data_ptr(), vs[0], vs[1],
+        c2.data_ptr(), s2.data_ptr(), c2.stride(0),
+        slots.data_ptr(), n, hkv, d, num_blocks, block_size, _DTYPES[dt],
+    )
+    if rc:
+        _native.check(rc, "pagedkv_kv_append_rope")
+    if _DEBUG:
+        _debug_check(k_cache.device, "kv_append_rope")
     return q_out
 
 
