@@ -9,9 +9,11 @@ the KV append of 256 new tokens through a slot mapping, then batched decode
 attention over all 256 contexts (which include the appended token).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload cfg2|cfg3|cfg4|cfg4-cow|cfg5|ops] [--gqa G]
+                  [--workload cfg1|cfg2|cfg3|cfg4|cfg4-cow|cfg5|ops] [--gqa G]
 
-Extra workloads (not the headline): ``cfg3`` = BASELINE config 3 (head_dim
+Extra workloads (not the headline): ``cfg1`` = BASELINE config 1 (the
+reference's CPU case: 8 sequences of U[1,512] tokens, 512-block pool; the CPU
+reference is timed on all host threads and on one); ``cfg3`` = config 3 (head_dim
 128, 8 kv heads, GQA G, 128 sequences with log-uniform lengths 16..8192,
 q x30); ``cfg4`` = config 4 (512 sequences in 8 groups sharing a 1024-token
 prefix + 256 own tokens); ``cfg4-cow`` = its copy-on-write variant (each
@@ -171,6 +173,28 @@ def make_workload(name: str, rank: int, gqa: int = 7) -> Workload:
             "cfg2: KV append (256 tokens) + paged GQA decode attention, 256 seqs x 2048 ctx, 14q/2kv heads, "
             "head_dim 64, block_size 16, fp16 pool 40960 blocks, shuffled tables",
             14, 2, 64, 16, 40960, s["tables"], s["lens"], s["slots"], s["q"], s["k_new"], s["v_new"], None,
+        )
+    if name == "cfg1":
+        n, hq, hkv, d, bs, nb = 8, 14, 2, 64, 16, 512
+        rng = np.random.default_rng(3100 + rank)
+        lens_l = [int(x) for x in rng.integers(1, 513, n)]
+        perm = list(range(nb))
+        random.Random(45 + rank).shuffle(perm)
+        rows, at = [], 0
+        for x in lens_l:
+            c = (x + bs - 1) // bs
+            rows.append(perm[at : at + c])
+            at += c
+        tables = _tables_from_lists(rows)
+        lens = torch.tensor(lens_l, dtype=torch.int32)
+        g = torch.Generator().manual_seed(1050 + rank)
+        q, k_new, v_new = _qkv(g, n, hq, hkv, d)
+        return Workload(
+            "cfg1",
+            "cfg1: KV append + paged decode attention, 8 seqs, lengths U[1,512], 14q/2kv heads, head_dim 64, "
+            "block_size 16, pool 512 blocks, shuffled tables (the reference's CPU case; fp16 on the GPU, "
+            "the CPU reference in fp32)",
+            hq, hkv, d, bs, nb, tables, lens, _slots_for(tables, lens, bs), q, k_new, v_new, None,
         )
     if name == "cfg3":
         n, hkv, d, bs = 128, 8, 128, 16
@@ -361,9 +385,7 @@ def cpu_reference_step(sm: dict) -> None:
     paged_ref.paged_attention_ref(sm["q"], sm["k"], sm["v"], sm["rows"], sm["lens"], sm["scale"])
 
 
-def time_cpu_reference(wl: Workload, num_seqs: int, min_seconds: float) -> dict:
-    sm = _cpu_sample(wl, num_seqs)
-    threads = torch.get_num_threads()
+def _time_cpu_calls(sm: dict, min_seconds: float) -> tuple[float, int, float]:
     cpu_reference_step(sm)  # warm
     n, t0 = 0, time.perf_counter()
     while True:
@@ -372,17 +394,110 @@ def time_cpu_reference(wl: Workload, num_seqs: int, min_seconds: float) -> dict:
         el = time.perf_counter() - t0
         if el >= min_seconds:
             break
-    per = el / n
+    return el / n, n, el
+
+
+def time_cpu_reference(wl: Workload, num_seqs: int, min_seconds: float) -> dict:
+    """The oracle on all host threads (the reported value) and on one thread
+    (``value_1thread``), each for about ``min_seconds`` (half of it for the
+    single thread)."""
+    sm = _cpu_sample(wl, num_seqs)
+    all_threads = os.cpu_count() or 1
+    torch.set_num_threads(all_threads)
+    per, n, el = _time_cpu_calls(sm, min_seconds)
+    torch.set_num_threads(1)
+    per1, n1, el1 = _time_cpu_calls(sm, min_seconds / 2)
+    torch.set_num_threads(all_threads)
     return {
         "value": round(sm["bytes"] / per / 1e9, 3),
         "unit": "GB/s",
-        "cores": threads,
+        "cores": all_threads,
         "kind": "port",
+        "value_1thread": round(sm["bytes"] / per1 / 1e9, 3),
+        "ms_per_call": round(per * 1e3, 3),
+        "ms_per_call_1thread": round(per1 * 1e3, 3),
         "sample": (
             f"first {sm['n']} of the {wl.num_seqs} sequences of {wl.name}, fp32 torch restatement of the "
             f"reference's naive_reference_paged_attention + append"
-            f"{' + copy-on-write' if sm['pairs'] is not None else ''}, {n} calls over {el:.1f} s, "
-            f"{threads} threads (os.cpu_count()={os.cpu_count()})"
+            f"{' + copy-on-write' if sm['pairs'] is not None else ''}: {n} calls over {el:.1f} s on "
+            f"{all_threads} threads, {n1} calls over {el1:.1f} s on 1 thread (os.cpu_count()={os.cpu_count()}, "
+            f"torch.get_num_threads()={torch.get_num_threads()})"
+        ),
+    }
+
+
+def time_cpu_model_step(min_seconds: float, source: torch.nn.Module | None = None, batch: int = 8,
+                        ctx: int = 512) -> dict:
+    """Config 5 on the host cores, bounded: one decode step of a batch of
+    ``batch`` sequences at context ``ctx`` through the same random-init
+    Qwen2.5-0.5B-architecture model in fp32 on CPU (the weights of ``source``
+    when given), with the oracle's RoPE, append and paged attention in place of
+    the kernels (the reference runner's CPU path). The whole trace is not
+    feasible on CPU."""
+    from oracle import paged_ref
+    from pagedkv.decode_runner import random_qwen2
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    if source is None:
+        model = random_qwen2(dtype=torch.float32, device="cpu", seed=0)
+    else:
+        # same weights without a second random init: an empty fp32 copy on the
+        # host filled from the source's state dict; the rotary table is not in
+        # the state dict and is rebuilt
+        model = random_qwen2(dtype=torch.float32, device="meta", seed=0).to_empty(device="cpu")
+        model.load_state_dict({k: v.detach().float().cpu() for k, v in source.state_dict().items()})
+        model.model.rotary_emb = type(model.model.rotary_emb)(config=model.config)
+        model.eval()
+    m = model.model
+    hq, hkv, d, bs = 14, 2, 64, 16
+    per_seq = (ctx + 1 + bs - 1) // bs
+    g = torch.Generator().manual_seed(5)
+    layers = len(m.layers)
+    kc = [torch.randn(batch * per_seq, bs, hkv, d, generator=g) for _ in range(layers)]
+    vc = [torch.randn(batch * per_seq, bs, hkv, d, generator=g) for _ in range(layers)]
+    tables = [list(range(s * per_seq, (s + 1) * per_seq)) for s in range(batch)]
+    lens = [ctx + 1] * batch
+    slots = paged_ref.decode_slots(tables, lens, bs)
+    ids = torch.randint(0, model.config.vocab_size, (batch,), generator=g)
+    pos = torch.full((batch,), ctx, dtype=torch.int64)
+
+    @torch.inference_mode()
+    def step():
+        x = m.embed_tokens(ids[:, None])
+        cos, sin = m.rotary_emb(x, pos[:, None])
+        c2, s2 = cos[:, 0], sin[:, 0]
+        for li, layer in enumerate(m.layers):
+            attn = layer.self_attn
+            h = layer.input_layernorm(x)
+            q = paged_ref.rope_ref(attn.q_proj(h).view(batch, hq, d), c2, s2)
+            k = paged_ref.rope_ref(attn.k_proj(h).view(batch, hkv, d), c2, s2)
+            v = attn.v_proj(h).view(batch, hkv, d)
+            paged_ref.kv_append_ref(kc[li].numpy(), vc[li].numpy(), k.numpy(), v.numpy(), slots)
+            o = paged_ref.paged_attention_ref(q, kc[li], vc[li], tables, lens, attn.scaling)
+            x = x + attn.o_proj(o.reshape(batch, 1, -1))
+            x = x + layer.mlp(layer.post_attention_layernorm(x))
+        return model.lm_head(m.norm(x)[:, 0]).argmax(-1)
+
+    step()  # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        step()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    per = el / n
+    return {
+        "value": round(batch / per, 2),
+        "unit": "decode tok/s",
+        "cores": threads,
+        "kind": "port",
+        "ms_per_step": round(per * 1e3, 2),
+        "sample": (
+            f"{n} decode steps over {el:.1f} s of a batch of {batch} at context {ctx} through the random-init "
+            f"model in fp32 on CPU with the oracle's RoPE, append and paged attention ({threads} threads); "
+            "the full trace is not feasible on CPU"
         ),
     }
 
@@ -654,7 +769,6 @@ def run_ours(args) -> None:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        torch.set_num_threads(os.cpu_count() or 1)
         cpu = time_cpu_reference(wl, 16, args.cpu_seconds)
 
     peaks = {}
@@ -820,6 +934,9 @@ def run_model(args) -> None:
         dist.destroy_process_group()
     if rank != 0:
         return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = time_cpu_model_step(args.cpu_seconds, source=model)
     line = {
         "metric": "decode tokens/s",
         "value": round(gen_all / elapsed_max, 1),
@@ -848,6 +965,7 @@ def run_model(args) -> None:
         "ttft_ms_p50": round(1e3 * float(np.median(ttft)), 2),
         "request_latency_s_p50": round(float(np.median(finish)), 3),
         "timing": "wall clock of the trace replay on rank 0 (max over ranks); decode steps are CUDA-graph replays",
+        "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
 
@@ -968,7 +1086,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg4-cow", "cfg5", "ops"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg4-cow", "cfg5", "ops"],
+                    default="cfg2")
     ap.add_argument("--requests", type=int, default=2000, help="cfg5: requests per GPU")
     ap.add_argument("--rate", type=float, default=32.0, help="cfg5: Poisson arrival rate per GPU (req/s)")
     ap.add_argument("--kv-budget-gb", type=float, default=60.0, help="cfg5: KV pool budget per GPU")
