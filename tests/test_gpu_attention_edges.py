@@ -92,3 +92,28 @@ def test_wide_groups_and_head_dim_32_on_tensor_cores(cuda_ready, d, g):
     q, k, v, tables, lists, lens_t = _random_case(d * 100 + g, len(lens), g * hkv, hkv, d, 16, lens, q_scale=4.0)
     _check_vs_oracle(cuda_ready, q, k, v, tables, lists, lens_t, 1 / math.sqrt(d))
     assert pagedkv.last_decode_launch_info()[1] == "tc"
+
+
+@pytest.mark.parametrize(
+    "d,g,hkv,dtype",
+    [
+        (128, 40, 2, torch.float16),   # 32 + 8 query heads per kv head
+        (128, 64, 1, torch.float16),   # two full chunks of 32
+        (64, 71, 1, torch.float16),    # MQA with 71 query heads: chunks 16,16,16,16,7
+        (64, 20, 3, torch.bfloat16),   # odd kv heads (a half-empty tile row) and 16 + 4
+        (32, 12, 5, torch.float16),    # four kv heads per tile row, 8 + 4
+        (32, 9, 4, torch.float16),
+    ],
+)
+def test_groups_wider_than_a_tile_run_in_chunks(cuda_ready, d, g, hkv, dtype):
+    """GQA groups above 32 / 16 / 8 query heads per kv head (head_dim 128 / 64
+    / 32) run on the tensor cores in chunks of that many heads, one segment per
+    chunk; long and short sequences, so chunk segments are also cut across CTAs
+    and combined."""
+    lens = [1, 100, 129, 3000, 20000]
+    q, k, v, tables, lists, lens_t = _random_case(d * 1000 + g, len(lens), g * hkv, hkv, d, 16, lens,
+                                                  q_scale=4.0, dtype=dtype)
+    tol = dict(atol=8e-3, rtol=8e-3) if dtype == torch.bfloat16 else {}
+    _check_vs_oracle(cuda_ready, q, k, v, tables, lists, lens_t, 1 / math.sqrt(d), **tol)
+    assert pagedkv.last_decode_launch_info()[1] == "tc"
+    assert pagedkv.read_error_flags(cuda_ready) == 0

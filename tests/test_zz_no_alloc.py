@@ -58,7 +58,7 @@ def _noalloc(out, q, k, v, tables, lens, scale):
     [
         (256, 14, 2, 64, 16, "cfg2"),    # tensor-core path, cut segments combined across CTAs
         (6, 56, 8, 128, 16, "varlen"),   # tensor-core path, head_dim 128, ragged lengths
-        (5, 8, 4, 64, 16, "simt"),       # CUDA-core split-K path
+        (5, 8, 4, 256, 16, "simt"),      # CUDA-core split-K path (head_dim 256)
     ],
 )
 def test_noalloc_matches_workspace_entry_point_twice(shape):

@@ -106,10 +106,11 @@ __device__ unsigned long long g_trace[kTraceCtas][7][kTraceSlots];
 
 struct TcParams {
   DecodeParams p;
-  int32_t head_groups;  // ceil(hkv / H)
+  int32_t head_groups;  // segments per sequence: ceil(hkv / H) tile rows x chunks
+  int32_t chunks;       // query-head chunks of GP heads per kv head (groups wider than GP)
   int32_t oob_row;      // num_blocks * block_size: first row past the pool
-  float *part_acc;      // [grid][H * G][head_dim] published partial sums
-  float2 *part_ml;      // [grid][H * G] (reference max, denominator) of those
+  float *part_acc;      // [grid][H * GP][head_dim] published partial sums
+  float2 *part_ml;      // [grid][H * GP] (reference max, denominator) of those
   uint32_t *flags;      // [grid] 1 = CTA's partial published; reset to 0 when consumed
 };
 
@@ -138,7 +139,9 @@ __device__ __forceinline__ int64_t owner_of(int64_t u, int64_t U, int64_t G) {
   return ((u + 1) * G + U - 1) / U - 1;
 }
 
-// One contiguous run of tiles of a (sequence, head group) segment.
+// One contiguous run of tiles of a (sequence, head group) segment. Head group
+// hg is tile row hg / chunks (H kv heads at x offset row * 128 of the pool
+// row) and query-head chunk hg % chunks (GP query heads of each of them).
 struct Piece {
   int seq, hg, len;
   int t0, t1;         // token range [t0, t1)
@@ -215,10 +218,10 @@ struct PieceAcc {
 // (at most once per CTA per launch).
 template <typename T, int GP, int D>
 __device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP> a, int64_t b1, int hl, int dim,
-                                            int kv, bool have_kv, T *out, volatile int *abort_flag, int row) {
+                                            int gn, bool have_kv, T *out, volatile int *abort_flag, int row) {
   using E = Elem<T>;
   const DecodeParams &p = tp.p;
-  const int HQS = (128 / D) * p.group;
+  const int HQS = (128 / D) * GP;  // partial slots per CTA
   if (row == 0) {
     for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) {
       const uint64_t t0 = globaltimer_ns();
@@ -233,9 +236,9 @@ __device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP> 
   named_bar(2, 128);
   if (have_kv) {
     for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) {
-      const int64_t hh0 = bb * HQS + hl * p.group;
+      const int64_t hh0 = bb * HQS + hl * GP;
       for (int g = 0; g < GP; ++g) {
-        if (g < p.group) {
+        if (g < gn) {
           const float2 ml = __ldcg(&tp.part_ml[hh0 + g]);
           const float av = __ldcg(&tp.part_acc[(hh0 + g) * D + dim]);
           const float mb = fmaxf(a.msel[g], ml.x);
@@ -248,8 +251,7 @@ __device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP> 
       }
     }
     for (int g = 0; g < GP; ++g)
-      if (g < p.group)
-        out[(int64_t)(kv * p.group + g) * p.o_sh] = E::from_float(a.lsum[g] > 0.f ? __fdividef(a.acc[g], a.lsum[g]) : 0.f);
+      if (g < gn) out[(int64_t)g * p.o_sh] = E::from_float(a.lsum[g] > 0.f ? __fdividef(a.acc[g], a.lsum[g]) : 0.f);
   }
   named_bar(2, 128);  // every partner partial read before its flag is cleared
   if (row == 0) {
@@ -301,7 +303,9 @@ struct RescaleSlot {
 };
 
 
-template <typename T, int H, int GP, int N, int SK, int SV>
+// CH: the group is wider than GP and runs in tp.chunks query-head chunks (a
+// separate instantiation, so the single-chunk kernels carry none of it).
+template <typename T, int H, int GP, int N, int SK, int SV, bool CH>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
                  const __grid_constant__ CUtensorMap tmap_v, const __grid_constant__ TcParams tp) {
@@ -345,6 +349,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const DecodeParams &p = tp.p;
+  const int nch = CH ? tp.chunks : 1;  // query-head chunks per tile row
 #ifdef PAGEDKV_TRACE
   uint64_t tw[kTraceSlots] = {};
   const uint64_t t_kernel0 = globaltimer_ns();
@@ -486,7 +491,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     const int nst = is_k ? SK : SV;
     const uint32_t ring = sbase + (is_k ? L::kOffK : L::kOffV);
     if (lane == 0) tma_prefetch_desc(tmap);
-    const uint64_t policy = l2_policy_evict_first();
+    // K/V rows are read once (evict first), or once per query-head chunk when
+    // the group is split, where the next chunk's segment re-reads them from L2.
+    const uint64_t policy = CH ? l2_policy_evict_normal() : l2_policy_evict_first();
     const int bpt = kTile / p.block_size;  // blocks per tile: 1..16, divides 32
     constexpr int kQChunks = 16 * N / 32;  // Q 16-byte chunks per lane
     int stage = 0;
@@ -536,14 +543,16 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         const int rem = idx - xh * 8 * N;
         const int n = rem >> 3, ch = rem & 7;
         const int hl = n / GP, g = n - hl * GP;
-        const int kv = q.hg * H + hl;
+        const int qrow = q.hg / nch;
+        const int kv = qrow * H + hl;
+        const int gq = (q.hg - qrow * nch) * GP + g;  // query head within the kv head's group
         // Element e of the 128-wide row belongs to kv head e / D of the group:
         // query column n (head hl) is nonzero only on its own head's D elements.
         const int e = xh * 64 + ch * 8;
-        const bool in = hl < H && g < p.group && kv < p.hkv && e / D == hl;
+        const bool in = hl < H && gq < p.group && kv < p.hkv && e / D == hl;
         const int d = e - hl * D;
         const T *src = reinterpret_cast<const T *>(p.q) +
-                       (in ? (int64_t)q.seq * p.q_ss + (int64_t)(kv * p.group + g) * p.q_sh + d : 0);
+                       (in ? (int64_t)q.seq * p.q_ss + (int64_t)(kv * p.group + gq) * p.q_sh + d : 0);
         const uint32_t addr = qbuf + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
         cp_async_16(addr, src, in ? 16u : 0u);
       }
@@ -561,6 +570,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       if (is_k && have_nx && !q_issue(nx, qi++)) break;
       const int lb0 = pc.t0 / p.block_size;
       const int need = (pc.t1 + p.block_size - 1) / p.block_size;
+      const int x0 = pc.hg / nch * 128;  // this tile row's first element
       for (int j = 0; j < pc.ntiles; ++j) {
         const int wofs = (j * bpt) & 31;
         if (wofs == 0) {
@@ -595,7 +605,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
             }
           }
           const uint32_t dst = ring + stage * kOperandBytes + h * kHalfBytes + b * p.block_size * 128;
-          tma_load_2d(dst, tmap, pc.hg * 128 + h * 64, y, full, policy);
+          tma_load_2d(dst, tmap, x0 + h * 64, y, full, policy);
         }
         ++issued;
         if (++stage == nst) {
@@ -890,7 +900,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     const int hl = row / D;   // kv head of the group this O row belongs to
     const int dim = row % D;
     const uint32_t tl = tmem + ((uint32_t)(q4 * 32) << 16);
-    const int HQS = H * p.group;  // query heads per segment
+    const int HQS = H * GP;  // partial slots per CTA (query columns of a segment)
     uint32_t gt = 0, pi = 0;
 
     // Sequences of length 0 own no tiles: CTA (seq % grid) writes their zeros.
@@ -958,17 +968,20 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       const uint64_t t_epi0 = clock64();
       tw[6] += 1;
 #endif
-      const int kv = pc.hg * H + hl;
+      const int prow = pc.hg / nch;
+      const int kv = prow * H + hl;
       const bool have_kv = kv < p.hkv;
-      T *out = reinterpret_cast<T *>(p.out) + (int64_t)pc.seq * p.o_ss + dim;
+      const int qb = (pc.hg - prow * nch) * GP;  // first query head of the chunk
+      const int gn = p.group - qb < GP ? p.group - qb : GP;  // query heads in the chunk
+      T *out = reinterpret_cast<T *>(p.out) + (int64_t)pc.seq * p.o_ss + (int64_t)(kv * p.group + qb) * p.o_sh + dim;
       if (pc.ntiles == pc.seg_tiles) {
         // Whole segment in this CTA: normalise and store.
         if (have_kv) {
 #pragma unroll
           for (int g = 0; g < GP; ++g) {
-            if (g < p.group) {
+            if (g < gn) {
               const float v = lsum[g] > 0.f ? __fdividef(acc[g], lsum[g]) : 0.f;
-              out[(int64_t)(kv * p.group + g) * p.o_sh] = E::from_float(v);
+              out[(int64_t)g * p.o_sh] = E::from_float(v);
             }
           }
         }
@@ -979,8 +992,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         if (have_kv) {
 #pragma unroll
           for (int g = 0; g < GP; ++g) {
-            if (g < p.group) {
-              const int64_t hh = (int64_t)blockIdx.x * HQS + hl * p.group + g;
+            if (g < gn) {
+              const int64_t hh = (int64_t)blockIdx.x * HQS + hl * GP + g;
               tp.part_acc[hh * D + dim] = acc[g];
               if (dim == 0) tp.part_ml[hh] = make_float2(msel[g], lsum[g]);
             }
@@ -1003,7 +1016,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           pa.lsum[g] = lsum[g];
           pa.msel[g] = msel[g];
         }
-        combine_pieces<T, GP, D>(tp, pa, owner_of(pc.seg_units + kSegUnits + (int64_t)pc.seg_tiles * kTileUnits - 1, U_total, G), hl, dim, kv,
+        combine_pieces<T, GP, D>(tp, pa, owner_of(pc.seg_units + kSegUnits + (int64_t)pc.seg_tiles * kTileUnits - 1, U_total, G), hl, dim, gn,
                                  have_kv, out, abort_flag, row);
       }
 #ifdef PAGEDKV_TRACE
@@ -1049,7 +1062,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 // ---- host side ----------------------------------------------------------------
 
 struct TcPlan {
-  int H, GP, N, stages, head_groups, grid;
+  int H, GP, N, stages, head_groups, chunks, grid;
 };
 
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
@@ -1059,11 +1072,16 @@ TcPlan make_plan(int32_t num_seqs, int32_t hq, int32_t hkv, int32_t head_dim, in
   TcPlan pl;
   pl.H = 128 / head_dim;
   const int G = hq / hkv;
-  pl.GP = round_up(G, 8);
+  // Query columns per kv head: the group padded to 8, at most 32 / H (N <= 32).
+  // A wider group is cut into chunks of that many heads, one segment each; the
+  // chunks of a tile row run back to back and re-read its K/V from L2.
+  const int gp_max = pl.H == 1 ? 32 : 16 / (pl.H / 2);
+  pl.chunks = (G + gp_max - 1) / gp_max;
+  pl.GP = pl.chunks > 1 ? gp_max : round_up(G, 8);
   if (pl.H == 1 && pl.GP > 16) pl.GP = 32;  // one kv head per tile: columns 17..32 share the N = 32 variant
   pl.N = round_up(pl.H * pl.GP, 16);
   pl.stages = pl.N <= 16 ? 3 : 2;
-  pl.head_groups = (hkv + pl.H - 1) / pl.H;
+  pl.head_groups = (hkv + pl.H - 1) / pl.H * pl.chunks;
   const int64_t max_tiles = ((int64_t)(max_tokens > 0 ? max_tokens : 1) + kTile - 1) / kTile;
   const int64_t tiles_upper = (int64_t)num_seqs * pl.head_groups * max_tiles;
   int grid = num_sms;
@@ -1079,7 +1097,9 @@ size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 size_t plan_workspace(const TcPlan &pl, int32_t num_seqs, int32_t hq, int32_t hkv, int32_t head_dim) {
   (void)num_seqs;
-  const size_t hqs = (size_t)pl.H * (hq / hkv);
+  (void)hq;
+  (void)hkv;
+  const size_t hqs = (size_t)pl.H * pl.GP;
   const size_t slots = (size_t)pl.grid;
   return kWorkspaceHeaderBytes + align256(slots * hqs * sizeof(float2)) +
          align256(slots * hqs * head_dim * sizeof(float));
@@ -1152,11 +1172,11 @@ bool make_map(CUtensorMap *map, const void *base, int dtype, uint64_t row_elems,
   return true;
 }
 
-template <typename T, int H, int GP, int N, int SK, int SV>
+template <typename T, int H, int GP, int N, int SK, int SV, bool CH = false>
 cudaError_t launch_tc(const CUtensorMap &mk, const CUtensorMap &mv, const TcParams &tp, int grid,
                       cudaStream_t stream) {
   using L = SmemLayout<N, SK, SV>;
-  auto kern = decode_tc_kernel<T, H, GP, N, SK, SV>;
+  auto kern = decode_tc_kernel<T, H, GP, N, SK, SV, CH>;
   // The shared-memory opt-in is a per-device function attribute: set it once
   // per device (outside any stream capture that follows the first call).
   static std::atomic<uint64_t> attr_done{0};
@@ -1187,6 +1207,12 @@ cudaError_t launch_tc(const CUtensorMap &mk, const CUtensorMap &mv, const TcPara
 template <typename T>
 cudaError_t dispatch_tc(const TcPlan &pl, const CUtensorMap &mk, const CUtensorMap &mv, const TcParams &tp,
                         cudaStream_t stream) {
+  if (pl.chunks > 1) {
+    if (pl.H == 1 && pl.GP == 32) return launch_tc<T, 1, 32, 32, 2, 2, true>(mk, mv, tp, pl.grid, stream);
+    if (pl.H == 2 && pl.GP == 16) return launch_tc<T, 2, 16, 32, 2, 2, true>(mk, mv, tp, pl.grid, stream);
+    if (pl.H == 4 && pl.GP == 8) return launch_tc<T, 4, 8, 32, 2, 2, true>(mk, mv, tp, pl.grid, stream);
+    return cudaErrorInvalidValue;
+  }
   if (pl.H == 2 && pl.GP == 8) return launch_tc<T, 2, 8, 16, 3, 3>(mk, mv, tp, pl.grid, stream);
   if (pl.H == 2 && pl.GP == 16) return launch_tc<T, 2, 16, 32, 2, 2>(mk, mv, tp, pl.grid, stream);
   if (pl.H == 1 && pl.GP == 8) return launch_tc<T, 1, 8, 16, 3, 3>(mk, mv, tp, pl.grid, stream);
@@ -1209,19 +1235,12 @@ bool tc_eligible(int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, in
   if (num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return false;
   const int G = num_q_heads / num_kv_heads;
   // A tile row is 128 elements: 128 / head_dim kv heads side by side, and their
-  // query columns (padded groups) must fit the N <= 32 MMA width. Every such
-  // group size runs here: the pipeline is bound by HBM, not by the MMA shape
+  // query columns (padded groups) fill at most the N = 32 MMA width; wider
+  // groups run in chunks of 32 / 16 / 8 query heads per kv head. Small groups
+  // run here too: the pipeline is bound by HBM, not by the MMA shape
   // (measured 1.1-2.7x faster than the CUDA-core kernel at G = 1, 2).
   if (G < 1) return false;
-  if (head_dim == 128) {
-    if (G > 32) return false;
-  } else if (head_dim == 64) {
-    if (G > 16) return false;
-  } else if (head_dim == 32) {
-    if (G > 8) return false;
-  } else {
-    return false;
-  }
+  if (head_dim != 128 && head_dim != 64 && head_dim != 32) return false;
   if (block_size < 8 || block_size > 128 || (block_size & (block_size - 1)) != 0) return false;
   return true;
 }
@@ -1260,8 +1279,9 @@ int tc_launch(DecodeParams &p, int dtype, void *workspace, size_t workspace_byte
   }
   TcParams tp{};
   tp.head_groups = pl.head_groups;
+  tp.chunks = pl.chunks;
   tp.oob_row = (int32_t)rows;
-  const size_t hqs = (size_t)pl.H * (p.hq / p.hkv);
+  const size_t hqs = (size_t)pl.H * pl.GP;
   const size_t slots = (size_t)pl.grid;
   char *ws = static_cast<char *>(workspace);
   tp.flags = reinterpret_cast<uint32_t *>(ws);  // zero between launches

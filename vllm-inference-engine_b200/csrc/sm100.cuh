@@ -117,6 +117,12 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   return p;
 }
 
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
 // Order this thread's generic-proxy shared-memory writes before later
 // async-proxy (tensor core / TMA) accesses.
 __device__ __forceinline__ void fence_proxy_async_smem() {
