@@ -282,17 +282,23 @@ SplitPlan plan_simt_splits(int32_t num_seqs, int32_t num_kv_heads, int32_t group
   return plan;
 }
 
+// Tokens per lane group per step: more loads in flight and fewer online-softmax
+// updates per token, as far as the registers of GMAX query heads allow.
+template <int D, int GMAX>
+constexpr int simt_unroll() {
+  return D <= 64 ? 4 : D == 128 ? (GMAX <= 2 ? 4 : 2) : (GMAX <= 2 ? 4 : GMAX == 4 ? 2 : 1);
+}
+
 template <typename T, int D>
 static cudaError_t launch_simt_d(const DecodeParams &p, cudaStream_t stream) {
-  constexpr int U = D <= 64 ? 4 : (D == 128 ? 2 : 1);
   const int gmax = p.group <= 1 ? 1 : p.group <= 2 ? 2 : p.group <= 4 ? 4 : 8;
   const int gchunks = (p.group + gmax - 1) / gmax;
   dim3 grid((unsigned)p.num_seqs, (unsigned)p.num_splits, (unsigned)(p.hkv * gchunks));
   switch (gmax) {
-    case 1: decode_simt_kernel<T, D, 1, U><<<grid, 128, 0, stream>>>(p); break;
-    case 2: decode_simt_kernel<T, D, 2, U><<<grid, 128, 0, stream>>>(p); break;
-    case 4: decode_simt_kernel<T, D, 4, U><<<grid, 128, 0, stream>>>(p); break;
-    default: decode_simt_kernel<T, D, 8, U><<<grid, 128, 0, stream>>>(p); break;
+    case 1: decode_simt_kernel<T, D, 1, simt_unroll<D, 1>()><<<grid, 128, 0, stream>>>(p); break;
+    case 2: decode_simt_kernel<T, D, 2, simt_unroll<D, 2>()><<<grid, 128, 0, stream>>>(p); break;
+    case 4: decode_simt_kernel<T, D, 4, simt_unroll<D, 4>()><<<grid, 128, 0, stream>>>(p); break;
+    default: decode_simt_kernel<T, D, 8, simt_unroll<D, 8>()><<<grid, 128, 0, stream>>>(p); break;
   }
   return cudaGetLastError();
 }
