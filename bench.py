@@ -864,9 +864,10 @@ def run_ours(args) -> None:
 def run_model(args) -> None:
     """Config 5: a random-init Qwen2.5-0.5B-architecture model (24 layers, 896
     hidden, 14/2 heads, MLP 4864, vocab 151936, fp16) served by the continuous-
-    batching decode runner over a seeded Poisson trace (per GPU: ``--requests``
-    at ``--rate`` req/s, prompts U[64, 1024] random ids, 128 output tokens,
-    greedy). Reports decode tokens/s (all GPUs) and latency figures."""
+    batching decode runner over a seeded Poisson trace (``--requests`` at
+    ``--rate`` req/s per GPU, prompts U[64, 1024] random ids, 128 output
+    tokens, greedy), its requests routed to the GPUs by least outstanding
+    tokens. Reports decode tokens/s (all GPUs) and latency figures."""
     import numpy as np
     from pagedkv.decode_runner import PagedDecodeRunner, random_qwen2
 
@@ -878,13 +879,23 @@ def run_model(args) -> None:
     num_blocks = min(int(args.kv_budget_gb * 1e9) // block_bytes, (2**31 - 1) // block_size)
     runner = PagedDecodeRunner(model, num_blocks=num_blocks, block_size=block_size, max_batch=256,
                                max_seq_len=1024 + 128)
-    rng = np.random.default_rng(5000 + rank)
-    n_req = args.requests
-    arrivals = np.cumsum(rng.exponential(1.0 / args.rate, n_req))
-    prompt_lens = rng.integers(64, 1025, n_req)
-    vocab = model.config.vocab_size
-    prompts = [rng.integers(0, vocab, int(L)).tolist() for L in prompt_lens]
+    # One global trace (world x requests at world x rate), routed by
+    # least-outstanding-tokens (pagedkv.router.route_trace): every rank computes
+    # the same assignment and serves its share; nothing is exchanged.
+    from pagedkv.router import route_trace
+
+    rng = np.random.default_rng(5000)
+    n_all = args.requests * world
+    arr_all = np.cumsum(rng.exponential(1.0 / (args.rate * world), n_all))
+    lens_all = rng.integers(64, 1025, n_all)
     out_tokens = 128
+    mine = [i for i, r_ in enumerate(route_trace([int(L) + out_tokens for L in lens_all], world)) if r_ == rank]
+    n_req = len(mine)
+    arrivals = arr_all[mine]
+    prompt_lens = lens_all[mine]
+    vocab = model.config.vocab_size
+    prng = np.random.default_rng(6000 + rank)
+    prompts = [prng.integers(0, vocab, int(L)).tolist() for L in prompt_lens]
 
     # warm-up: graphs for every bucket and one prefill, outside the timed trace
     runner.warm_prefill(1024)
@@ -959,11 +970,13 @@ def run_model(args) -> None:
         "config": {
             "workload": "cfg5: random-init Qwen2.5-0.5B architecture (24 layers, hidden 896, 14q/2kv, head_dim 64, "
                         "MLP 4864, vocab 151936, tied embeddings, fp16), continuous batching over a seeded Poisson "
-                        f"trace per GPU: {n_req} requests at {args.rate} req/s, prompts U[64,1024] random ids, "
-                        f"{out_tokens} output tokens, greedy",
+                        f"trace of {n_all} requests at {args.rate * world:g} req/s ({args.rate:g} per GPU), "
+                        f"prompts U[64,1024] random ids, {out_tokens} output tokens, greedy",
             "kv_budget_gb": args.kv_budget_gb,
             "num_blocks": num_blocks,
-            "parallelism": f"dp{world}: one runner, pool and trace per GPU",
+            "requests_this_rank": n_req,
+            "parallelism": f"dp{world}: one runner and pool per GPU; requests routed by least outstanding tokens "
+                           "(the same deterministic assignment computed on every rank, no exchange)",
         },
         "elapsed_s": round(elapsed_max, 3),
         "generated_tokens": int(gen_all),

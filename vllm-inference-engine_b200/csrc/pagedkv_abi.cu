@@ -1,5 +1,7 @@
 // C ABI of the pagedkv library: argument validation, kernel selection and the
 // device error word. Declarations and contracts live in include/pagedkv.h.
+#include <nvtx3/nvToolsExt.h>
+
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -33,6 +35,16 @@ int fail(int code, const char *fmt, ...) {
 int cuda_fail(cudaError_t e, const char *what) {
   return fail(PAGEDKV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
+
+// One NVTX range per call of a launching entry point, named after it, so a
+// profiler timeline (nsys, ncu --nvtx) shows every layer's host call around the
+// kernels it launched. With no tool attached a range costs a pointer test.
+struct NvtxRange {
+  explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange &) = delete;
+  NvtxRange &operator=(const NvtxRange &) = delete;
+};
 
 constexpr int kMaxDevices = 64;
 
@@ -125,6 +137,7 @@ int pagedkv_decode_attention(void *out, int64_t out_stride_seq, int64_t out_stri
                              int64_t num_blocks, int32_t block_size, int32_t max_blocks_per_seq,
                              float scale, int32_t dtype, void *workspace, size_t workspace_bytes,
                              void *stream) {
+  NvtxRange nvtx("pagedkv_decode_attention");
   t_last_launches = 0;
   t_last_kernel = "none";
   if (num_seqs < 0) return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "num_seqs must be >= 0 (got %d)", num_seqs);
@@ -229,6 +242,7 @@ int pagedkv_kv_append(void *k_cache, void *v_cache, const void *k_new, int64_t k
                       int64_t v_new_stride_head, const int64_t *slot_mapping, int32_t num_tokens,
                       int32_t num_kv_heads, int32_t head_dim, int64_t num_blocks,
                       int32_t block_size, int32_t dtype, void *stream) {
+  NvtxRange nvtx("pagedkv_kv_append");
   if (num_tokens < 0) return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "num_tokens must be >= 0");
   if (num_tokens == 0) return PAGEDKV_OK;
   if (dtype != PAGEDKV_DTYPE_F16 && dtype != PAGEDKV_DTYPE_BF16)
@@ -255,6 +269,7 @@ int pagedkv_kv_append(void *k_cache, void *v_cache, const void *k_new, int64_t k
 int pagedkv_copy_blocks(void *const *k_cache_ptrs, void *const *v_cache_ptrs, int32_t num_layers,
                         const int64_t *block_mapping, int32_t num_pairs, int64_t block_bytes,
                         int64_t num_blocks, void *stream) {
+  NvtxRange nvtx("pagedkv_copy_blocks");
   if (num_pairs < 0 || num_layers < 0)
     return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "num_pairs and num_layers must be >= 0");
   if (num_pairs == 0 || num_layers == 0) return PAGEDKV_OK;
@@ -283,6 +298,7 @@ int pagedkv_kv_append_rope(void *q_out, int64_t q_out_stride_tok, int64_t q_out_
                            int64_t cos_sin_stride_tok, const int64_t *slot_mapping, int32_t num_tokens,
                            int32_t num_kv_heads, int32_t head_dim, int64_t num_blocks, int32_t block_size,
                            int32_t dtype, void *stream) {
+  NvtxRange nvtx("pagedkv_kv_append_rope");
   if (num_tokens < 0) return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "num_tokens must be >= 0");
   if (num_tokens == 0) return PAGEDKV_OK;
   if (dtype != PAGEDKV_DTYPE_F16 && dtype != PAGEDKV_DTYPE_BF16)
@@ -337,6 +353,7 @@ int pagedkv_kv_write_prefill(void *const *k_caches, void *const *v_caches, const
                              int32_t src_dtype, const int64_t *block_ids, int32_t num_write_blocks,
                              int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
                              int64_t num_blocks, int32_t block_size, int32_t dtype, void *stream) {
+  NvtxRange nvtx("pagedkv_kv_write_prefill");
   if (num_layers < 0 || num_write_blocks < 0 || num_tokens < 0)
     return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "num_layers, num_write_blocks, num_tokens must be >= 0");
   if (num_layers == 0 || num_write_blocks == 0) return PAGEDKV_OK;

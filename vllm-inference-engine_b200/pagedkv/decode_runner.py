@@ -98,6 +98,7 @@ class PagedDecodeRunner:
 
     # ---- prefill ---------------------------------------------------------------
     @torch.inference_mode()
+    @torch.cuda.nvtx.range("pagedkv.prefill")
     def prefill(self, prompt_ids: Sequence[int], max_new_tokens: int) -> Sequence_:
         """Run the prompt through the model, write its K/V into freshly
         allocated blocks of every layer (one launch) and sample the first token."""
@@ -183,6 +184,7 @@ class PagedDecodeRunner:
         return self._host[bsz]
 
     @torch.inference_mode()
+    @torch.cuda.nvtx.range("pagedkv.decode_step")
     def decode_step(self, seqs: List[Sequence_], return_logits: bool = False) -> Optional[torch.Tensor]:
         """Append each sequence's last token and sample the next one. With
         ``return_logits`` the step runs eagerly on the padded batch and also
