@@ -117,3 +117,27 @@ def test_groups_wider_than_a_tile_run_in_chunks(cuda_ready, d, g, hkv, dtype):
     _check_vs_oracle(cuda_ready, q, k, v, tables, lists, lens_t, 1 / math.sqrt(d), **tol)
     assert pagedkv.last_decode_launch_info()[1] == "tc"
     assert pagedkv.read_error_flags(cuda_ready) == 0
+
+
+@pytest.mark.parametrize(
+    "g,hkv,bs,dtype",
+    [
+        (1, 2, 16, torch.float16),
+        (2, 8, 16, torch.float16),    # Gemma-2-9B-like: 16 query / 8 kv heads
+        (7, 1, 8, torch.float16),
+        (16, 2, 16, torch.bfloat16),
+        (20, 1, 128, torch.float16),  # chunks of 16 + 4 query heads
+        (32, 2, 16, torch.float16),   # two full chunks
+    ],
+)
+def test_head_dim_256_on_tensor_cores(cuda_ready, g, hkv, bs, dtype):
+    """head_dim 256: each head is two 128-element sub-rows (two K and two V ring
+    stages per tile, S summed over both, one O accumulator each); partial last
+    blocks, short and long sequences cut across CTAs."""
+    lens = [1, 37, 128, 129, 2000, 9000]
+    q, k, v, tables, lists, lens_t = _random_case(256 * 100 + g, len(lens), g * hkv, hkv, 256, bs, lens,
+                                                  q_scale=4.0, dtype=dtype)
+    tol = dict(atol=8e-3, rtol=8e-3) if dtype == torch.bfloat16 else {}
+    _check_vs_oracle(cuda_ready, q, k, v, tables, lists, lens_t, 1 / 16.0, **tol)
+    assert pagedkv.last_decode_launch_info()[1] == "tc"
+    assert pagedkv.read_error_flags(cuda_ready) == 0

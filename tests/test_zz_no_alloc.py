@@ -58,7 +58,7 @@ def _noalloc(out, q, k, v, tables, lens, scale):
     [
         (256, 14, 2, 64, 16, "cfg2"),    # tensor-core path, cut segments combined across CTAs
         (6, 56, 8, 128, 16, "varlen"),   # tensor-core path, head_dim 128, ragged lengths
-        (5, 8, 4, 256, 16, "simt"),      # CUDA-core split-K path (head_dim 256)
+        (5, 8, 4, 64, 4, "simt"),        # CUDA-core split-K path (block_size 4)
     ],
 )
 def test_noalloc_matches_workspace_entry_point_twice(shape):
@@ -86,9 +86,9 @@ def test_noalloc_matches_workspace_entry_point_twice(shape):
 def test_noalloc_rejects_shapes_beyond_its_scratch():
     assert torch.cuda.is_available(), "GPU test selected but no CUDA device is visible"
     dev = torch.device("cuda", 0)
-    # One long sequence on the CUDA-core split-K path (head_dim 256): it is
-    # split into ~1200 chunks whose partials need ~9.7 MB, beyond the 4 MiB.
-    n, hq, hkv, d, bs, width = 1, 8, 1, 256, 16, 18944
+    # One long sequence on the CUDA-core split-K path (block_size 4): it is
+    # split into ~1200 chunks whose partials need ~9.8 MB, beyond the 4 MiB.
+    n, hq, hkv, d, bs, width = 1, 8, 1, 256, 4, 75776
     q = torch.zeros(n, hq, d, dtype=torch.half, device=dev)
     k = torch.zeros(64, bs, hkv, d, dtype=torch.half, device=dev)
     tables = torch.zeros(n, width, dtype=torch.int32, device=dev)

@@ -207,21 +207,21 @@ struct Walker {
 
 // Running (sum, denominator, reference max) of one correction thread's
 // query columns.
-template <int GP>
+template <int GP, int D2>
 struct PieceAcc {
-  float acc[GP], lsum[GP], msel[GP];
+  float acc[D2][GP], lsum[GP], msel[GP];
 };
 
 // Stream-K combine, run by the 128 correction threads of the CTA holding a
 // cut segment's first tile: wait for the partials CTAs b+1..b1 published, fold
 // them into this CTA's piece, store the normalised output and clear the flags
 // (at most once per CTA per launch).
-template <typename T, int GP, int D>
-__device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP> a, int64_t b1, int hl, int dim,
+template <typename T, int GP, int D, int D2>
+__device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP, D2> a, int64_t b1, int hl, int dim,
                                             int gn, bool have_kv, T *out, volatile int *abort_flag, int row) {
   using E = Elem<T>;
   const DecodeParams &p = tp.p;
-  const int HQS = (128 / D) * GP;  // partial slots per CTA
+  const int HQS = (128 * D2 / D) * GP;  // partial slots per CTA
   if (row == 0) {
     for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) {
       const uint64_t t0 = globaltimer_ns();
@@ -240,18 +240,26 @@ __device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP> 
       for (int g = 0; g < GP; ++g) {
         if (g < gn) {
           const float2 ml = __ldcg(&tp.part_ml[hh0 + g]);
-          const float av = __ldcg(&tp.part_acc[(hh0 + g) * D + dim]);
           const float mb = fmaxf(a.msel[g], ml.x);
           const float sc = a.msel[g] == kNegInf ? 0.f : fast_exp2(a.msel[g] - mb);
           const float f = ml.x == kNegInf ? 0.f : fast_exp2(ml.x - mb);
           a.lsum[g] = fmaf(f, ml.y, a.lsum[g] * sc);
-          a.acc[g] = fmaf(f, av, a.acc[g] * sc);
+#pragma unroll
+          for (int sub = 0; sub < D2; ++sub) {
+            const float av = __ldcg(&tp.part_acc[(hh0 + g) * D + sub * 128 + dim]);
+            a.acc[sub][g] = fmaf(f, av, a.acc[sub][g] * sc);
+          }
           a.msel[g] = mb;
         }
       }
     }
     for (int g = 0; g < GP; ++g)
-      if (g < gn) out[(int64_t)g * p.o_sh] = E::from_float(a.lsum[g] > 0.f ? __fdividef(a.acc[g], a.lsum[g]) : 0.f);
+      if (g < gn) {
+#pragma unroll
+        for (int sub = 0; sub < D2; ++sub)
+          out[(int64_t)g * p.o_sh + sub * 128] =
+              E::from_float(a.lsum[g] > 0.f ? __fdividef(a.acc[sub][g], a.lsum[g]) : 0.f);
+      }
   }
   named_bar(2, 128);  // every partner partial read before its flag is cleared
   if (row == 0) {
@@ -267,9 +275,10 @@ struct MiscSmem {
   long long lo, hi, total, grid, u0;
 };
 
-template <int N, int SK, int SV>
+template <int N, int SK, int SV, int D2 = 1>
 struct SmemLayout {
-  static constexpr int kQBytes = 2 * N * 128;  // B operand [N x 128], two K-halves
+  static constexpr int kQSubBytes = 2 * N * 128;     // B operand [N x 128], two K-halves
+  static constexpr int kQBytes = D2 * kQSubBytes;    // one per 128-element sub-row of a head
   static constexpr int kPBytes = N * 256;      // B operand P^T, MN-major SW32: N/16 atoms x 4 KB
   static constexpr int kSlotBytes = 8 * N + 16;  // per-tile rescale record, see RescaleSlot
   static constexpr int kOffK = 0;                               // K ring: SK tiles
@@ -305,15 +314,20 @@ struct RescaleSlot {
 
 // CH: the group is wider than GP and runs in tp.chunks query-head chunks (a
 // separate instantiation, so the single-chunk kernels carry none of it).
-template <typename T, int H, int GP, int N, int SK, int SV, bool CH>
+// D2: 128-element sub-rows per head (2 for head_dim 256: every tile is two K
+// and two V ring stages, S sums both, O has one accumulator per sub-row).
+template <typename T, int H, int GP, int N, int SK, int SV, bool CH, int D2>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
                  const __grid_constant__ CUtensorMap tmap_v, const __grid_constant__ TcParams tp) {
-  using L = SmemLayout<N, SK, SV>;
+  using L = SmemLayout<N, SK, SV, D2>;
   using E = Elem<T>;
   using Slot = RescaleSlot<N>;
-  constexpr int D = 128 / H;                          // head_dim
-  constexpr uint32_t kCols = 4 * N;                  // TMEM: S[2] then O[2]
+  constexpr int D = 128 * D2 / H;                     // head_dim
+  // TMEM: S[2] then O[2][D2], N columns each, rounded up to a power of two
+  constexpr uint32_t kColsUsed = (2 + 2 * D2) * N;
+  constexpr uint32_t kCols = kColsUsed <= 64 ? 64 : kColsUsed <= 128 ? 128 : 256;
+  static_assert(D2 == 1 || H == 1, "a head wider than a tile row has the tile row to itself");
   constexpr uint32_t kFmt = E::kDtype == PAGEDKV_DTYPE_BF16 ? 1u : 0u;
   constexpr uint32_t kIdescS = idesc_f16(kFmt, N, false, false);
   constexpr uint32_t kIdescO = idesc_f16(kFmt, N, true, true);
@@ -495,7 +509,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     // the group is split, where the next chunk's segment re-reads them from L2.
     const uint64_t policy = CH ? l2_policy_evict_normal() : l2_policy_evict_first();
     const int bpt = kTile / p.block_size;  // blocks per tile: 1..16, divides 32
-    constexpr int kQChunks = 16 * N / 32;  // Q 16-byte chunks per lane
+    constexpr int kQChunks = 16 * N * D2 / 32;  // Q 16-byte chunks per lane
     int stage = 0;
     uint32_t sphase = 0;
     uint32_t qi = 0;
@@ -539,8 +553,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 #pragma unroll
       for (int c = 0; c < kQChunks; ++c) {
         const int idx = lane + c * 32;
-        const int xh = idx / (8 * N);
-        const int rem = idx - xh * 8 * N;
+        const int sub = idx / (16 * N);  // 128-element sub-row of the head
+        const int ix = idx - sub * 16 * N;
+        const int xh = ix / (8 * N);
+        const int rem = ix - xh * 8 * N;
         const int n = rem >> 3, ch = rem & 7;
         const int hl = n / GP, g = n - hl * GP;
         const int qrow = q.hg / nch;
@@ -548,12 +564,13 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         const int gq = (q.hg - qrow * nch) * GP + g;  // query head within the kv head's group
         // Element e of the 128-wide row belongs to kv head e / D of the group:
         // query column n (head hl) is nonzero only on its own head's D elements.
-        const int e = xh * 64 + ch * 8;
+        const int e = sub * 128 + xh * 64 + ch * 8;
         const bool in = hl < H && gq < p.group && kv < p.hkv && e / D == hl;
         const int d = e - hl * D;
         const T *src = reinterpret_cast<const T *>(p.q) +
                        (in ? (int64_t)q.seq * p.q_ss + (int64_t)(kv * p.group + gq) * p.q_sh + d : 0);
-        const uint32_t addr = qbuf + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
+        const uint32_t addr =
+            qbuf + sub * L::kQSubBytes + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
         cp_async_16(addr, src, in ? 16u : 0u);
       }
       cp_async_mbar_arrive(q_full(i));
@@ -570,7 +587,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       if (is_k && have_nx && !q_issue(nx, qi++)) break;
       const int lb0 = pc.t0 / p.block_size;
       const int need = (pc.t1 + p.block_size - 1) / p.block_size;
-      const int x0 = pc.hg / nch * 128;  // this tile row's first element
+      const int x0 = pc.hg / nch * 128 * D2;  // this tile row's first element
       for (int j = 0; j < pc.ntiles; ++j) {
         const int wofs = (j * bpt) & 31;
         if (wofs == 0) {
@@ -583,35 +600,38 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         }
         const uint32_t slot = wk % 3u;
         if (wofs + bpt >= 32 || j + 1 == pc.ntiles) ++wk;  // last tile of this window
-        if (!PKV_TW(1, mbar_wait(is_k ? kempty(stage) : vempty(stage), sphase ^ 1u, abort_flag, kTimeoutNs))) {
-          ok = false;
-          break;
-        }
-        const uint32_t full = is_k ? kfull(stage) : vfull(stage);
-        if (lane == 0) mbar_arrive_expect_tx(full, kOperandBytes);
-        __syncwarp();
-        if (lane < 2 * bpt) {
-          // lane -> (block b of the tile, 64-element half h)
-          const int h = lane >= bpt ? 1 : 0;
-          const int b = lane - h * bpt;
-          const int lb = lb0 + j * bpt + b;
-          int32_t y = tp.oob_row;  // out of range: TMA fills zeros, reads nothing
-          if (lb < need) {
-            const int32_t blk = win[slot * 32 + wofs + b];
-            if (blk >= 0 && blk < p.num_blocks) {
-              y = blk * p.block_size;
-            } else if (is_k && h == 0) {
-              set_error(p.err, PAGEDKV_EFLAG_BLOCK_ID_RANGE);
-            }
+        for (int sub = 0; sub < D2; ++sub) {  // one ring stage per 128-element sub-row
+          if (!PKV_TW(1, mbar_wait(is_k ? kempty(stage) : vempty(stage), sphase ^ 1u, abort_flag, kTimeoutNs))) {
+            ok = false;
+            break;
           }
-          const uint32_t dst = ring + stage * kOperandBytes + h * kHalfBytes + b * p.block_size * 128;
-          tma_load_2d(dst, tmap, x0 + h * 64, y, full, policy);
+          const uint32_t full = is_k ? kfull(stage) : vfull(stage);
+          if (lane == 0) mbar_arrive_expect_tx(full, kOperandBytes);
+          __syncwarp();
+          if (lane < 2 * bpt) {
+            // lane -> (block b of the tile, 64-element half h)
+            const int h = lane >= bpt ? 1 : 0;
+            const int b = lane - h * bpt;
+            const int lb = lb0 + j * bpt + b;
+            int32_t y = tp.oob_row;  // out of range: TMA fills zeros, reads nothing
+            if (lb < need) {
+              const int32_t blk = win[slot * 32 + wofs + b];
+              if (blk >= 0 && blk < p.num_blocks) {
+                y = blk * p.block_size;
+              } else if (is_k && h == 0 && sub == 0) {
+                set_error(p.err, PAGEDKV_EFLAG_BLOCK_ID_RANGE);
+              }
+            }
+            const uint32_t dst = ring + stage * kOperandBytes + h * kHalfBytes + b * p.block_size * 128;
+            tma_load_2d(dst, tmap, x0 + sub * 128 + h * 64, y, full, policy);
+          }
+          ++issued;
+          if (++stage == nst) {
+            stage = 0;
+            sphase ^= 1u;
+          }
         }
-        ++issued;
-        if (++stage == nst) {
-          stage = 0;
-          sphase ^= 1u;
-        }
+        if (!ok) break;
       }
       pc = nx;
       have = have_nx;
@@ -645,27 +665,34 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       const uint32_t qbuf = sbase + L::kOffQ + (qi % kQSlots) * L::kQBytes;
       for (int j = 0; j < pc.ntiles; ++j) {
         const uint32_t b = gt & 1u;
-        if (!PKV_TW(1, mbar_wait(kfull(kst), kph, abort_flag, kTimeoutNs))) { ok = false; break; }
-        if (!PKV_TW(2, mbar_wait(bar2(1, b), ((gt >> 1) & 1u) ^ 1u, abort_flag, kTimeoutNs))) { ok = false; break; }
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t ka = sbase + L::kOffK + kst * kOperandBytes;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t ad = smem_desc_sw128(ka + (kk >> 2) * kHalfBytes + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = smem_desc_sw128(qbuf + (kk >> 2) * (N * 128) + (kk & 3) * 32, 16, 1024);
-            mma_f16_ss(tmem + b * N, ad, bd, kIdescS, kk > 0 ? 1u : 0u);
+        for (int sub = 0; sub < D2; ++sub) {  // S sums the sub-rows' products
+          if (!PKV_TW(1, mbar_wait(kfull(kst), kph, abort_flag, kTimeoutNs))) { ok = false; break; }
+          if (sub == 0 && !PKV_TW(2, mbar_wait(bar2(1, b), ((gt >> 1) & 1u) ^ 1u, abort_flag, kTimeoutNs))) {
+            ok = false;
+            break;
           }
-          mma_commit(bar2(0, b));   // s_full
-          mma_commit(kempty(kst));  // K tile read: free it for the next load
-          if (j + 1 == pc.ntiles) mma_commit(q_empty(qi));  // piece's last S: Q read
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t ka = sbase + L::kOffK + kst * kOperandBytes;
+            const uint32_t qsub = qbuf + sub * L::kQSubBytes;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint64_t ad = smem_desc_sw128(ka + (kk >> 2) * kHalfBytes + (kk & 3) * 32, 16, 1024);
+              const uint64_t bd = smem_desc_sw128(qsub + (kk >> 2) * (N * 128) + (kk & 3) * 32, 16, 1024);
+              mma_f16_ss(tmem + b * N, ad, bd, kIdescS, (sub > 0 || kk > 0) ? 1u : 0u);
+            }
+            if (sub + 1 == D2) mma_commit(bar2(0, b));  // s_full
+            mma_commit(kempty(kst));  // K stage read: free it for the next load
+            if (sub + 1 == D2 && j + 1 == pc.ntiles) mma_commit(q_empty(qi));  // piece's last S: Q read
+          }
+          __syncwarp();
+          if (++kst == SK) {
+            kst = 0;
+            kph ^= 1u;
+          }
         }
-        __syncwarp();
+        if (!ok) break;
         ++gt;
-        if (++kst == SK) {
-          kst = 0;
-          kph ^= 1u;
-        }
       }
       ++qi;
       pc = nx;
@@ -691,47 +718,52 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       for (int j = 0; j < pc.ntiles; ++j) {
         const uint32_t b = gt & 1u;
         const uint32_t bph = (gt >> 1) & 1u;
-        if (!PKV_TW(3, mbar_wait(vfull(vst), vph, abort_flag, kTimeoutNs))) { ok = false; break; }
-        const uint32_t va = sbase + L::kOffV + vst * kOperandBytes;
-        // Rows of the last block past the sequence end hold stale pool data:
-        // zero them so 0 * (non-finite stale value) never reaches the sum.
-        const int tile_t0 = pc.t0 + j * kTile;
-        if (pc.t1 == pc.len && tile_t0 + kTile >= pc.len && (pc.len % p.block_size) != 0) {
-          const int r0 = pc.len - tile_t0;  // first stale row in the tile
-          const int r1 = ((pc.len + p.block_size - 1) / p.block_size) * p.block_size - tile_t0;
-          const int chunks = (r1 - r0) * 8 * 2;
-          for (int idx = lane; idx < chunks; idx += 32) {
-            const int xh = idx / ((r1 - r0) * 8);
-            const int rr = idx - xh * (r1 - r0) * 8;
-            const uint32_t addr = va + xh * kHalfBytes + (r0 + (rr >> 3)) * 128 + (rr & 7) * 16;
-            asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(addr), "r"(0u) : "memory");
+        for (int sub = 0; sub < D2; ++sub) {  // one O accumulator per sub-row
+          if (!PKV_TW(3, mbar_wait(vfull(vst), vph, abort_flag, kTimeoutNs))) { ok = false; break; }
+          const uint32_t va = sbase + L::kOffV + vst * kOperandBytes;
+          // Rows of the last block past the sequence end hold stale pool data:
+          // zero them so 0 * (non-finite stale value) never reaches the sum.
+          const int tile_t0 = pc.t0 + j * kTile;
+          if (pc.t1 == pc.len && tile_t0 + kTile >= pc.len && (pc.len % p.block_size) != 0) {
+            const int r0 = pc.len - tile_t0;  // first stale row in the tile
+            const int r1 = ((pc.len + p.block_size - 1) / p.block_size) * p.block_size - tile_t0;
+            const int chunks = (r1 - r0) * 8 * 2;
+            for (int idx = lane; idx < chunks; idx += 32) {
+              const int xh = idx / ((r1 - r0) * 8);
+              const int rr = idx - xh * (r1 - r0) * 8;
+              const uint32_t addr = va + xh * kHalfBytes + (r0 + (rr >> 3)) * 128 + (rr & 7) * 16;
+              asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(addr), "r"(0u) : "memory");
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
           }
-          fence_proxy_async_smem();
-          __syncwarp();
-        }
-        if (!PKV_TW(4, mbar_wait(bar2(2, b), bph, abort_flag, kTimeoutNs))) { ok = false; break; }
-        if (!PKV_TW(5, mbar_wait(bar2(5, b), bph ^ 1u, abort_flag, kTimeoutNs))) { ok = false; break; }
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t pbuf = sbase + L::kOffP + b * L::kPBytes;
+          if (sub == 0) {
+            if (!PKV_TW(4, mbar_wait(bar2(2, b), bph, abort_flag, kTimeoutNs))) { ok = false; break; }
+            if (!PKV_TW(5, mbar_wait(bar2(5, b), bph ^ 1u, abort_flag, kTimeoutNs))) { ok = false; break; }
+          }
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t pbuf = sbase + L::kOffP + b * L::kPBytes;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            // A = V^T: MN-major SW128, 64-element atoms 16 KB apart (LBO), 8-token groups 1 KB apart (SBO)
-            const uint64_t ad = smem_desc_sw128(va + kk * 2048, kHalfBytes, 1024);
-            // B = P^T: MN-major SW32, 16-column atoms 4 KB apart (LBO), 8-token groups 256 B apart (SBO)
-            const uint64_t bd = smem_desc(pbuf + kk * 512, 4096, 256, kLayoutSwizzle32);
-            mma_f16_ss(tmem + 2 * N + b * N, ad, bd, kIdescO, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < 8; ++kk) {
+              // A = V^T: MN-major SW128, 64-element atoms 16 KB apart (LBO), 8-token groups 1 KB apart (SBO)
+              const uint64_t ad = smem_desc_sw128(va + kk * 2048, kHalfBytes, 1024);
+              // B = P^T: MN-major SW32, 16-column atoms 4 KB apart (LBO), 8-token groups 256 B apart (SBO)
+              const uint64_t bd = smem_desc(pbuf + kk * 512, 4096, 256, kLayoutSwizzle32);
+              mma_f16_ss(tmem + 2 * N + (b * D2 + sub) * N, ad, bd, kIdescO, kk > 0 ? 1u : 0u);
+            }
+            if (sub + 1 == D2) mma_commit(bar2(4, b));  // o_full
+            mma_commit(vempty(vst));                     // V stage read
+            if (sub + 1 == D2) mma_commit(bar2(3, b));  // p_empty
           }
-          mma_commit(bar2(4, b));   // o_full
-          mma_commit(vempty(vst));  // V tile read
-          mma_commit(bar2(3, b));   // p_empty
+          __syncwarp();
+          if (++vst == SV) {
+            vst = 0;
+            vph ^= 1u;
+          }
         }
-        __syncwarp();
+        if (!ok) break;
         ++gt;
-        if (++vst == SV) {
-          vst = 0;
-          vph ^= 1u;
-        }
       }
       pc = nx;
       have = have_nx;
@@ -919,10 +951,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     while (have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
-      float acc[GP], msel[GP];
+      float acc[D2][GP], msel[GP];  // acc[sub]: dims sub * 128 + dim
 #pragma unroll
       for (int g = 0; g < GP; ++g) {
-        acc[g] = 0.f;
+#pragma unroll
+        for (int sub = 0; sub < D2; ++sub) acc[sub][g] = 0.f;
         msel[g] = kNegInf;
       }
       for (int j = 0; j < pc.ntiles; ++j) {
@@ -941,17 +974,21 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         }
         PKV_TW(1, mbar_wait(bar2(4, b), (gt >> 1) & 1u, abort_flag, kTimeoutNs));
         tc_fence_after();
-        float o[GP];
-        tmem_ld<GP>(tl + 2 * N + b * N + hl * GP, o);
+        float o[D2][GP];
+#pragma unroll
+        for (int sub = 0; sub < D2; ++sub) tmem_ld<GP>(tl + 2 * N + (b * D2 + sub) * N + hl * GP, o[sub]);
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(bar2(5, b));
-        if (resc) {
 #pragma unroll
-          for (int g = 0; g < GP; ++g) acc[g] = fmaf(acc[g], a[g], o[g]);
-        } else {
+        for (int sub = 0; sub < D2; ++sub) {
+          if (resc) {
 #pragma unroll
-          for (int g = 0; g < GP; ++g) acc[g] += o[g];
+            for (int g = 0; g < GP; ++g) acc[sub][g] = fmaf(acc[sub][g], a[g], o[sub][g]);
+          } else {
+#pragma unroll
+            for (int g = 0; g < GP; ++g) acc[sub][g] += o[sub][g];
+          }
         }
         ++gt;
       }
@@ -980,8 +1017,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 #pragma unroll
           for (int g = 0; g < GP; ++g) {
             if (g < gn) {
-              const float v = lsum[g] > 0.f ? __fdividef(acc[g], lsum[g]) : 0.f;
-              out[(int64_t)g * p.o_sh] = E::from_float(v);
+#pragma unroll
+              for (int sub = 0; sub < D2; ++sub) {
+                const float v = lsum[g] > 0.f ? __fdividef(acc[sub][g], lsum[g]) : 0.f;
+                out[(int64_t)g * p.o_sh + sub * 128] = E::from_float(v);
+              }
             }
           }
         }
@@ -994,7 +1034,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           for (int g = 0; g < GP; ++g) {
             if (g < gn) {
               const int64_t hh = (int64_t)blockIdx.x * HQS + hl * GP + g;
-              tp.part_acc[hh * D + dim] = acc[g];
+#pragma unroll
+              for (int sub = 0; sub < D2; ++sub) tp.part_acc[hh * D + sub * 128 + dim] = acc[sub][g];
               if (dim == 0) tp.part_ml[hh] = make_float2(msel[g], lsum[g]);
             }
           }
@@ -1009,14 +1050,15 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         // CTA's range: this is this CTA's last piece, and this CTA combines.
         // The other pieces are the first pieces of CTAs b+1..b1, published
         // early in their runs.
-        PieceAcc<GP> pa;
+        PieceAcc<GP, D2> pa;
 #pragma unroll
         for (int g = 0; g < GP; ++g) {
-          pa.acc[g] = acc[g];
+#pragma unroll
+          for (int sub = 0; sub < D2; ++sub) pa.acc[sub][g] = acc[sub][g];
           pa.lsum[g] = lsum[g];
           pa.msel[g] = msel[g];
         }
-        combine_pieces<T, GP, D>(tp, pa, owner_of(pc.seg_units + kSegUnits + (int64_t)pc.seg_tiles * kTileUnits - 1, U_total, G), hl, dim, gn,
+        combine_pieces<T, GP, D, D2>(tp, pa, owner_of(pc.seg_units + kSegUnits + (int64_t)pc.seg_tiles * kTileUnits - 1, U_total, G), hl, dim, gn,
                                  have_kv, out, abort_flag, row);
       }
 #ifdef PAGEDKV_TRACE
@@ -1062,7 +1104,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 // ---- host side ----------------------------------------------------------------
 
 struct TcPlan {
-  int H, GP, N, stages, head_groups, chunks, grid;
+  int H, D2, GP, N, stages, head_groups, chunks, grid;
 };
 
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
@@ -1070,12 +1112,16 @@ int round_up(int x, int m) { return (x + m - 1) / m * m; }
 TcPlan make_plan(int32_t num_seqs, int32_t hq, int32_t hkv, int32_t head_dim, int32_t max_tokens,
                  int32_t num_sms) {
   TcPlan pl;
-  pl.H = 128 / head_dim;
+  // A tile row is 128 elements: H = 128 / head_dim kv heads side by side, or
+  // for head_dim 256 one head as D2 = 2 sub-rows (two ring stages per tile).
+  pl.D2 = head_dim > 128 ? head_dim / 128 : 1;
+  pl.H = head_dim > 128 ? 1 : 128 / head_dim;
   const int G = hq / hkv;
-  // Query columns per kv head: the group padded to 8, at most 32 / H (N <= 32).
+  // Query columns per kv head: the group padded to 8, at most 32 / H (N <= 32),
+  // 16 with two sub-rows (their correction threads hold twice the sums).
   // A wider group is cut into chunks of that many heads, one segment each; the
   // chunks of a tile row run back to back and re-read its K/V from L2.
-  const int gp_max = pl.H == 1 ? 32 : 16 / (pl.H / 2);
+  const int gp_max = pl.D2 > 1 ? 16 : pl.H == 1 ? 32 : 16 / (pl.H / 2);
   pl.chunks = (G + gp_max - 1) / gp_max;
   pl.GP = pl.chunks > 1 ? gp_max : round_up(G, 8);
   if (pl.H == 1 && pl.GP > 16) pl.GP = 32;  // one kv head per tile: columns 17..32 share the N = 32 variant
@@ -1172,11 +1218,12 @@ bool make_map(CUtensorMap *map, const void *base, int dtype, uint64_t row_elems,
   return true;
 }
 
-template <typename T, int H, int GP, int N, int SK, int SV, bool CH = false>
+template <typename T, int H, int GP, int N, int SK, int SV, bool CH = false, int D2 = 1>
 cudaError_t launch_tc(const CUtensorMap &mk, const CUtensorMap &mv, const TcParams &tp, int grid,
                       cudaStream_t stream) {
-  using L = SmemLayout<N, SK, SV>;
-  auto kern = decode_tc_kernel<T, H, GP, N, SK, SV, CH>;
+  using L = SmemLayout<N, SK, SV, D2>;
+  static_assert(L::kAlloc <= 227 * 1024, "dynamic shared memory above the sm_100 per-block limit");
+  auto kern = decode_tc_kernel<T, H, GP, N, SK, SV, CH, D2>;
   // The shared-memory opt-in is a per-device function attribute: set it once
   // per device (outside any stream capture that follows the first call).
   static std::atomic<uint64_t> attr_done{0};
@@ -1207,6 +1254,13 @@ cudaError_t launch_tc(const CUtensorMap &mk, const CUtensorMap &mv, const TcPara
 template <typename T>
 cudaError_t dispatch_tc(const TcPlan &pl, const CUtensorMap &mk, const CUtensorMap &mv, const TcParams &tp,
                         cudaStream_t stream) {
+  if (pl.D2 == 2) {
+    // head_dim 256: 3 K + 2 V ring stages of half a tile each (shared memory)
+    if (pl.chunks > 1) return launch_tc<T, 1, 16, 16, 3, 2, true, 2>(mk, mv, tp, pl.grid, stream);
+    if (pl.GP == 8) return launch_tc<T, 1, 8, 16, 3, 2, false, 2>(mk, mv, tp, pl.grid, stream);
+    if (pl.GP == 16) return launch_tc<T, 1, 16, 16, 3, 2, false, 2>(mk, mv, tp, pl.grid, stream);
+    return cudaErrorInvalidValue;
+  }
   if (pl.chunks > 1) {
     if (pl.H == 1 && pl.GP == 32) return launch_tc<T, 1, 32, 32, 2, 2, true>(mk, mv, tp, pl.grid, stream);
     if (pl.H == 2 && pl.GP == 16) return launch_tc<T, 2, 16, 32, 2, 2, true>(mk, mv, tp, pl.grid, stream);
@@ -1234,13 +1288,14 @@ extern "C" int pagedkv_trace_read(unsigned long long *host, size_t count) {
 bool tc_eligible(int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size) {
   if (num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0) return false;
   const int G = num_q_heads / num_kv_heads;
-  // A tile row is 128 elements: 128 / head_dim kv heads side by side, and their
-  // query columns (padded groups) fill at most the N = 32 MMA width; wider
-  // groups run in chunks of 32 / 16 / 8 query heads per kv head. Small groups
+  // A tile row is 128 elements: 128 / head_dim kv heads side by side (or one
+  // head_dim-256 head as two sub-rows), and their query columns (padded
+  // groups) fill at most the N = 32 MMA width; wider groups run in chunks of
+  // 32 / 16 / 8 / 16 query heads per kv head. Small groups
   // run here too: the pipeline is bound by HBM, not by the MMA shape
   // (measured 1.1-2.7x faster than the CUDA-core kernel at G = 1, 2).
   if (G < 1) return false;
-  if (head_dim != 128 && head_dim != 64 && head_dim != 32) return false;
+  if (head_dim != 256 && head_dim != 128 && head_dim != 64 && head_dim != 32) return false;
   if (block_size < 8 || block_size > 128 || (block_size & (block_size - 1)) != 0) return false;
   return true;
 }
