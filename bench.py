@@ -9,7 +9,7 @@ the KV append of 256 new tokens through a slot mapping, then batched decode
 attention over all 256 contexts (which include the appended token).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload cfg1|cfg2|cfg3|cfg4|cfg4-cow|cfg5|ops] [--gqa G]
+                  [--workload cfg1|cfg2|cfg3|cfg4|cfg4-cow|cfg5|ops|d256] [--gqa G]
 
 Extra workloads (not the headline): ``cfg1`` = BASELINE config 1 (the
 reference's CPU case: 8 sequences of U[1,512] tokens, 512-block pool; the CPU
@@ -18,7 +18,8 @@ reference is timed on all host threads and on one); ``cfg3`` = config 3 (head_di
 q x30); ``cfg4`` = config 4 (512 sequences in 8 groups sharing a 1024-token
 prefix + 256 own tokens); ``cfg4-cow`` = its copy-on-write variant (each
 group's partially filled fork block is copied to a private block for every
-sequence before its append, every step).
+sequence before its append, every step); ``d256`` = the head_dim-256 mode
+(64 x 2048 tokens, 8 query / 4 kv heads; not a BASELINE config).
 
 N > 1 runs under torchrun, one process per GPU; sequences are sharded
 data-parallel (each rank owns its own pool, weak scaling) and nothing crosses
@@ -217,6 +218,23 @@ def make_workload(name: str, rank: int, gqa: int = 7) -> Workload:
             "cfg3",
             f"cfg3: KV append + paged decode attention, 128 seqs, lengths log-uniform 16..8192, head_dim 128, "
             f"{hq}q/{hkv}kv heads (GQA {gqa}), block_size 16, q x30, shuffled tables",
+            hq, hkv, d, bs, nb, tables, lens, _slots_for(tables, lens, bs), q, k_new, v_new, None,
+        )
+    if name == "d256":
+        # beyond the BASELINE configs: the head_dim-256 mode (Gemma-2-9B-like
+        # 8 query / 4 kv heads per shard), 64 sequences x 2048 tokens
+        n, hq, hkv, d, bs, ctx = 64, 8, 4, 256, 16, 2048
+        nb = n * ctx // bs + 64
+        perm = list(range(nb))
+        random.Random(46 + rank).shuffle(perm)
+        tables = torch.tensor(perm[: n * ctx // bs], dtype=torch.int32).view(n, ctx // bs)
+        lens = torch.full((n,), ctx, dtype=torch.int32)
+        g = torch.Generator().manual_seed(1300 + rank)
+        q, k_new, v_new = _qkv(g, n, hq, hkv, d)
+        return Workload(
+            "d256",
+            "d256: KV append + paged decode attention, 64 seqs x 2048 ctx, 8q/4kv heads, head_dim 256, "
+            "block_size 16, fp16, shuffled tables",
             hq, hkv, d, bs, nb, tables, lens, _slots_for(tables, lens, bs), q, k_new, v_new, None,
         )
     if name in ("cfg4", "cfg4-cow"):
@@ -576,12 +594,15 @@ def _sum_over_ranks(dist, value: float, device) -> float:
 
 
 def _read_traffic(kernel: str, workload: str) -> int | None:
+    """ncu DRAM bytes per launch of ``kernel`` on ``workload`` from
+    profiles/traffic.json (keys "kernel" for config 2, "kernel:workload" for
+    the others), or None where no capture exists."""
     p = ROOT / "profiles" / "traffic.json"
-    if not p.exists() or workload != "cfg2":
+    if not p.exists():
         return None
     try:
         data = json.loads(p.read_text())
-        entry = data.get(kernel)
+        entry = data.get(kernel if workload == "cfg2" else f"{kernel}:{workload}")
         return int(entry["bytes_per_launch"]) if entry else None
     except (ValueError, KeyError, TypeError):
         return None
@@ -1108,7 +1129,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg4-cow", "cfg5", "ops"],
+    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg4-cow", "cfg5", "ops", "d256"],
                     default="cfg2")
     ap.add_argument("--requests", type=int, default=2000, help="cfg5: requests per GPU")
     ap.add_argument("--rate", type=float, default=32.0, help="cfg5: Poisson arrival rate per GPU (req/s)")
