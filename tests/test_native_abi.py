@@ -110,3 +110,27 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_native, "LIB_PATH", tmp_path / "nope.so")
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         _native.lib()
+
+
+def test_pipeline_timeout_report_rezeroes_the_workspace_flags(monkeypatch):
+    """A decode launch that gave up (EFLAG_PIPE_TIMEOUT) may leave cross-CTA
+    completion flags set; reading the report zeroes the cached workspace's
+    8 KiB flag header and leaves the rest alone (host logic, no device)."""
+    import torch
+
+    from pagedkv import paged_attention as pa
+
+    class FakeLib:
+        def pagedkv_read_error_flags(self, out_ref, clear, stream):
+            out_ref._obj.value = _native.EFLAG_PIPE_TIMEOUT | _native.EFLAG_SLOT_RANGE
+            return _native.PAGEDKV_OK
+
+    monkeypatch.setattr(_native, "lib", lambda: FakeLib())
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 0)
+    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a, **k: None)
+    monkeypatch.setattr(pa, "_stream_handle", lambda dev: 0)
+    ws = torch.ones(16384, dtype=torch.uint8)
+    monkeypatch.setitem(pa._workspaces, 0, ws)
+    flags = pa.read_error_flags(0)
+    assert flags & _native.EFLAG_PIPE_TIMEOUT and flags & _native.EFLAG_SLOT_RANGE
+    assert int(ws[:8192].sum()) == 0 and int(ws[8192:].sum()) == 8192

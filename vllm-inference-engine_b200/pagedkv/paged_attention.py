@@ -108,7 +108,12 @@ def _debug_check(device: torch.device, what: str) -> None:
 
 def read_error_flags(device: torch.device | str | int | None = None, clear: bool = True) -> int:
     """Return (and by default clear) the device error word the kernels set when
-    they skip an out-of-range block id, slot or length. Synchronises the stream."""
+    they skip an out-of-range block id, slot or length. Synchronises the stream.
+
+    A reported pipeline timeout (``EFLAG_PIPE_TIMEOUT``) means a decode launch
+    gave up part way, possibly leaving completion flags set in its workspace
+    header; the header of this device's cached workspace is zeroed again here,
+    so the next launch starts from the state the kernels expect."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     if dev.type == "cuda" and dev.index is None:
         dev = torch.device("cuda", torch.cuda.current_device())
@@ -120,7 +125,13 @@ def read_error_flags(device: torch.device | str | int | None = None, clear: bool
     else:
         rc = _native.lib().pagedkv_read_error_flags(_native.ctypes.byref(out), int(clear), _stream_handle(dev))
     _native.check(rc, "pagedkv_read_error_flags")
-    return int(out.value)
+    flags = int(out.value)
+    if flags & _native.EFLAG_PIPE_TIMEOUT:
+        ws = _workspaces.get(dev.index)
+        if ws is not None:
+            ws[:8192].zero_()  # the cross-CTA completion flags
+            torch.cuda.synchronize(dev)
+    return flags
 
 
 def _decode_into(
