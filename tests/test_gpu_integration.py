@@ -121,3 +121,58 @@ def test_copy_on_write_then_append_keeps_the_shared_block(cuda_ready):
         assert torch.equal(pool.k_cache[layer][2], k0[layer][2])  # shared block untouched
         assert torch.equal(pool.k_cache[layer][15][:5], k0[layer][2][:5])  # copied prefix
         assert torch.equal(pool.k_cache[layer][15][5], new[0])  # appended row
+
+
+def test_runner_decode_step_batched_syncs_match_per_sequence_results(cuda_ready):
+    """integration.decode_step (installed over the reference runner's
+    decode_step) on a 2-layer random-init Qwen2 model: next tokens, pool
+    writes, host logits and logit margins equal those of the same forward
+    followed by the reference's per-sequence diagnostics."""
+    from pagedkv.decode_runner import random_qwen2
+
+    dev = cuda_ready
+    model = random_qwen2(num_layers=2, device=dev, seed=3)
+    cfg = model.config
+    hkv, d, bs, nb = cfg.num_key_value_heads, cfg.hidden_size // cfg.num_attention_heads, 16, 64
+    g = torch.Generator(device=dev).manual_seed(4)
+    kc = [torch.randn(nb, bs, hkv, d, generator=g, device=dev).half() for _ in range(2)]
+    vc = [torch.randn(nb, bs, hkv, d, generator=g, device=dev).half() for _ in range(2)]
+
+    def state():
+        pool = SimpleNamespace(k_cache=[t.clone() for t in kc], v_cache=[t.clone() for t in vc], device=dev)
+        seqs = [
+            SimpleNamespace(seq_id=0, block_table=SimpleNamespace(physical_block_ids=[5, 9], num_tokens=20),
+                            last_token_id=101, last_logits=None, last_logit_margin=None),
+            SimpleNamespace(seq_id=1, block_table=SimpleNamespace(physical_block_ids=[2], num_tokens=7),
+                            last_token_id=7, last_logits=None, last_logit_margin=None),
+            SimpleNamespace(seq_id=2, block_table=SimpleNamespace(physical_block_ids=[30, 31, 40], num_tokens=33),
+                            last_token_id=150000, last_logits=None, last_logit_margin=None),
+        ]
+        runner = SimpleNamespace(block_size=bs, device=dev, pool=pool, model=model,
+                                 allocator=SimpleNamespace(ref_counts={}))
+        return seqs, runner
+
+    seqs, runner = state()
+    got = integration.decode_step(runner, seqs, None)
+
+    seqs_e, runner_e = state()
+    with torch.inference_mode():
+        lens = []
+        for s in seqs_e:
+            s.block_table.num_tokens += 1
+            lens.append(s.block_table.num_tokens)
+        ids = torch.tensor([[s.last_token_id] for s in seqs_e], device=dev)
+        pos = torch.tensor([[n - 1] for n in lens], device=dev)
+        ctx = integration.PagedAttentionContext(pool=runner_e.pool, block_tables=[s.block_table for s in seqs_e],
+                                                seq_lens=lens, block_size=bs, is_decode=True)
+        with integration.patch_paged_attention(model, ctx):
+            logits = model(input_ids=ids, position_ids=pos, use_cache=False).logits[:, -1, :]
+        want = torch.argmax(logits, dim=-1).tolist()
+    assert got == want
+    for i, (a, b) in enumerate(zip(seqs, seqs_e)):
+        assert a.block_table.num_tokens == b.block_table.num_tokens
+        assert torch.equal(a.last_logits, logits[i].cpu())
+        top2 = torch.topk(logits[i], k=2).values
+        assert a.last_logit_margin == float((top2[0] - top2[1]).item())
+    for x, y in zip(runner.pool.k_cache + runner.pool.v_cache, runner_e.pool.k_cache + runner_e.pool.v_cache):
+        assert torch.equal(x, y)

@@ -105,13 +105,103 @@ def test_install_replaces_reference_symbols_and_uninstall_restores():
         assert integ.paged_decode_attention_forward is integration.paged_decode_attention_forward
         assert pa.naive_reference_paged_attention.__module__ == "engine.kernels.paged_attention"
         assert integ.KernelPagedManualDecode._copy_prefill_kv is integration.copy_prefill_kv
+        assert integ.KernelPagedManualDecode.decode_step is integration.decode_step
         from engine.memory.block_allocator import BlockAllocator
 
         assert BlockAllocator.lookup_prefix is prefix_index.lookup_prefix
     finally:
         integration.uninstall(saved)
     assert integ.KernelPagedManualDecode._copy_prefill_kv is not integration.copy_prefill_kv
+    assert integ.KernelPagedManualDecode.decode_step is not integration.decode_step
     from engine.memory.block_allocator import BlockAllocator
 
     assert BlockAllocator.lookup_prefix is not prefix_index.lookup_prefix
     assert (pa.paged_attention_decode_batched, integ.paged_attention_decode_batched, integ.PagedAttentionContext) == before
+
+
+def _decode_step_fixture(dtype):
+    """Sequences of every kind the reference's decode_step accepts, a fake
+    model whose logits depend on the input ids only, and a fake runner."""
+
+    class BT:
+        def __init__(self, ids, n):
+            self.physical_block_ids = list(ids)
+            self.num_tokens = n
+
+    class NoDiag:  # no last_logits attribute: no diagnostics stored
+        def __init__(self, bt, gen):
+            self.block_table = bt
+            self.generated_ids = gen
+
+    seqs = [
+        SimpleNamespace(seq_id=0, block_table=BT([3, 4], 17), last_token_id=11, last_logits=None,
+                        last_logit_margin=None),
+        {"seq_id": 1, "block_table": BT([7], 5), "last_token_id": 42},
+        NoDiag(BT([9, 10, 12], 40), [5, 77]),
+        SimpleNamespace(seq_id=3, block_table=BT([1], 15), last_token_id=3, last_logits=None,
+                        last_logit_margin=None),
+    ]
+    vocab = 257
+
+    class FakeModel:
+        def __call__(self, input_ids, position_ids, use_cache):
+            rows = []
+            for tok, pos in zip(input_ids[:, 0].tolist(), position_ids[:, 0].tolist()):
+                g = torch.Generator().manual_seed(tok * 1000 + pos)
+                rows.append((torch.randn(vocab, generator=g) * 4).to(dtype))
+            return SimpleNamespace(logits=torch.stack(rows)[:, None, :])
+
+    runner = SimpleNamespace(block_size=16, device=torch.device("cpu"), pool=SimpleNamespace(device="cpu"),
+                             model=FakeModel(), allocator=SimpleNamespace(ref_counts={3: 1, 4: 1, 7: 1}))
+    return seqs, runner
+
+
+class _NullPatch:
+    def __init__(self, *a, **k):
+        pass
+
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
+
+
+@pytest.mark.skipif(not (REFERENCE / "engine").exists(), reason="reference checkout not present")
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_decode_step_matches_the_reference_with_batched_syncs(monkeypatch, dtype):
+    """integration.decode_step against the reference's own
+    KernelPagedManualDecode.decode_step on the same sequences and logits: the
+    same next tokens, length bumps, last_logits and logit margins (the model
+    forward is a fake; the kernels are covered by the GPU tests)."""
+    if str(REFERENCE) not in sys.path:
+        sys.path.insert(0, str(REFERENCE))
+    import engine.kernels.paged_attention_integration as integ
+
+    seqs_ref, runner_ref = _decode_step_fixture(dtype)
+    seqs_new, runner_new = _decode_step_fixture(dtype)
+    for mod in (integ, integration):
+        monkeypatch.setattr(mod, "patch_paged_attention", _NullPatch)
+        monkeypatch.setattr(mod, "PagedAttentionContext", lambda **k: None)
+    want = integ.KernelPagedManualDecode.decode_step(runner_ref, seqs_ref, None)
+    got = integration.decode_step(runner_new, seqs_new, None)
+    assert got == want
+    for a, b in zip(seqs_ref, seqs_new):
+        f = (lambda s, k: s[k]) if isinstance(a, dict) else getattr
+        assert f(a, "block_table").num_tokens == f(b, "block_table").num_tokens
+        if isinstance(a, dict) or hasattr(a, "last_logits"):
+            assert torch.equal(f(a, "last_logits"), f(b, "last_logits"))
+            assert f(a, "last_logit_margin") == f(b, "last_logit_margin")
+        else:
+            assert not hasattr(b, "last_logits")
+
+
+def test_decode_step_refuses_missing_and_shared_write_blocks():
+    seqs, runner = _decode_step_fixture(torch.float16)
+    seqs[0].block_table.num_tokens = 32  # write block index 2: not allocated
+    with pytest.raises(AssertionError, match="no allocated block"):
+        integration.decode_step(runner, seqs[:1], None)
+    seqs, runner = _decode_step_fixture(torch.float16)
+    runner.allocator.ref_counts[4] = 3  # seq 0 writes into block 4, now shared
+    with pytest.raises(AssertionError, match="shared"):
+        integration.decode_step(runner, seqs[:1], None)

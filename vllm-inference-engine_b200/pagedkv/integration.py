@@ -19,7 +19,10 @@ iteration (:150-160). This module provides:
   layer, no host sync) and attention by the sm_100a kernel;
 * :func:`prepare_copy_on_write` — the block bookkeeping of a copy-on-write
   append (fresh block for every sequence whose write block is shared), whose
-  data copy :func:`pagedkv.copy_blocks` performs for all layers at once.
+  data copy :func:`pagedkv.copy_blocks` performs for all layers at once;
+* :func:`decode_step` — the runner's batched decode step with its
+  per-sequence host syncs batched (installed over
+  ``KernelPagedManualDecode.decode_step``).
 """
 from __future__ import annotations
 
@@ -211,6 +214,96 @@ def patch_paged_attention(model: torch.nn.Module, context: PagedAttentionContext
                     delattr(module, attr)
 
 
+def _seq_field(seq: Any, name: str, default: Any = None) -> Any:
+    if hasattr(seq, name):
+        return getattr(seq, name)
+    if isinstance(seq, dict):
+        return seq.get(name, default)
+    return default
+
+
+@torch.inference_mode()
+def decode_step(self: Any, seqs: List[Any], allocator: Any = None) -> List[int]:
+    """``KernelPagedManualDecode.decode_step`` (integration.py:519-651) with the
+    same bookkeeping, asserts and results, and its host synchronisation
+    batched.
+
+    Per sequence, as the reference: the write slot is block
+    ``num_tokens // block_size`` of its table, which must exist and must not be
+    shared (ref count > 1); ``num_tokens`` is bumped by one; the input token is
+    ``last_token_id`` (else the last of ``generated_ids``). One forward through
+    the paged attention gives the greedy next tokens. The diagnostics the
+    reference stores per sequence (``last_logits`` on the host and
+    ``last_logit_margin`` = top-1 minus top-2 logit, in the logits' dtype) come
+    from one top-2 over the batch and two device-to-host copies in all, instead
+    of a ``.cpu()``, a ``topk`` and an ``.item()`` sync per sequence; each
+    ``last_logits`` is a row of one host tensor of the batch's logits.
+    """
+    n = len(seqs)
+    if n == 0:
+        return []
+    allocator = allocator or self.allocator
+    seq_lens: List[int] = []
+    tables: List[Any] = []
+    last_tokens: List[int] = []
+    for seq in seqs:
+        bt = _seq_field(seq, "block_table")
+        if bt is None:
+            raise ValueError("Sequence must provide a block_table attribute or dict key.")
+        write_idx = bt.num_tokens // self.block_size
+        if write_idx >= len(bt.physical_block_ids):
+            raise AssertionError(
+                f"Decode write for seq {_seq_field(seq, 'seq_id', '?')} has no allocated block "
+                f"at logical index {write_idx}."
+            )
+        write_block = bt.physical_block_ids[write_idx]
+        if allocator.ref_counts.get(write_block, 0) > 1:
+            raise AssertionError(
+                f"Decode write for seq {_seq_field(seq, 'seq_id', '?')} would modify shared "
+                f"block {write_block} with ref_count {allocator.ref_counts[write_block]}."
+            )
+        bt.num_tokens += 1
+        seq_lens.append(bt.num_tokens)
+        tables.append(bt)
+        tok = _seq_field(seq, "last_token_id")
+        if tok is None:
+            gen = _seq_field(seq, "generated_ids")
+            if not gen:
+                raise ValueError("Sequence must provide last_token_id or non-empty generated_ids.")
+            tok = gen[-1]
+        last_tokens.append(int(tok))
+
+    # token ids and positions in one host->device copy
+    host = torch.tensor([last_tokens, [s - 1 for s in seq_lens]], dtype=torch.long)
+    if torch.device(self.device).type == "cuda":
+        host = host.pin_memory()
+    dev_ids = host.to(self.device, non_blocking=True)
+    input_ids, position_ids = dev_ids[0].unsqueeze(1), dev_ids[1].unsqueeze(1)
+    ctx = PagedAttentionContext(pool=self.pool, block_tables=tables, seq_lens=seq_lens,
+                                block_size=self.block_size, is_decode=True)
+    with patch_paged_attention(self.model, ctx):
+        step_out = self.model(input_ids=input_ids, position_ids=position_ids, use_cache=False)
+    logits = step_out.logits[:, -1, :]
+    next_t = torch.argmax(logits, dim=-1)
+    want = [i for i, s in enumerate(seqs) if hasattr(s, "last_logits") or isinstance(s, dict)]
+    if not want:
+        return next_t.tolist()
+    top2 = torch.topk(logits, k=2, dim=-1).values
+    margin = top2[:, 0] - top2[:, 1]  # in the logits' dtype, as the reference's per-row difference
+    # float64 holds every token id and every 16/32-bit margin exactly
+    packed = torch.cat([next_t.to(torch.float64), margin.to(torch.float64)]).tolist()
+    host_logits = logits.detach().cpu()
+    for i in want:
+        seq = seqs[i]
+        if hasattr(seq, "last_logits"):
+            seq.last_logits = host_logits[i]
+            seq.last_logit_margin = float(packed[n + i])
+        else:
+            seq["last_logits"] = host_logits[i]
+            seq["last_logit_margin"] = float(packed[n + i])
+    return [int(x) for x in packed[:n]]
+
+
 def prepare_copy_on_write(
     block_tables: Iterable[Any],
     allocator: Any,
@@ -338,12 +431,12 @@ def install(paged_attention_module: Any = None, integration_module: Any = None,
             if hasattr(mod, name):
                 saved[(mod, name)] = getattr(mod, name)
                 setattr(mod, name, fn)
-    # The runner's prefill write (a method, patched on the class).
+    # The runner's prefill write and decode step (methods, patched on the class).
     runner_cls = getattr(integration_module, "KernelPagedManualDecode", None)
-    if runner_cls is not None and hasattr(runner_cls, "_copy_prefill_kv"):
-        saved[(runner_cls, "_copy_prefill_kv")] = runner_cls.__dict__.get(
-            "_copy_prefill_kv", getattr(runner_cls, "_copy_prefill_kv"))
-        setattr(runner_cls, "_copy_prefill_kv", copy_prefill_kv)
+    for name, fn in (("_copy_prefill_kv", copy_prefill_kv), ("decode_step", decode_step)):
+        if runner_cls is not None and hasattr(runner_cls, name):
+            saved[(runner_cls, name)] = runner_cls.__dict__.get(name, getattr(runner_cls, name))
+            setattr(runner_cls, name, fn)
     # The allocator's prefix lookup: a per-parent index instead of a full scan
     # of the cache per block (block_allocator.py:231-252).
     if allocator_module is None:
