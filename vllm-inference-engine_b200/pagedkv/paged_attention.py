@@ -84,10 +84,6 @@ def _launch(idx: int, fn, *args) -> int:
         return fn(*args, _stream_handle(idx))
 
 
-def _aligned(t: torch.Tensor) -> bool:
-    return t.data_ptr() % 16 == 0
-
-
 def _qo_ok(t: torch.Tensor) -> bool:
     s0, s1, s2 = t.stride()
     return s2 == 1 and s0 % 8 == 0 and s1 % 8 == 0 and t.data_ptr() % 16 == 0
