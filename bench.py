@@ -919,7 +919,7 @@ def run_model(args) -> None:
     prompts = [prng.integers(0, vocab, int(L)).tolist() for L in prompt_lens]
 
     # warm-up: graphs for every bucket and one prefill, outside the timed trace
-    runner.warm_prefill(1024)
+    runner.warm_prefill(1024, batches=(2, 4, 8))
     warm = [runner.prefill(prompts[i % n_req][:64], 2) for i in range(2)]
     for b in (1, 2, 4, 8, 16, 32, 64, 128, 256):
         runner._graph_for(b)
@@ -936,20 +936,25 @@ def run_model(args) -> None:
     t0 = time.perf_counter()
     while waiting or running:
         now = time.perf_counter() - t0
-        admitted = 0
-        while (waiting and arrivals[waiting[0]] <= now and len(running) < runner.max_batch
-               and runner.can_admit(int(prompt_lens[waiting[0]]), out_tokens)):
-            i = waiting.pop(0)
+        # admit the arrived requests that fit, up to 8 per step, prefilled together
+        batch, free_blocks = [], len(runner.free)
+        while (waiting and arrivals[waiting[0]] <= now and len(running) + len(batch) < runner.max_batch
+               and len(batch) < 8):
+            i = waiting[0]
+            need = (int(prompt_lens[i]) + out_tokens + runner.block_size - 1) // runner.block_size
+            if need > free_blocks or need > runner.max_blocks_per_seq:
+                break
+            free_blocks -= need
+            batch.append(waiting.pop(0))
+        if batch:
             tp = time.perf_counter()
-            seq = runner.prefill(prompts[i], out_tokens)
+            new_seqs = runner.prefill_many([prompts[i] for i in batch], out_tokens)
             torch.cuda.synchronize(dev)
             prefill_time += time.perf_counter() - tp
-            seq.arrival = arrivals[i]
-            ttft.append(time.perf_counter() - t0 - arrivals[i])
-            running.append(seq)
-            admitted += 1
-            if admitted >= 8:  # keep decoding between bursts of arrivals
-                break
+            for i, seq in zip(batch, new_seqs):
+                seq.arrival = arrivals[i]
+                ttft.append(time.perf_counter() - t0 - arrivals[i])
+                running.append(seq)
         if running:
             td = time.perf_counter()
             runner.decode_step(running)

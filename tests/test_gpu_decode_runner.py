@@ -90,3 +90,27 @@ def test_padded_prefill_keeps_rows_and_first_token(cuda_ready, small_model):
             ra = a.k_cache[layer][sa.blocks[t // 16], t % 16].float()
             rb = b.k_cache[layer][sb.blocks[t // 16], t % 16].float()
             assert (ra - rb).abs().max().item() <= 1e-2 * max(1.0, ra.abs().max().item())
+
+
+def test_batched_prefill_matches_one_prompt_at_a_time(cuda_ready, small_model):
+    """prefill_many on prompts of different lengths (batch padded to 4 rows):
+    the same first tokens and, within GEMM rounding, the same K/V rows as
+    prefill() of each prompt alone; then decoding continues from both."""
+    prompts = [list(range(7, 7 + 45)), list(range(100, 100 + 130)), list(range(300, 300 + 3))]
+    a = PagedDecodeRunner(small_model, num_blocks=64, block_size=16, max_batch=4, max_seq_len=256)
+    b = PagedDecodeRunner(small_model, num_blocks=64, block_size=16, max_batch=4, max_seq_len=256)
+    one = [a.prefill(p, 4) for p in prompts]
+    many = b.prefill_many(prompts, 4)
+    assert [s.last_token for s in one] == [s.last_token for s in many]
+    assert [s.generated for s in many] == [[s.last_token] for s in many]
+    for sa, sb, p in zip(one, many, prompts):
+        assert sb.prompt_len == len(p) and sb.num_tokens == len(p)
+        for layer in range(small_model.config.num_hidden_layers):
+            for t in range(len(p)):
+                for pool_a, pool_b in ((a.k_cache, b.k_cache), (a.v_cache, b.v_cache)):
+                    ra = pool_a[layer][sa.blocks[t // 16], t % 16].float()
+                    rb = pool_b[layer][sb.blocks[t // 16], t % 16].float()
+                    assert (ra - rb).abs().max().item() <= 1e-2 * max(1.0, ra.abs().max().item())
+    a.decode_step(one)
+    b.decode_step(many)
+    assert [s.last_token for s in one] == [s.last_token for s in many]

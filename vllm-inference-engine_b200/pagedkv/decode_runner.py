@@ -127,6 +127,56 @@ class PagedDecodeRunner:
         self._next_id += 1
         return seq
 
+    @torch.inference_mode()
+    @torch.cuda.nvtx.range("pagedkv.prefill_many")
+    def prefill_many(self, prompts: Sequence[Sequence[int]], max_new_tokens: int) -> List[Sequence_]:
+        """Prefill several prompts in one forward: right-padded to one bucketed
+        length (causal attention keeps padding out of every real token), the
+        batch padded to a power of two with empty rows, then one prefill-write
+        launch per prompt and the first token of each from one device-to-host
+        copy. Same sequences as :meth:`prefill` on each prompt (up to the
+        rounding of a differently shaped forward)."""
+        b = len(prompts)
+        assert b >= 1
+        lens = [len(x) for x in prompts]
+        need = [(p + max_new_tokens + self.block_size - 1) // self.block_size for p in lens]
+        assert sum(need) <= len(self.free), "KV pool exhausted"
+        padded = (max(lens) + self.prefill_bucket - 1) // self.prefill_bucket * self.prefill_bucket
+        rows = 1
+        while rows < b:
+            rows *= 2
+        ids = torch.zeros((rows, padded), dtype=torch.long)
+        for i, x in enumerate(prompts):
+            ids[i, : lens[i]] = torch.tensor(list(x), dtype=torch.long)
+        keep = torch.tensor(lens + [1] * (rows - b), dtype=torch.long) - 1
+        out = self.model(input_ids=ids.to(self.dev, non_blocking=True), use_cache=True,
+                         logits_to_keep=keep.to(self.dev, non_blocking=True))
+        # row i's logits at its own last prompt position: the diagonal of [rows, rows, vocab]
+        diag = torch.arange(b, device=self.dev)
+        first_t = out.logits[diag, diag].argmax(-1)
+        pkv = out.past_key_values
+        seqs: List[Sequence_] = []
+        for i in range(b):
+            p = lens[i]
+            blocks = self._allocate(need[i])
+            nblk = (p + self.block_size - 1) // self.block_size
+            k_srcs, v_srcs = [], []
+            for layer in range(self.num_layers):
+                lk = pkv.layers[layer].keys if hasattr(pkv, "layers") else pkv[layer][0]
+                lv = pkv.layers[layer].values if hasattr(pkv, "layers") else pkv[layer][1]
+                k_srcs.append(lk[i, :, :p, :].permute(1, 0, 2))
+                v_srcs.append(lv[i, :, :p, :].permute(1, 0, 2))
+            block_ids = torch.tensor(blocks[:nblk], dtype=torch.int64, device=self.dev)
+            kv_write_prefill(k_srcs, v_srcs, self.k_cache, self.v_cache, block_ids, p)
+            row = np.zeros(self.max_blocks_per_seq, dtype=np.int64)
+            row[: len(blocks)] = blocks
+            seqs.append(Sequence_(self._next_id, p, max_new_tokens, blocks, p, -1, [], row))
+            self._next_id += 1
+        for seq, tok in zip(seqs, first_t.tolist()):
+            seq.last_token = tok
+            seq.generated = [tok]
+        return seqs
+
     # ---- decode ----------------------------------------------------------------
     def _logits(self, ids: torch.Tensor, pos: torch.Tensor, tables: torch.Tensor, lens: torch.Tensor,
                 slots: torch.Tensor) -> torch.Tensor:
@@ -231,12 +281,16 @@ class PagedDecodeRunner:
             s.generated.append(int(t))
         return logits
 
-    def warm_prefill(self, max_prompt: int) -> None:
-        """Run one prefill per bucket length up to ``max_prompt`` (kernel
+    def warm_prefill(self, max_prompt: int, batches: Sequence[int] = ()) -> None:
+        """Run one prefill per bucket length up to ``max_prompt``, and one
+        :meth:`prefill_many` per length and batch size in ``batches`` (kernel
         selection for each shape happens here, not inside a timed trace)."""
         for L in range(self.prefill_bucket, max_prompt + self.prefill_bucket, self.prefill_bucket):
             seq = self.prefill([1] * min(L, max_prompt), 1)
             self.release(seq)
+            for nb in batches:
+                for s_ in self.prefill_many([[1] * min(L, max_prompt)] * nb, 1):
+                    self.release(s_)
 
 
 def random_qwen2(num_layers: int = 24, hidden: int = 896, intermediate: int = 4864, heads: int = 14,
