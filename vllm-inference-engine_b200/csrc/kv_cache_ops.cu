@@ -81,11 +81,12 @@ kv_append_scalar_kernel(uint16_t *__restrict__ k_cache, uint16_t *__restrict__ v
 }
 
 // Copy-on-write: for every (src, dst) pair and layer, K block src -> dst and
-// V block src -> dst of that layer's pool. One warp per (pair, layer) unit at a
-// time, K and V together; every lane keeps kCopyUnroll 16-byte loads in flight
-// before the matching stores (128 KB per SM at four CTAs), and the grid is a
-// few CTAs per SM striding over the units, so neither launch cost nor CTA
-// scheduling grows with the pair count.
+// V block src -> dst of that layer's pool. One warp per (pair, layer, K|V)
+// unit at a time; every lane keeps kCopyUnroll 16-byte loads in flight before
+// the matching stores (one round covers a 4 KiB block), and the grid is a few
+// CTAs per SM striding over the units, so neither launch cost nor CTA
+// scheduling grows with the pair count, and a decode step's few hundred pairs
+// still spread over every SM.
 constexpr int kCopyUnroll = 8;
 constexpr int kCopyThreads = 256;
 
@@ -99,39 +100,35 @@ copy_blocks_kernel(char *const *__restrict__ k_ptrs, char *const *__restrict__ v
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (kCopyThreads / 32);
-  const int64_t units = (int64_t)num_pairs * num_layers;
+  const int64_t per_pair = 2 * (int64_t)num_layers;  // (layer, K|V) units of a pair
+  const int64_t units = (int64_t)num_pairs * per_pair;
   const int64_t n16 = block_bytes >> 4;  // 16-byte chunks per block
-  const int64_t total = 2 * n16;         // the K block's chunks, then the V block's
   for (int64_t unit = (int64_t)blockIdx.x * (kCopyThreads / 32) + (threadIdx.x >> 5); unit < units;
        unit += warps) {
-    const int pair = (int)(unit / num_layers);
-    const int layer = (int)(unit - (int64_t)pair * num_layers);
+    const int pair = (int)(unit / per_pair);
+    const int rem = (int)(unit - (int64_t)pair * per_pair);
+    const int layer = rem >> 1;
+    const bool is_v = rem & 1;
     const int64_t src = __ldg(mapping + 2 * pair);
     const int64_t dst = __ldg(mapping + 2 * pair + 1);
     if (src < 0 || src >= num_blocks || dst < 0 || dst >= num_blocks) {
-      if (lane == 0 && layer == 0) set_error(err, PAGEDKV_EFLAG_COPY_RANGE);
+      if (lane == 0 && rem == 0) set_error(err, PAGEDKV_EFLAG_COPY_RANGE);
       continue;
     }
-    char *kb = k_ptrs[layer];
-    char *vb = v_ptrs[layer];
-    const char *ks = kb + src * block_bytes;
-    const char *vs = vb + src * block_bytes;
-    char *kd = kb + dst * block_bytes;
-    char *vd = vb + dst * block_bytes;
-    for (int64_t c0 = lane; c0 < total; c0 += 32 * kCopyUnroll) {
+    char *base = is_v ? v_ptrs[layer] : k_ptrs[layer];
+    const char *s = base + src * block_bytes;
+    char *d = base + dst * block_bytes;
+    for (int64_t c0 = lane; c0 < n16; c0 += 32 * kCopyUnroll) {
       uint4 r[kCopyUnroll];
 #pragma unroll
       for (int u = 0; u < kCopyUnroll; ++u) {
         const int64_t c = c0 + u * 32;
-        if (c < total) r[u] = c < n16 ? ldg_stream16(ks + c * 16) : ldg_stream16(vs + (c - n16) * 16);
+        if (c < n16) r[u] = ldg_stream16(s + c * 16);
       }
 #pragma unroll
       for (int u = 0; u < kCopyUnroll; ++u) {
         const int64_t c = c0 + u * 32;
-        if (c < total) {
-          if (c < n16) stg16(kd + c * 16, r[u]);
-          else stg16(vd + (c - n16) * 16, r[u]);
-        }
+        if (c < n16) stg16(d + c * 16, r[u]);
       }
     }
   }
@@ -174,7 +171,7 @@ cudaError_t launch_copy_blocks(void *const *k_ptrs, void *const *v_ptrs, int32_t
                                const int64_t *mapping, int32_t num_pairs, int64_t block_bytes,
                                int64_t num_blocks, int num_sms, unsigned int *err, cudaStream_t stream) {
   if (num_pairs == 0 || num_layers == 0) return cudaSuccess;
-  const int64_t units = (int64_t)num_pairs * num_layers;
+  const int64_t units = (int64_t)num_pairs * num_layers * 2;
   const int64_t need = (units + kCopyThreads / 32 - 1) / (kCopyThreads / 32);
   const int64_t cap = (int64_t)(num_sms > 0 ? num_sms : 148) * 4;
   cudaLaunchConfig_t cfg = {};
