@@ -3,28 +3,35 @@
 
 Default workload (one GPU's shard): 256 sequences x
 2048-token contexts, Qwen2.5-0.5B attention shape (14 query / 2 kv heads,
-head_dim 64), block_size 16, fp16 pool of 40960 blocks with shuffled block
-tables. One "step" = one decode layer-step of the hot path over that batch:
-the KV append of 256 new tokens through a slot mapping, then batched decode
-attention over all 256 contexts (which include the appended token).
+head_dim 64), block_size 16, fp16 pools of 40960 blocks with shuffled block
+tables. One "step" = one decode step of the hot path over that batch in
+every layer of the model (``--layers``, 24 for Qwen2.5-0.5B, each layer its
+own pool): per layer, the KV append of 256 new tokens through a slot mapping,
+then batched decode attention over all 256 contexts (which include the
+appended token). The line also carries ``model_decode``: decode tokens/s of
+the whole random-init model (BASELINE config 5's architecture) over a short
+saturated trace per GPU.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--workload cfg1|cfg2|cfg3|cfg4|cfg4-cow|cfg5|ops|d256] [--gqa G]
+                  [--layers L] [--model-requests R]
 
 Extra workloads (not the headline): ``cfg1`` = BASELINE config 1 (the
 reference's CPU case: 8 sequences of U[1,512] tokens, 512-block pool; the CPU
 reference is timed on all host threads and on one); ``cfg3`` = config 3 (head_dim
 128, 8 kv heads, GQA G, 128 sequences with log-uniform lengths 16..8192,
 q x30); ``cfg4`` = config 4 (512 sequences in 8 groups sharing a 1024-token
-prefix + 256 own tokens); ``cfg4-cow`` = its copy-on-write variant (each
-group's partially filled fork block is copied to a private block for every
-sequence before its append, every step); ``d256`` = the head_dim-256 mode
+prefix + 256 own tokens; roofline over the unique bytes); ``cfg4-cow`` = the
+same with each sequence's last block shared by its group when the step
+starts and copied to the sequence's private block (all layers) before its
+append; ``cfg5`` = config 5 alone (``--requests`` at ``--rate`` per GPU);
+``ops`` = the pool-write kernels alone; ``d256`` = the head_dim-256 mode
 (64 x 2048 tokens, 8 query / 4 kv heads; not a BASELINE config).
 
 N > 1 runs under torchrun, one process per GPU; sequences are sharded
-data-parallel (each rank owns its own pool, weak scaling) and nothing crosses
-GPUs on the data path: torch.distributed (NCCL) is used only for the barrier
-around the timed region and the max-over-ranks of the elapsed time.
+data-parallel (each rank owns its own pools, weak scaling) and nothing
+crosses GPUs on the data path: a gloo (host) process group carries only the
+barrier around each timed region and the max / sum of the per-rank timings.
 
 ``--impl reference`` times the reference algorithm's CPU path (the pinned
 oracle restatement of engine/kernels/paged_attention.py:30-83 plus the append
@@ -98,14 +105,24 @@ class Workload:
         """Read new K/V, write them into the pool, read the slots."""
         return self.num_seqs * self.row_bytes * 2 * 2 + self.num_seqs * 8
 
-    def copy_bytes(self) -> int:
+    def copy_bytes(self, layers: int = 1) -> int:
+        """Copy-on-write: read + write of each pair's K and V block in every
+        layer, plus the pair list."""
         if self.pairs is None:
             return 0
         block = self.block_size * self.row_bytes
-        return int(self.pairs.shape[0]) * (block * 2 * 2 + 16)
+        return int(self.pairs.shape[0]) * (layers * block * 2 * 2 + 16)
 
-    def step_bytes(self) -> int:
-        return self.attention_bytes() + self.append_bytes() + self.copy_bytes()
+    def step_bytes(self, layers: int = 1) -> int:
+        """A decode step over ``layers`` layers: the copy-on-write copy (one
+        launch for all layers), then per layer the append and the attention."""
+        return layers * (self.attention_bytes() + self.append_bytes()) + self.copy_bytes(layers)
+
+    def attention_unique_bytes(self) -> int:
+        """Attention bytes counting each distinct K/V block once (shared
+        prefixes read once from HBM) plus q, out, tables and lengths."""
+        qo = self.num_seqs * self.num_q_heads * self.head_dim * ELEM * 2
+        return self.unique_kv_bytes() + qo + self.tables.numel() * 4 + self.num_seqs * 4
 
     def flops(self) -> int:
         return int(self.lens.to(torch.int64).sum()) * 4 * self.head_dim * self.num_q_heads
@@ -238,11 +255,16 @@ def make_workload(name: str, rank: int, gqa: int = 7) -> Workload:
             hq, hkv, d, bs, nb, tables, lens, _slots_for(tables, lens, bs), q, k_new, v_new, None,
         )
     if name in ("cfg4", "cfg4-cow"):
+        # 8 groups x 64 sequences; a group's tables share one 1024-token prefix
+        # (64 identical block ids), then 256 tokens of the sequence's own (16
+        # private blocks); the step appends the 1280th token. cfg4-cow: the
+        # last of those blocks (15 of 16 rows filled) starts the step shared by
+        # the group's 64 sequences, and each sequence copies it to its private
+        # block (over all layers) before its append.
         groups, per_group, hq, hkv, d, bs = 8, 64, 14, 2, 64, 16
         n = groups * per_group
-        prefix_blocks = 1024 // bs
+        prefix_blocks, own = 1024 // bs, 256 // bs
         cow = name == "cfg4-cow"
-        own = 1 if cow else 256 // bs
         nb = groups * (prefix_blocks + (1 if cow else 0)) + n * own + 64
         perm = list(range(nb))
         random.Random(44 + rank).shuffle(perm)
@@ -261,15 +283,15 @@ def make_workload(name: str, rank: int, gqa: int = 7) -> Workload:
             at += own
             rows.append(prefixes[gi] + mine)
             if cow:
-                pairs.append((forks[gi], mine[0]))
+                pairs.append((forks[gi], mine[-1]))
         tables = _tables_from_lists(rows)
-        ctx = 1024 + (8 + 1 if cow else 256)
-        lens = torch.full((n,), ctx, dtype=torch.int32)
+        lens = torch.full((n,), 1024 + 256, dtype=torch.int32)
         g = torch.Generator().manual_seed(1200 + rank)
         q, k_new, v_new = _qkv(g, n, hq, hkv, d)
         desc = (
-            "cfg4-cow: copy-on-write of each group's shared fork block (8 tokens) to 512 private blocks, "
-            "then KV append + decode attention; 8 groups x 64 seqs sharing a 1024-token prefix, ctx 1033"
+            "cfg4-cow: 8 groups x 64 seqs sharing a 1024-token prefix (identical block ids) + 256 own tokens, "
+            "ctx 1280; each sequence's last block (15 rows) starts the step shared by its group (ref count 64) "
+            "and is copied to a private block over all layers (512 pairs) before the KV append + decode attention"
             if cow
             else "cfg4: KV append + decode attention; 8 groups x 64 seqs sharing a 1024-token prefix "
             "(identical block ids) + 256 own tokens, ctx 1280"
@@ -282,8 +304,19 @@ def make_workload(name: str, rank: int, gqa: int = 7) -> Workload:
 
 
 # ---- clocks -------------------------------------------------------------------
+_REASON_BITS = {
+    "hw_slowdown": 0x8,
+    "hw_thermal_slowdown": 0x40,
+    "sw_thermal_slowdown": 0x20,
+    "sw_power_cap": 0x4,
+}
+
+
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason sampling while the timed region runs."""
+    """SM clock, power and throttle-reason samples taken WHILE the timed
+    region runs: a thread of this process polls NVML every ``interval_s``
+    (the GPUs found by UUID, so the indices agree whatever
+    CUDA_VISIBLE_DEVICES maps); without NVML, ``nvidia-smi -lms`` instead."""
 
     QUERY = (
         "timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -291,24 +324,73 @@ class ClockSampler:
         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
     )
 
-    def __init__(self, gpu_indices: list[int], interval_ms: int = 50):
-        self.gpus = gpu_indices
-        self.interval = interval_ms
+    def __init__(self, devices: list[int], interval_s: float = 0.002):
+        self.devices = devices
+        self.interval = interval_s
+        self.samples: list[tuple[float, float, int]] = []  # (sm MHz, power W, reason bits)
+        self.smax: list[float] = []
+        self.thread = None
         self.proc = None
+        self.source = "none"
 
     def start(self):
+        import threading
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", str(self.interval)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
-            )
-        except (OSError, ValueError):
-            self.proc = None
-        time.sleep(0.3)
+            import pynvml
+
+            pynvml.nvmlInit()
+            handles = []
+            for d in self.devices:
+                uuid = str(torch.cuda.get_device_properties(d).uuid)
+                uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+                handles.append(pynvml.nvmlDeviceGetHandleByUUID(uuid))
+            self.smax = [float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)) for h in handles]
+            self._stop = threading.Event()
+
+            def loop():
+                while not self._stop.is_set():
+                    for h in handles:
+                        try:
+                            sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                            pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                            rs = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+                        except pynvml.NVMLError:
+                            continue
+                        self.samples.append((sm, pw, rs))
+                    self._stop.wait(self.interval)
+
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+            self.source = f"NVML in-process, every {self.interval * 1e3:g} ms"
+        except Exception:  # noqa: BLE001 - any NVML failure falls back to nvidia-smi
+            self.thread = None
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "50"],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+                )
+                self.source = "nvidia-smi -lms 50"
+            except (OSError, ValueError):
+                self.proc = None
+            time.sleep(0.3)
 
     def stop(self) -> dict:
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
+            sm = [x[0] for x in self.samples]
+            reasons = sorted({name for _, _, bits in self.samples for name, b in _REASON_BITS.items() if bits & b})
+            return {
+                "sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(self.smax) if self.smax else None,
+                "reasons": reasons,
+                "samples": len(self.samples),
+                "power_w_max": round(max(x[1] for x in self.samples), 1) if self.samples else None,
+                "source": self.source,
+            }
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no NVML and no nvidia-smi"], "samples": 0}
         time.sleep(0.2)
         self.proc.terminate()
         try:
@@ -322,12 +404,6 @@ class ClockSampler:
         for line in out.splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 10:
-                continue
-            try:
-                idx = int(parts[1])
-            except ValueError:
-                continue
-            if idx not in self.gpus:
                 continue
             n += 1
             try:
@@ -343,6 +419,7 @@ class ClockSampler:
             "sm_max_mhz": max(smax) if smax else None,
             "reasons": sorted(reasons),
             "samples": n,
+            "source": self.source,
         }
 
 
@@ -527,15 +604,18 @@ def run_reference_arm(args) -> None:
     torch.set_num_threads(os.cpu_count() or 1)
     wl = make_workload(args.workload, 0, args.gqa)
     sm = _cpu_sample(wl, 8)
+    # a step runs the sample once per layer, as our arm's step runs every layer
+    layers = args.layers if args.workload != "cfg5" else 1
     for _ in range(args.warmup):
         cpu_reference_step(sm)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        cpu_reference_step(sm)
+        for _ in range(layers):
+            cpu_reference_step(sm)
         times.append(time.perf_counter() - t0)
     per = sum(times) / len(times)
-    value = sm["bytes"] / per / 1e9
+    value = layers * sm["bytes"] / per / 1e9
     threads = torch.get_num_threads()
     line = {
         "impl": "reference",
@@ -551,10 +631,12 @@ def run_reference_arm(args) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": wl.description, "sample_seqs_per_step": sm["n"], "parallelism": "host cores of rank 0"},
+        "config": {"workload": wl.description, "layers_per_step": layers, "sample_seqs_per_step": sm["n"],
+                   "parallelism": "host cores of rank 0"},
         "cpu_baseline": {
             "value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"first {sm['n']} sequences of {wl.name} per step (fp32 oracle restatement, torch CPU)",
+            "sample": f"first {sm['n']} sequences of {wl.name}, {layers} layer passes per step (fp32 oracle "
+                      "restatement, torch CPU)",
         },
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -563,6 +645,9 @@ def run_reference_arm(args) -> None:
 
 # ---- our arm ------------------------------------------------------------------
 def _dist_setup(args):
+    """One process per GPU. The ranks share nothing on the data path; a gloo
+    (host) group carries only the barrier around each timed region and the
+    max / sum of the per-rank timings, so NCCL is not used at all."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -573,22 +658,22 @@ def _dist_setup(args):
     if world > 1:
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
+        dist.init_process_group("gloo", timeout=timedelta(seconds=180))
     return dist, rank, world, local
 
 
-def _max_over_ranks(dist, value: float, device) -> float:
+def _max_over_ranks(dist, value: float, device=None) -> float:
     if dist is None:
         return value
-    t = torch.tensor([value], dtype=torch.float64, device=device)
+    t = torch.tensor([value], dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
 
-def _sum_over_ranks(dist, value: float, device) -> float:
+def _sum_over_ranks(dist, value: float, device=None) -> float:
     if dist is None:
         return value
-    t = torch.tensor([value], dtype=torch.float64, device=device)
+    t = torch.tensor([value], dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.SUM)
     return float(t.item())
 
@@ -617,55 +702,74 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local)
     _native.lib()
     wl = make_workload(args.workload, rank, args.gqa)
-    pools = make_pools(rank, dev, wl.num_blocks, wl.block_size, wl.num_kv_heads, wl.head_dim)
-    kc, vc = pools["k_cache"], pools["v_cache"]
-    q = wl.q.to(dev)
+    L = args.layers
+    # One pool per layer, as the model's PhysicalBlockPool holds them: a step
+    # runs the paged path of every layer, and no layer's K/V is in L2 when
+    # the next layer's kernels read theirs.
+    kcs, vcs = [], []
+    for layer in range(L):
+        pl = make_pools(rank * 1000 + layer, dev, wl.num_blocks, wl.block_size, wl.num_kv_heads, wl.head_dim)
+        kcs.append(pl["k_cache"])
+        vcs.append(pl["v_cache"])
+    # per-layer step inputs: distinct buffers holding the same seeded values
+    qs = [wl.q.to(dev) for _ in range(L)]
+    kns = [wl.k_new.to(dev) for _ in range(L)]
+    vns = [wl.v_new.to(dev) for _ in range(L)]
     tables = wl.tables.to(dev)
     lens = wl.lens.to(dev)
     slots = wl.slots.to(dev)
-    k_new = wl.k_new.to(dev)
-    v_new = wl.v_new.to(dev)
     pairs = wl.pairs.to(dev) if wl.pairs is not None else None
     scale = 1.0 / math.sqrt(wl.head_dim)
     stream = torch.cuda.current_stream(dev)
+    outs: list = [None] * L
 
     def step():
         if pairs is not None:
-            pagedkv.copy_blocks([kc], [vc], pairs)
-        pagedkv.kv_append(k_new, v_new, kc, vc, slots)
-        return pagedkv.paged_attention_decode_batched(q, kc, vc, tables, lens, scale)
+            pagedkv.copy_blocks(kcs, vcs, pairs)  # copy-on-write: one launch for every layer
+        for layer in range(L):
+            pagedkv.kv_append(kns[layer], vns[layer], kcs[layer], vcs[layer], slots)
+            outs[layer] = pagedkv.paged_attention_decode_batched(qs[layer], kcs[layer], vcs[layer], tables, lens,
+                                                                 scale)
 
-    # correctness spot-check of this shard against the oracle (first and last sequence)
-    out = step()
+    def attention_only():
+        for layer in range(L):
+            pagedkv.paged_attention_decode_batched(qs[layer], kcs[layer], vcs[layer], tables, lens, scale)
+
+    # correctness spot-check of this shard against the oracle (first and last
+    # sequence of the first and last layer)
+    step()
     torch.cuda.synchronize(dev)
     sel = [0, wl.num_seqs - 1]
-    nbk = [(int(wl.lens[s]) + wl.block_size - 1) // wl.block_size for s in sel]
-    used = sorted({int(b) for s, n in zip(sel, nbk) for b in wl.tables[s, :n].tolist()})
+    nbk = [(int(wl.lens[s_]) + wl.block_size - 1) // wl.block_size for s_ in sel]
+    used = sorted({int(b) for s_, n in zip(sel, nbk) for b in wl.tables[s_, :n].tolist()})
     remap = {b: i for i, b in enumerate(used)}
     idx = torch.tensor(used, device=dev)
-    ref = paged_ref.paged_attention_ref(
-        q[sel].float().cpu(), kc[idx].float().cpu(), vc[idx].float().cpu(),
-        [[remap[int(b)] for b in wl.tables[s, :n].tolist()] for s, n in zip(sel, nbk)],
-        [int(wl.lens[s]) for s in sel], scale,
-    )
-    max_err = (out[sel].float().cpu() - ref).abs().max().item()
-    if not max_err < 2e-3 + 2e-3 * ref.abs().max().item():
-        raise SystemExit(f"bench spot-check failed: max |err| {max_err}")
+    max_err = 0.0
+    for layer in sorted({0, L - 1}):
+        ref = paged_ref.paged_attention_ref(
+            qs[layer][sel].float().cpu(), kcs[layer][idx].float().cpu(), vcs[layer][idx].float().cpu(),
+            [[remap[int(b)] for b in wl.tables[s_, :n].tolist()] for s_, n in zip(sel, nbk)],
+            [int(wl.lens[s_]) for s_ in sel], scale,
+        )
+        err = (outs[layer][sel].float().cpu() - ref).abs().max().item()
+        if not err < 2e-3 + 2e-3 * ref.abs().max().item():
+            raise SystemExit(f"bench spot-check failed on layer {layer}: max |err| {err}")
+        max_err = max(max_err, err)
     launches_attn, family = pagedkv.last_decode_launch_info()
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
 
-    # The decode step and the attention alone, each captured once as a CUDA
-    # graph and replayed: a serving engine replays the decode step the same
-    # way, so the device time is not bounded by Python.
+    # The decode step and its attention launches alone, each captured once as
+    # a CUDA graph and replayed: a serving engine replays the decode step the
+    # same way, so the device time is not bounded by Python.
     g_step = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_step):
         step()
     g_attn = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_attn):
-        pagedkv.paged_attention_decode_batched(q, kc, vc, tables, lens, scale)
+        attention_only()
     for _ in range(args.warmup):
         g_step.replay()
         g_attn.replay()
@@ -685,28 +789,29 @@ def run_ours(args) -> None:
             dist.barrier()
         return a.elapsed_time(b)
 
-    sampler = ClockSampler([local] if world == 1 else list(range(world))) if rank == 0 else None
+    sampler = ClockSampler(list(range(world)) if world > 1 else [local]) if rank == 0 else None
     if sampler:
         sampler.start()
     total_ms = timed(g_step.replay, args.steps)
     clocks = sampler.stop() if sampler else None
-    attn_ms = timed(g_attn.replay, args.steps) / args.steps
-    eager_ms = timed(step, max(10, args.steps // 10)) / max(10, args.steps // 10)
-    append_ms = _max_over_ranks(dist, max(0.0, total_ms / args.steps - attn_ms), dev)
-    total_ms = _max_over_ranks(dist, total_ms, dev)
-    attn_ms_max = _max_over_ranks(dist, attn_ms, dev)
-    eager_ms = _max_over_ranks(dist, eager_ms, dev)
+    attn_ms = timed(g_attn.replay, args.steps) / args.steps  # L launches per replay
+    eager_n = max(3, args.steps // 4)
+    eager_ms = timed(step, eager_n) / eager_n
+    total_ms = _max_over_ranks(dist, total_ms)
+    attn_ms_max = _max_over_ranks(dist, attn_ms)
+    eager_ms = _max_over_ranks(dist, eager_ms)
     ms_per_step = total_ms / args.steps
+    other_ms = max(0.0, ms_per_step - attn_ms_max)
 
     a_bytes = wl.attention_bytes()
-    step_bytes = wl.step_bytes()
+    step_bytes = wl.step_bytes(L)
     value = world * step_bytes / (ms_per_step * 1e-3) / 1e9
 
     # ---- end to end through the public API from pinned host buffers -------------
-    # The step's inputs (q, new K/V, slots, tables, lengths) are staged in one
-    # pinned host buffer and moved with ONE host->device copy; the output comes
-    # back with one device->host copy. Every step copies them again.
-    parts = [wl.q, wl.k_new, wl.v_new, wl.slots, wl.tables, wl.lens]
+    # Every step copies its inputs host->device (the block tables, lengths and
+    # slots once; each layer's q and new K/V rows) and reads every layer's
+    # attention output back device->host.
+    parts = [wl.slots, wl.tables, wl.lens] + [t for _ in range(L) for t in (wl.q, wl.k_new, wl.v_new)]
     sizes = [t.numel() * t.element_size() for t in parts]
     offs = [0]
     for sz in sizes:
@@ -714,40 +819,54 @@ def run_ours(args) -> None:
     h_in = torch.empty(offs[-1], dtype=torch.uint8).pin_memory()
     for t, o, sz in zip(parts, offs, sizes):
         h_in[o : o + sz].copy_(t.contiguous().view(-1).view(torch.uint8))
-    d_in = torch.empty(offs[-1], dtype=torch.uint8, device=dev)
-    views = [d_in[o : o + sz].view(t.dtype).view(t.shape) for t, o, sz in zip(parts, offs, sizes)]
-    h_out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    out_elems = wl.q.numel()
     h2d = sum(sizes)
-    d2h = h_out.numel() * h_out.element_size()
+    d2h = L * out_elems * ELEM
+
+    def make_views(buf):
+        return [buf[o : o + sz].view(t.dtype).view(t.shape) for t, o, sz in zip(parts, offs, sizes)]
+
+    def run_layers(views, out_buf):
+        ds, dt, dl = views[:3]
+        if pairs is not None:
+            pagedkv.copy_blocks(kcs, vcs, pairs)
+        for layer in range(L):
+            dq, dk, dv = views[3 + 3 * layer : 6 + 3 * layer]
+            pagedkv.kv_append(dk, dv, kcs[layer], vcs[layer], ds)
+            o = pagedkv.paged_attention_decode_batched(dq, kcs[layer], vcs[layer], dt, dl, scale)
+            out_buf[layer].copy_(o)
+
+    d_in = torch.empty(offs[-1], dtype=torch.uint8, device=dev)
+    views = make_views(d_in)
+    d_out = torch.empty((L,) + tuple(wl.q.shape), dtype=torch.float16, device=dev)
+    h_out = torch.empty((L,) + tuple(wl.q.shape), dtype=torch.float16).pin_memory()
 
     def e2e_step():
         d_in.copy_(h_in, non_blocking=True)
-        dq, dk, dv, ds, dt, dl = views
-        if pairs is not None:
-            pagedkv.copy_blocks([kc], [vc], pairs)
-        pagedkv.kv_append(dk, dv, kc, vc, ds)
-        o = pagedkv.paged_attention_decode_batched(dq, kc, vc, dt, dl, scale)
-        h_out.copy_(o, non_blocking=True)
+        run_layers(views, d_out)
+        h_out.copy_(d_out, non_blocking=True)
 
     for _ in range(max(3, args.warmup)):
         e2e_step()
     torch.cuda.synchronize(dev)
-    serial_ms = _max_over_ranks(dist, timed(e2e_step, args.steps), dev) / args.steps
+    serial_ms = _max_over_ranks(dist, timed(e2e_step, args.steps)) / args.steps
     serial_out = h_out.clone()
 
     # Pipelined: the same calls and copies, with step i+1's inputs copied on a
     # side stream into the other of two device buffers before step i's
-    # kernels are issued (so the copy has a whole step to land), and step i's
-    # output read back on a second side stream (the two copy engines run in
-    # parallel with the SMs). Every step still moves all of its inputs
-    # host->device and its output device->host inside the timed region.
+    # kernels are issued, and step i's outputs read back on a second side
+    # stream (the copy engines run beside the SMs). Every step still moves all
+    # of its inputs host->device and its outputs device->host inside the
+    # timed region.
     d_in2 = [d_in, torch.empty_like(d_in)]
-    views2 = [views, [d_in2[1][o : o + sz].view(t.dtype).view(t.shape) for t, o, sz in zip(parts, offs, sizes)]]
+    views2 = [views, make_views(d_in2[1])]
+    d_out2 = [d_out, torch.empty_like(d_out)]
     h_out2 = [h_out, torch.empty_like(h_out).pin_memory()]
     s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     free = [torch.cuda.Event(), torch.cuda.Event()]
     ready = [torch.cuda.Event(), torch.cuda.Event()]
     done = [torch.cuda.Event(), torch.cuda.Event()]
+    out_free = [torch.cuda.Event(), torch.cuda.Event()]
 
     def stage_inputs(i):
         free[i].wait(s_h2d)  # the step that last read this buffer is done
@@ -758,25 +877,22 @@ def run_ours(args) -> None:
 
     def e2e_pipelined_step(i, prefetch):
         # A serving loop consumes each result: the host waits for the read-back
-        # of step i-2 before issuing step i, so it runs at most two steps ahead
-        # (and the allocator recycles the output buffers instead of growing).
+        # of step i-2 before issuing step i, so it runs at most two steps ahead.
+        b = i % 2
         if i >= 2:
-            done[i % 2].synchronize()
+            done[b].synchronize()
         if prefetch:
             stage_inputs((i + 1) % 2)
-        ready[i % 2].wait(stream)
-        dq, dk, dv, ds, dt, dl = views2[i % 2]
-        if pairs is not None:
-            pagedkv.copy_blocks([kc], [vc], pairs)
-        pagedkv.kv_append(dk, dv, kc, vc, ds)
-        o = pagedkv.paged_attention_decode_batched(dq, kc, vc, dt, dl, scale)
-        free[i % 2].record(stream)
-        free[i % 2].wait(s_d2h)
+        ready[b].wait(stream)
+        out_free[b].wait(stream)
+        run_layers(views2[b], d_out2[b])
+        free[b].record(stream)
+        free[b].wait(s_d2h)
         torch.cuda.set_stream(s_d2h)
-        h_out2[i % 2].copy_(o, non_blocking=True)
+        h_out2[b].copy_(d_out2[b], non_blocking=True)
         torch.cuda.set_stream(stream)
-        o.record_stream(s_d2h)
-        done[i % 2].record(s_d2h)
+        done[b].record(s_d2h)
+        out_free[b].record(s_d2h)
 
     def e2e_pipelined(n):
         # the side streams start after the region's opening event and the
@@ -791,9 +907,18 @@ def run_ours(args) -> None:
 
     e2e_pipelined(max(3, args.warmup))
     torch.cuda.synchronize(dev)
-    e2e_ms = _max_over_ranks(dist, timed(lambda: e2e_pipelined(args.steps), 1), dev) / args.steps
+    e2e_ms = _max_over_ranks(dist, timed(lambda: e2e_pipelined(args.steps), 1)) / args.steps
     pipe_match = bool(torch.equal(h_out2[(args.steps - 1) % 2], serial_out))
     e2e_value = world * step_bytes / (e2e_ms * 1e-3) / 1e9
+
+    # release this workload's pools before the model-level run
+    del kcs, vcs, g_step, g_attn, d_in, d_in2, views, views2, d_out, d_out2, outs
+    torch.cuda.empty_cache()
+
+    model_block = None
+    if args.model_requests > 0 and args.workload == "cfg2":
+        model_block = model_decode_trace(args, dist, rank, world, dev, args.model_requests, args.model_rate,
+                                         args.model_kv_gb, with_cpu=False)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -805,15 +930,36 @@ def run_ours(args) -> None:
         peaks = json.loads(pp.read_text())
     peak = float(peaks.get("hbm_gbs", 6650.0))
     measured_peak = "hbm_gbs" in peaks
-    achieved = a_bytes / (attn_ms * 1e-3) / 1e9
+    per_launch_ms = attn_ms / L
+    shared_prefix = wl.name.startswith("cfg4")
+    roof_bytes = wl.attention_unique_bytes() if shared_prefix else a_bytes
+    achieved = roof_bytes / (per_launch_ms * 1e-3) / 1e9
     kernel_name = f"decode_{family}"
     traffic = _read_traffic(kernel_name, wl.name)
-    launches_per_step = 1 + launches_attn + (1 if pairs is not None else 0)
+    launches_per_step = L * (1 + launches_attn) + (1 if pairs is not None else 0)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
+    roofline = {
+        "bound": "hbm",
+        "kernel": kernel_name,
+        "achieved": round(achieved, 1),
+        "peak": peak,
+        "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if measured_peak else "fallback 6650 GB/s",
+        "unit": "GB/s",
+        "frac": round(achieved / peak, 4),
+        "traffic": traffic,
+        "algorithmic_bytes_per_launch": roof_bytes,
+        "launch_us": round(per_launch_ms * 1e3, 3),
+        "launches_timed": L * args.steps,
+        "flops_per_launch": wl.flops(),
+    }
+    if shared_prefix:
+        roofline["bytes_basis"] = "unique: each distinct K/V block once (a shared prefix is read once from HBM)"
+        roofline["logical_bytes_per_launch"] = a_bytes
+        roofline["achieved_logical"] = round(a_bytes / (per_launch_ms * 1e-3) / 1e9, 1)
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -829,6 +975,10 @@ def run_ours(args) -> None:
         "data": "synthetic",
         "config": {
             "workload": wl.description,
+            "layers_per_step": L,
+            "step": f"one decode step of the paged path over {L} layers (one pool per layer): "
+                    + ("the copy-on-write copy over all layers, then " if pairs is not None else "")
+                    + "per layer the KV append and the decode attention",
             "num_seqs_per_gpu": wl.num_seqs,
             "total_context_tokens_per_gpu": int(wl.lens.to(torch.int64).sum()),
             "heads": f"{wl.num_q_heads}q/{wl.num_kv_heads}kv",
@@ -836,29 +986,19 @@ def run_ours(args) -> None:
             "block_size": wl.block_size,
             "num_blocks": wl.num_blocks,
             "decode_kernel": family,
-            "l2": f"inputs exceed L2: {a_bytes / 1e6:.1f} MB read per step vs {L2_BYTES / 2**20:.0f} MiB L2, no flush"
-            if a_bytes > L2_BYTES else f"{a_bytes / 1e6:.1f} MB read per step, below the {L2_BYTES / 2**20:.0f} MiB L2",
+            "l2": f"inputs exceed L2: each layer reads {a_bytes / 1e6:.1f} MB of its own pool, a step "
+                  f"{L * a_bytes / 1e9:.2f} GB, vs {L2_BYTES / 2**20:.0f} MiB L2; no flush",
             "parallelism": f"dp{world}: sequences sharded, one pool per GPU, no collective on the data path",
             "bytes_per_step": step_bytes,
-            "unique_kv_bytes_per_step": wl.unique_kv_bytes(),
+            "unique_kv_bytes_per_layer": wl.unique_kv_bytes(),
         },
-        "decode_tokens_per_s": round(world * wl.num_seqs / (ms_per_step * 1e-3), 1),
-        "attention_ms": round(attn_ms_max, 5),
-        "append_ms": round(append_ms, 5),
-        "timing": "CUDA-graph replay of the step, CUDA events on the launch stream",
+        "paged_path_tokens_per_s": round(world * wl.num_seqs / (ms_per_step * 1e-3), 1),
+        "attention_us_per_layer": round(attn_ms_max / L * 1e3, 3),
+        "other_us_per_layer": round(other_ms / L * 1e3, 3),
+        "timing": f"CUDA-graph replay of the {L}-layer step, CUDA events on the launch stream; attention alone "
+                  f"from a graph of its {L} launches",
         "eager_ms_per_step": round(eager_ms, 5),
-        "roofline": {
-            "bound": "hbm",
-            "kernel": kernel_name,
-            "achieved": round(achieved, 1),
-            "peak": peak,
-            "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if measured_peak else "fallback 6650 GB/s",
-            "unit": "GB/s",
-            "frac": round(achieved / peak, 4),
-            "traffic": traffic,
-            "algorithmic_bytes_per_launch": a_bytes,
-            "flops_per_launch": wl.flops(),
-        },
+        "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": {
             "value": round(e2e_value, 2),
@@ -866,9 +1006,10 @@ def run_ours(args) -> None:
             "ms_per_step": round(e2e_ms, 5),
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
-            "api": "pagedkv public API; step inputs staged in one pinned buffer, one H2D and one D2H copy per step",
-            "overlap": "step i+1's H2D (issued before step i's kernels) and step i-1's D2H run on side streams "
-                       "(double-buffered) while step i computes; the host waits for step i-2's read-back before "
+            "api": "pagedkv public API; each step's inputs staged in one pinned buffer (one H2D copy) and the "
+                   "outputs of all layers read back with one D2H copy",
+            "overlap": "step i+1's H2D (issued before step i's kernels) and step i's D2H run on side streams "
+                       "(double-buffered) while the SMs compute; the host waits for step i-2's read-back before "
                        "issuing step i",
             "serial_ms_per_step": round(serial_ms, 5),
             "serial_value": round(world * step_bytes / (serial_ms * 1e-3) / 1e9, 2),
@@ -878,26 +1019,29 @@ def run_ours(args) -> None:
         "clocks": clocks,
         "spot_check_max_abs_err": max_err,
     }
+    if model_block is not None:
+        line["model_decode"] = model_block
     print(json.dumps(line), flush=True)
 
 
 # ---- config 5: full-model decode under continuous batching ------------------
-def run_model(args) -> None:
-    """Config 5: a random-init Qwen2.5-0.5B-architecture model (24 layers, 896
-    hidden, 14/2 heads, MLP 4864, vocab 151936, fp16) served by the continuous-
-    batching decode runner over a seeded Poisson trace (``--requests`` at
-    ``--rate`` req/s per GPU, prompts U[64, 1024] random ids, 128 output
-    tokens, greedy), its requests routed to the GPUs by least outstanding
-    tokens. Reports decode tokens/s (all GPUs) and latency figures."""
+def model_decode_trace(args, dist, rank: int, world: int, dev, requests: int, rate: float, kv_gb: float,
+                       with_cpu: bool) -> dict:
+    """Config 5 on this rank: a random-init Qwen2.5-0.5B-architecture model
+    (24 layers, 896 hidden, 14/2 heads, MLP 4864, vocab 151936, fp16) served by
+    the continuous-batching decode runner over a seeded Poisson trace
+    (``requests`` per GPU at ``rate`` req/s per GPU, prompts U[64, 1024]
+    random ids, 128 output tokens, greedy), the requests of the global trace
+    routed to the GPUs by least outstanding tokens. Returns the figures of the
+    whole job (decode tokens/s over all GPUs, max elapsed over ranks) and, per
+    decode step, the split between graph-replay device time and host time."""
     import numpy as np
     from pagedkv.decode_runner import PagedDecodeRunner, random_qwen2
 
-    dist, rank, world, local = _dist_setup(args)
-    dev = torch.device("cuda", local)
     model = random_qwen2(device=dev, seed=0)
     block_size = 16
     block_bytes = 2 * model.config.num_hidden_layers * block_size * model.config.num_key_value_heads * 64 * 2
-    num_blocks = min(int(args.kv_budget_gb * 1e9) // block_bytes, (2**31 - 1) // block_size)
+    num_blocks = min(int(kv_gb * 1e9) // block_bytes, (2**31 - 1) // block_size)
     runner = PagedDecodeRunner(model, num_blocks=num_blocks, block_size=block_size, max_batch=256,
                                max_seq_len=1024 + 128)
     # One global trace (world x requests at world x rate), routed by
@@ -906,8 +1050,8 @@ def run_model(args) -> None:
     from pagedkv.router import route_trace
 
     rng = np.random.default_rng(5000)
-    n_all = args.requests * world
-    arr_all = np.cumsum(rng.exponential(1.0 / (args.rate * world), n_all))
+    n_all = requests * world
+    arr_all = np.cumsum(rng.exponential(1.0 / (rate * world), n_all))
     lens_all = rng.integers(64, 1025, n_all)
     out_tokens = 128
     mine = [i for i, r_ in enumerate(route_trace([int(L) + out_tokens for L in lens_all], world)) if r_ == rank]
@@ -930,6 +1074,7 @@ def run_model(args) -> None:
     if dist:
         dist.barrier()
 
+    runner.timing = []  # (start event, end event) around every decode replay
     waiting = list(range(n_req))
     running = []
     ttft, finish, decode_time, decode_steps, prefill_time = [], [], 0.0, 0, 0.0
@@ -971,34 +1116,33 @@ def run_model(args) -> None:
         elif waiting:
             time.sleep(max(0.0, min(0.01, arrivals[waiting[0]] - (time.perf_counter() - t0))))
     elapsed = time.perf_counter() - t0
+    torch.cuda.synchronize(dev)
+    replay_ms = sum(a.elapsed_time(b) for a, b in runner.timing)
+    runner.timing = None
     gen = n_req * out_tokens
-    elapsed_max = _max_over_ranks(dist, elapsed, dev)
-    gen_all = _sum_over_ranks(dist, float(gen), dev)
+    elapsed_max = _max_over_ranks(dist, elapsed)
+    gen_all = _sum_over_ranks(dist, float(gen))
     dec_tok = n_req * (out_tokens - 1)  # the first token of each request comes from its prefill
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
     cpu = None
-    if world == 1 and not args.no_cpu_baseline:
+    if with_cpu and rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = time_cpu_model_step(args.cpu_seconds, source=model)
-    line = {
+    del runner, model
+    torch.cuda.empty_cache()
+    mean_step = 1e3 * decode_time / max(1, decode_steps)
+    mean_dev = replay_ms / max(1, decode_steps)
+    return {
         "metric": "decode tokens/s",
         "value": round(gen_all / elapsed_max, 1),
         "unit": "tok/s",
         "n_gpus": world,
         "higher_is_better": True,
         "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "f16",
-        "data": "synthetic",
         "config": {
             "workload": "cfg5: random-init Qwen2.5-0.5B architecture (24 layers, hidden 896, 14q/2kv, head_dim 64, "
                         "MLP 4864, vocab 151936, tied embeddings, fp16), continuous batching over a seeded Poisson "
-                        f"trace of {n_all} requests at {args.rate * world:g} req/s ({args.rate:g} per GPU), "
+                        f"trace of {n_all} requests at {rate * world:g} req/s ({rate:g} per GPU), "
                         f"prompts U[64,1024] random ids, {out_tokens} output tokens, greedy",
-            "kv_budget_gb": args.kv_budget_gb,
+            "kv_budget_gb": kv_gb,
             "num_blocks": num_blocks,
             "requests_this_rank": n_req,
             "parallelism": f"dp{world}: one runner and pool per GPU; requests routed by least outstanding tokens "
@@ -1008,13 +1152,33 @@ def run_model(args) -> None:
         "generated_tokens": int(gen_all),
         "decode_only_tokens_per_s": round(dec_tok / decode_time, 1) if decode_time > 0 else None,
         "decode_steps": decode_steps,
-        "mean_decode_step_ms": round(1e3 * decode_time / max(1, decode_steps), 3),
+        "mean_decode_step_ms": round(mean_step, 3),
+        "mean_decode_replay_device_ms": round(mean_dev, 3),
+        "mean_decode_host_ms": round(max(0.0, mean_step - mean_dev), 3),
         "prefill_s": round(prefill_time, 3),
         "ttft_ms_p50": round(1e3 * float(np.median(ttft)), 2),
         "request_latency_s_p50": round(float(np.median(finish)), 3),
-        "timing": "wall clock of the trace replay on rank 0 (max over ranks); decode steps are CUDA-graph replays",
+        "timing": "wall clock of the trace replay (max over ranks); decode steps are CUDA-graph replays whose "
+                  "device time comes from CUDA events around each replay",
         "cpu_baseline": cpu,
     }
+
+
+def run_model(args) -> None:
+    """``--workload cfg5``: config 5 on its own, one JSON line."""
+    dist, rank, world, local = _dist_setup(args)
+    dev = torch.device("cuda", local)
+    block = model_decode_trace(args, dist, rank, world, dev, args.requests, args.rate, args.kv_budget_gb,
+                               with_cpu=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {k: v for k, v in block.items()}
+    line["vs_baseline"] = None
+    line["dtype"] = "f16"
+    line["data"] = "synthetic"
     print(json.dumps(line), flush=True)
 
 
@@ -1140,6 +1304,14 @@ def main() -> None:
     ap.add_argument("--rate", type=float, default=32.0, help="cfg5: Poisson arrival rate per GPU (req/s)")
     ap.add_argument("--kv-budget-gb", type=float, default=60.0, help="cfg5: KV pool budget per GPU")
     ap.add_argument("--gqa", type=int, default=7, help="GQA group for --workload cfg3 (1, 2, 4 or 7)")
+    ap.add_argument("--layers", type=int, default=24,
+                    help="layers per decode step (one pool each; Qwen2.5-0.5B has 24)")
+    ap.add_argument("--model-requests", type=int, default=256,
+                    help="cfg2 line: requests per GPU of the saturated config-5 trace in its model_decode block "
+                         "(0 = skip)")
+    ap.add_argument("--model-rate", type=float, default=1000.0,
+                    help="cfg2 line: arrival rate per GPU (req/s) of that trace")
+    ap.add_argument("--model-kv-gb", type=float, default=60.0, help="cfg2 line: KV budget per GPU of that trace")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()

@@ -1,6 +1,5 @@
 """CPU: host-side logic of the drop-in integration (no kernel launches)."""
 import sys
-from pathlib import Path
 from types import SimpleNamespace
 
 import numpy as np
@@ -8,10 +7,10 @@ import pytest
 import torch
 
 import cases
+import refpath
 from oracle import paged_ref
 from pagedkv import integration, prefix_index
 
-REFERENCE = Path("/root/reference")
 
 
 def test_decode_metadata_matches_oracle_slots():
@@ -70,9 +69,9 @@ def test_prepare_copy_on_write_with_fake_allocator():
     assert alloc.ref_counts[shared] == 1 and alloc.ref_counts[pairs[0][1]] == 1
 
 
-@pytest.mark.skipif(not (REFERENCE / "engine").exists(), reason="reference checkout not present")
+@refpath.requires_reference
 def test_prepare_copy_on_write_with_reference_allocator():
-    sys.path.insert(0, str(REFERENCE))
+    refpath.ensure_on_path()
     from engine.memory.block_allocator import BlockAllocator, BlockTable
 
     alloc = BlockAllocator(num_blocks=32)
@@ -88,9 +87,9 @@ def test_prepare_copy_on_write_with_reference_allocator():
     alloc.check_invariants()
 
 
-@pytest.mark.skipif(not (REFERENCE / "engine").exists(), reason="reference checkout not present")
+@refpath.requires_reference
 def test_install_replaces_reference_symbols_and_uninstall_restores():
-    sys.path.insert(0, str(REFERENCE))
+    refpath.ensure_on_path()
     import engine.kernels.paged_attention as pa
     import engine.kernels.paged_attention_integration as integ
 
@@ -167,15 +166,14 @@ class _NullPatch:
         return False
 
 
-@pytest.mark.skipif(not (REFERENCE / "engine").exists(), reason="reference checkout not present")
+@refpath.requires_reference
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
 def test_decode_step_matches_the_reference_with_batched_syncs(monkeypatch, dtype):
     """integration.decode_step against the reference's own
     KernelPagedManualDecode.decode_step on the same sequences and logits: the
     same next tokens, length bumps, last_logits and logit margins (the model
     forward is a fake; the kernels are covered by the GPU tests)."""
-    if str(REFERENCE) not in sys.path:
-        sys.path.insert(0, str(REFERENCE))
+    refpath.ensure_on_path()
     import engine.kernels.paged_attention_integration as integ
 
     seqs_ref, runner_ref = _decode_step_fixture(dtype)
@@ -205,3 +203,72 @@ def test_decode_step_refuses_missing_and_shared_write_blocks():
     runner.allocator.ref_counts[4] = 3  # seq 0 writes into block 4, now shared
     with pytest.raises(AssertionError, match="shared"):
         integration.decode_step(runner, seqs[:1], None)
+
+
+class _FakeAttention(torch.nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.q_proj = self.k_proj = self.v_proj = self.o_proj = torch.nn.Identity()
+
+    def forward(self, hidden_states, position_embeddings=None, attention_mask=None, past_key_values=None, **kw):
+        return ("original", hidden_states)
+
+
+def test_patch_paged_attention_binds_once_and_only_swaps_the_context():
+    """The attention modules are bound to the paged forward on first use and
+    never rebound; entering / leaving a decode block only swaps the context,
+    and with no decode context a module runs its original forward."""
+    model = torch.nn.Sequential(_FakeAttention(), torch.nn.Sequential(_FakeAttention()))
+    attn = [m for m in model.modules() if isinstance(m, _FakeAttention)]
+    not_decode = SimpleNamespace(is_decode=False)
+    with integration.patch_paged_attention(model, not_decode):
+        bound = [m.__dict__["forward"] for m in attn]
+        assert model._pagedkv_context_holder.ctx is not_decode
+        assert attn[0](hidden_states=5, position_embeddings=None) == ("original", 5)
+    assert model._pagedkv_context_holder.ctx is None
+    for _ in range(3):
+        with integration.patch_paged_attention(model, not_decode):
+            assert all(m.__dict__["forward"] is b for m, b in zip(attn, bound))
+    assert attn[1](hidden_states=7, position_embeddings=None) == ("original", 7)  # outside a step: original forward
+    integration.detach_paged_attention(model)
+    assert all("forward" not in m.__dict__ and "_pagedkv_context_holder" not in m.__dict__ for m in attn)
+    assert "_pagedkv_context_holder" not in model.__dict__
+
+
+def test_install_options_are_set_on_the_runner_class_and_removed():
+    class Runner:
+        def decode_step(self):
+            pass
+
+        def _copy_prefill_kv(self):
+            pass
+
+    pa, integ = SimpleNamespace(), SimpleNamespace(KernelPagedManualDecode=Runner)
+    saved = integration.install(pa, integ, SimpleNamespace(), copy_on_write=True, cuda_graphs=False)
+    assert Runner._pagedkv_copy_on_write is True and Runner._pagedkv_cuda_graphs is False
+    assert Runner.decode_step is integration.decode_step
+    integration.uninstall(saved)
+    assert "_pagedkv_copy_on_write" not in Runner.__dict__ and "_pagedkv_cuda_graphs" not in Runner.__dict__
+    assert Runner.decode_step is not integration.decode_step
+
+
+def test_decode_step_copy_on_write_replaces_the_shared_block_assert(monkeypatch):
+    """With copy-on-write on, a shared write block is given to the sequence as
+    a fresh copy (one copy_blocks call for all layers) instead of raising."""
+    seqs, runner = _decode_step_fixture(torch.float16)
+    alloc = _FakeAllocator(64)
+    for b in range(16):
+        alloc.ref_counts[b] = 1
+    alloc.free_ids = [i for i in alloc.free_ids if i >= 16]
+    alloc.ref_counts[4] = 2  # seq 0 writes into block 4, shared
+    runner.allocator = alloc
+    runner._pagedkv_copy_on_write = True
+    calls = []
+    monkeypatch.setattr(integration, "copy_on_write", lambda pool, pairs: calls.append(list(pairs)))
+    monkeypatch.setattr(integration, "patch_paged_attention", _NullPatch)
+    monkeypatch.setattr(integration, "PagedAttentionContext", lambda **k: None)
+    seqs[0].block_table.num_tokens = 17
+    out = integration.decode_step(runner, seqs[:1], None)
+    assert len(out) == 1 and len(calls) == 1 and calls[0][0][0] == 4
+    new_block = seqs[0].block_table.physical_block_ids[1]
+    assert new_block != 4 and alloc.ref_counts[4] == 1 and alloc.ref_counts[new_block] == 1

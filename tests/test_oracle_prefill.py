@@ -3,7 +3,6 @@ KernelPagedManualDecode._copy_prefill_kv (paged_attention_integration.py:278-326
 run here on CPU with a fake model's cache (the reference's prefix-cache test uses
 the same construction). Pins the oracle the GPU prefill-write tests check against."""
 import sys
-from pathlib import Path
 from types import SimpleNamespace
 
 import pytest
@@ -11,9 +10,9 @@ import torch
 
 from oracle import paged_ref
 
-REFERENCE = Path("/root/reference")
-if (REFERENCE / "engine").exists() and str(REFERENCE) not in sys.path:
-    sys.path.insert(0, str(REFERENCE))
+import refpath
+
+refpath.ensure_on_path()
 
 
 def _runner_and_cache(num_layers, hkv, d, bs, nb, prompt_len, dtype, src_dtype, seed):
@@ -32,7 +31,7 @@ def _runner_and_cache(num_layers, hkv, d, bs, nb, prompt_len, dtype, src_dtype, 
     return runner, pkv
 
 
-@pytest.mark.skipif(not (REFERENCE / "engine").exists(), reason="reference checkout not present")
+@refpath.requires_reference
 @pytest.mark.parametrize(
     "num_layers,hkv,d,bs,nb,prompt_len,skip,dtype,src_dtype",
     [

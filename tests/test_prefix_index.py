@@ -9,14 +9,13 @@ import importlib.util
 import random
 import sys
 import time
-from pathlib import Path
 
 import pytest
 
-REFERENCE = Path("/root/reference")
-pytestmark = pytest.mark.skipif(not (REFERENCE / "engine").exists(), reason="reference checkout not present")
-if (REFERENCE / "engine").exists() and str(REFERENCE) not in sys.path:
-    sys.path.insert(0, str(REFERENCE))
+import refpath  # noqa: E402
+
+pytestmark = refpath.requires_reference
+refpath.ensure_on_path()
 
 from pagedkv import prefix_index  # noqa: E402
 
@@ -34,7 +33,7 @@ def patched():
 
 @pytest.mark.parametrize("seed", [7, 19, 2025, 65537])
 def test_reference_state_machine_on_patched_allocator(patched, seed):
-    spec = importlib.util.spec_from_file_location("ref_test_block_allocator", REFERENCE / "tests" / "test_block_allocator.py")
+    spec = importlib.util.spec_from_file_location("ref_test_block_allocator", refpath.reference_test_file("test_block_allocator.py"))
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     assert mod.BlockAllocator is patched and patched.lookup_prefix is prefix_index.lookup_prefix

@@ -13,6 +13,7 @@ import pytest
 import torch
 
 import pagedkv
+from oracle import paged_ref
 from pagedkv import _native
 
 pytestmark = pytest.mark.gpu
@@ -61,7 +62,7 @@ def _noalloc(out, q, k, v, tables, lens, scale):
         (5, 8, 4, 64, 4, "simt"),        # CUDA-core split-K path (block_size 4)
     ],
 )
-def test_noalloc_matches_workspace_entry_point_twice(shape):
+def test_noalloc_matches_oracle_and_workspace_entry_point_twice(shape):
     assert torch.cuda.is_available(), "GPU test selected but no CUDA device is visible"
     dev = torch.device("cuda", 0)
     n, hq, hkv, d, bs, kind = shape
@@ -74,12 +75,16 @@ def test_noalloc_matches_workspace_entry_point_twice(shape):
     q, k, v, tables, lens_t = _case(7, n, hq, hkv, d, bs, lens, dev)
     scale = 1.0 / math.sqrt(d)
     ref = pagedkv.paged_attention_decode_batched(q, k, v, tables, lens_t, scale)
+    # the fp32 CPU oracle (the reference's naive_reference_paged_attention restated)
+    rows = [tables[i, : (x + bs - 1) // bs].tolist() for i, x in enumerate(lens)]
+    expected = paged_ref.paged_attention_ref(q.float().cpu(), k.float().cpu(), v.float().cpu(), rows, lens, scale)
     for _ in range(2):  # the shared scratch keeps the previous call's contents
         out = torch.full_like(q, float("nan"))
         rc = _noalloc(out, q, k, v, tables, lens_t, scale)
         assert rc == _native.PAGEDKV_OK, _native.lib().pagedkv_last_error().decode()
         torch.cuda.synchronize()
         torch.testing.assert_close(out.float().cpu(), ref.float().cpu(), atol=ATOL, rtol=RTOL)
+        torch.testing.assert_close(out.float().cpu(), expected, atol=ATOL, rtol=RTOL)
     assert pagedkv.read_error_flags(dev) == 0
 
 

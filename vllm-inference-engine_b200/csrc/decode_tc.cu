@@ -34,11 +34,13 @@
 //     combine partials — off the softmax warps' path, so a piece boundary does
 //     not stall S -> P.
 //   * Work split (stream-K): the (sequence, head group) segments are laid end
-//     to end as one sequence of 128-token tiles; CTA b takes tiles
-//     [b*T/grid, (b+1)*T/grid). A segment cut by CTA boundaries is combined by
-//     the CTA holding its first tile, at the end of its range; the other
-//     pieces are the first pieces of the following CTAs, published early
-//     (partial + release flag) — no second launch, equal tiles per SM.
+//     to end as one sequence of 128-token tiles; range r takes tiles
+//     [r*T/grid, (r+1)*T/grid) and runs in block grid - 1 - r. A segment cut
+//     by range boundaries is combined by the CTA holding its first tile, at
+//     the end of its range; the other pieces are the first pieces of the
+//     following ranges, published early (partial + release flag) by
+//     lower-numbered blocks, so a combining CTA only ever waits on CTAs
+//     dispatched before it — no second launch, equal tiles per SM.
 //   * Warp roles (12 warps): 0 K-tile TMA producer (also copies each piece's
 //     Q), 6 V-tile TMA producer, 1 S-MMA issuer (TMEM owner), 11 O-MMA issuer,
 //     2-5 softmax, 7-10 correction / epilogue. Each tcgen05.mma costs its
@@ -127,13 +129,13 @@ __device__ __forceinline__ int tiles_of(int len) { return (len + kTile - 1) / kT
 // segment of nt tiles costs kSegUnits + nt * kTileUnits (the per-segment part
 // is its first piece's fixed work: Q copy, the full max reduction of its first
 // tile, the epilogue; measured, a one-tile segment costs about two streaming
-// tiles). CTA b takes the units [b*U/G, (b+1)*U/G) and owns every tile whose
+// tiles). Range b takes the units [b*U/G, (b+1)*U/G) and owns every tile whose
 // last unit falls in them, so SMs that draw many short sequences get fewer
 // tiles and each CTA still owns one contiguous run of tiles.
 constexpr int64_t kTileUnits = 8;
 constexpr int64_t kSegUnits = 8;
 
-// First unit of CTA b and the CTA owning unit u, for U units over G CTAs.
+// First unit of range b and the range owning unit u, for U units over G ranges.
 __device__ __forceinline__ int64_t range_lo(int64_t b, int64_t U, int64_t G) { return b * U / G; }
 __device__ __forceinline__ int64_t owner_of(int64_t u, int64_t U, int64_t G) {
   return ((u + 1) * G + U - 1) / U - 1;
@@ -213,17 +215,24 @@ struct PieceAcc {
 };
 
 // Stream-K combine, run by the 128 correction threads of the CTA holding a
-// cut segment's first tile: wait for the partials CTAs b+1..b1 published, fold
-// them into this CTA's piece, store the normalised output and clear the flags
-// (at most once per CTA per launch).
+// cut segment's first tile (range index vb): wait for the partials the CTAs of
+// ranges vb+1..b1 published, fold them into this CTA's piece, store the
+// normalised output and clear the flags (at most once per CTA per launch).
+// Ranges are assigned in reverse block order (range vb runs in block
+// G - 1 - vb), so the CTAs waited on have LOWER block indices than the
+// waiting one: under in-order block dispatch they were resident first, and
+// each publishes its piece before it waits on anything, so the wait ends
+// even when other work holds part of the GPU and not every CTA of the grid
+// is resident at once.
 template <typename T, int GP, int D, int D2>
-__device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP, D2> a, int64_t b1, int hl, int dim,
-                                            int gn, bool have_kv, T *out, volatile int *abort_flag, int row) {
+__device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP, D2> a, int64_t vb, int64_t b1, int hl,
+                                            int dim, int gn, bool have_kv, T *out, volatile int *abort_flag,
+                                            int row) {
   using E = Elem<T>;
   const DecodeParams &p = tp.p;
   const int HQS = (128 * D2 / D) * GP;  // partial slots per CTA
   if (row == 0) {
-    for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) {
+    for (int64_t bb = vb + 1; bb <= b1; ++bb) {
       const uint64_t t0 = globaltimer_ns();
       while (ld_acquire_u32(tp.flags + bb) == 0u) {
         if (globaltimer_ns() - t0 > kTimeoutNs) {
@@ -235,7 +244,7 @@ __device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP, 
   }
   named_bar(2, 128);
   if (have_kv) {
-    for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) {
+    for (int64_t bb = vb + 1; bb <= b1; ++bb) {
       const int64_t hh0 = bb * HQS + hl * GP;
       for (int g = 0; g < GP; ++g) {
         if (g < gn) {
@@ -263,7 +272,7 @@ __device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP, 
   }
   named_bar(2, 128);  // every partner partial read before its flag is cleared
   if (row == 0) {
-    for (int64_t bb = blockIdx.x + 1; bb <= b1; ++bb) st_volatile_u32(tp.flags + bb, 0u);
+    for (int64_t bb = vb + 1; bb <= b1; ++bb) st_volatile_u32(tp.flags + bb, 0u);
   }
 }
 
@@ -271,7 +280,7 @@ struct MiscSmem {
   uint32_t tmem;
   int abort;
   int len0, len1;  // clamped lengths of seq0 and seq0 + 1
-  int seq0, hg0, off0, pad;
+  int seq0, hg0, off0, vcta;  // vcta: this CTA's range index
   long long lo, hi, total, grid, u0;
 };
 
@@ -443,9 +452,13 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     // tile, and the owners of a segment are consecutive.
     const long long wide = Ut / (kSegUnits + kTileUnits);
     const long long Ge = wide < (long long)gridDim.x ? wide : (long long)gridDim.x;
-    const long long lo = (long long)blockIdx.x < Ge ? range_lo(blockIdx.x, Ut, Ge) : Ut;
-    const long long hi = (long long)blockIdx.x < Ge ? range_lo(blockIdx.x + 1, Ut, Ge) : Ut;
+    // Range vb runs in block Ge - 1 - vb: a range's stream-K partners (the
+    // ranges after it) run in lower-numbered blocks (see combine_pieces).
+    const long long vb = (long long)blockIdx.x < Ge ? Ge - 1 - (long long)blockIdx.x : (long long)blockIdx.x;
+    const long long lo = vb < Ge ? range_lo(vb, Ut, Ge) : Ut;
+    const long long hi = vb < Ge ? range_lo(vb + 1, Ut, Ge) : Ut;
     if (threadIdx.x == 0) {
+      misc->vcta = (int)vb;
       misc->lo = lo;
       misc->hi = hi;
       misc->total = Ut;
@@ -490,6 +503,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
   const uint32_t tmem = misc->tmem;
   const int64_t U_total = misc->total;
   const int64_t G = misc->grid;
+  const int64_t vcta = misc->vcta;
   Walker walk{misc->u0, misc->hi, misc->seq0, misc->hg0, misc->off0, false, misc->len0, misc->len1};
 
   if (warp == 0 || warp == 6) {
@@ -1033,7 +1047,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 #pragma unroll
           for (int g = 0; g < GP; ++g) {
             if (g < gn) {
-              const int64_t hh = (int64_t)blockIdx.x * HQS + hl * GP + g;
+              const int64_t hh = vcta * HQS + hl * GP + g;
 #pragma unroll
               for (int sub = 0; sub < D2; ++sub) tp.part_acc[hh * D + sub * 128 + dim] = acc[sub][g];
               if (dim == 0) tp.part_ml[hh] = make_float2(msel[g], lsum[g]);
@@ -1043,12 +1057,12 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         named_bar(2, 128);
         if (row == 0) {
           __threadfence();  // release every thread's partial (cumulative over the barrier)
-          st_volatile_u32(tp.flags + blockIdx.x, 1u);
+          st_volatile_u32(tp.flags + vcta, 1u);
         }
       } else {
         // First tile of the segment is here and the segment runs past this
         // CTA's range: this is this CTA's last piece, and this CTA combines.
-        // The other pieces are the first pieces of CTAs b+1..b1, published
+        // The other pieces are the first pieces of ranges b+1..b1, published
         // early in their runs.
         PieceAcc<GP, D2> pa;
 #pragma unroll
@@ -1058,7 +1072,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           pa.lsum[g] = lsum[g];
           pa.msel[g] = msel[g];
         }
-        combine_pieces<T, GP, D, D2>(tp, pa, owner_of(pc.seg_units + kSegUnits + (int64_t)pc.seg_tiles * kTileUnits - 1, U_total, G), hl, dim, gn,
+        combine_pieces<T, GP, D, D2>(tp, pa, vcta, owner_of(pc.seg_units + kSegUnits + (int64_t)pc.seg_tiles * kTileUnits - 1, U_total, G), hl, dim, gn,
                                  have_kv, out, abort_flag, row);
       }
 #ifdef PAGEDKV_TRACE

@@ -82,6 +82,8 @@ class PagedDecodeRunner:
         self._graphs: Dict[int, tuple] = {}
         self._host: Dict[int, tuple] = {}
         self._next_id = 0
+        # When a list: (start, end) CUDA events around every decode-graph replay.
+        self.timing: Optional[list] = None
 
     # ---- allocator -------------------------------------------------------------
     def can_admit(self, prompt_len: int, max_new_tokens: int) -> bool:
@@ -268,7 +270,14 @@ class PagedDecodeRunner:
             g, m64, m32, out = self._graph_for(bsz)
             m64.copy_(h64, non_blocking=True)
             m32.copy_(h32, non_blocking=True)
-            g.replay()
+            if self.timing is not None:
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record()
+                g.replay()
+                ev[1].record()
+                self.timing.append(ev)
+            else:
+                g.replay()
         else:
             m64, m32 = self._static(bsz)
             m64.copy_(h64, non_blocking=True)

@@ -27,8 +27,9 @@ iteration (:150-160). This module provides:
 from __future__ import annotations
 
 import math
+import weakref
 from contextlib import contextmanager
-from typing import Any, Callable, Iterable, List, Optional, Sequence, Tuple, Union
+from typing import Any, Dict, Iterable, List, Optional, Sequence, Tuple, Union
 
 import torch
 
@@ -146,6 +147,9 @@ def paged_decode_attention_forward(
     integration.py:65-176): projections, RoPE fused with the KV append through
     the slot mapping (one launch per layer), batched paged attention, o_proj."""
     ctx = getattr(self, "_paged_attention_context", None)
+    if ctx is None:
+        holder = getattr(self, "_pagedkv_context_holder", None)
+        ctx = holder.ctx if holder is not None else None
     if ctx is None or not ctx.is_decode:
         orig_forward = getattr(self, "_orig_attention_forward", None)
         if orig_forward is not None:
@@ -192,26 +196,80 @@ def paged_decode_attention_forward(
     return attn_output, None
 
 
+class _ContextHolder:
+    """The decode context every patched attention module of one model reads;
+    ``None`` outside a decode step (the modules then run their own forward)."""
+
+    __slots__ = ("ctx",)
+
+    def __init__(self) -> None:
+        self.ctx: Optional[PagedAttentionContext] = None
+
+
+# Models whose attention modules are routed through the paged forward.
+_attached: "weakref.WeakSet[torch.nn.Module]" = weakref.WeakSet()
+
+
+def _is_attention(module: torch.nn.Module) -> bool:
+    return all(hasattr(module, a) for a in ("q_proj", "k_proj", "v_proj", "o_proj"))
+
+
+def attach_paged_attention(model: torch.nn.Module) -> _ContextHolder:
+    """Route every decoder attention module of ``model`` through
+    :func:`paged_decode_attention_forward`, once per model, and return the
+    holder whose ``ctx`` selects the paged path.
+
+    The reference rebinds ``forward`` on every attention module at every
+    decode step and restores it afterwards (integration.py:179-208, used at
+    :629-634). Here the binding is made on first use and kept: a step only
+    stores its context in the holder (one assignment), and with no context
+    the modules fall back to their original forward (prefill, generation
+    outside the runner), as the reference's patched forward does."""
+    holder = getattr(model, "_pagedkv_context_holder", None)
+    if holder is not None:
+        return holder
+    holder = _ContextHolder()
+    for module in model.modules():
+        if _is_attention(module) and not hasattr(module, "_pagedkv_context_holder"):
+            module._orig_attention_forward = module.forward
+            module._pagedkv_own_forward = "forward" in module.__dict__
+            module._pagedkv_context_holder = holder
+            module.forward = paged_decode_attention_forward.__get__(module, module.__class__)
+    model._pagedkv_context_holder = holder
+    _attached.add(model)
+    return holder
+
+
+def detach_paged_attention(model: torch.nn.Module) -> None:
+    """Undo :func:`attach_paged_attention` (restore every module's forward)."""
+    for module in model.modules():
+        if module is not model and getattr(module, "_pagedkv_context_holder", None) is not None:
+            if module.__dict__.get("_pagedkv_own_forward"):
+                module.forward = module._orig_attention_forward
+            else:
+                del module.__dict__["forward"]
+            for attr in ("_orig_attention_forward", "_pagedkv_context_holder", "_pagedkv_own_forward"):
+                if attr in module.__dict__:
+                    delattr(module, attr)
+    if "_pagedkv_context_holder" in model.__dict__:
+        delattr(model, "_pagedkv_context_holder")
+    _attached.discard(model)
+
+
 @contextmanager
 def patch_paged_attention(model: torch.nn.Module, context: PagedAttentionContext):
-    """Temporarily route every decoder attention module of ``model`` through
-    :func:`paged_decode_attention_forward` (reference integration.py:179-208)."""
-    patched: List[Tuple[torch.nn.Module, Callable]] = []
-    for module in model.modules():
-        if all(hasattr(module, a) for a in ("q_proj", "k_proj", "v_proj", "o_proj")):
-            orig = module.forward
-            module._orig_attention_forward = orig
-            module._paged_attention_context = context
-            module.forward = paged_decode_attention_forward.__get__(module, module.__class__)
-            patched.append((module, orig))
+    """Route the decoder attention modules of ``model`` through
+    :func:`paged_decode_attention_forward` with ``context`` for the duration
+    of the block (reference integration.py:179-208). The modules are bound
+    once (:func:`attach_paged_attention`); entering and leaving the block only
+    swaps the context."""
+    holder = attach_paged_attention(model)
+    prev = holder.ctx
+    holder.ctx = context
     try:
         yield context
     finally:
-        for module, orig in patched:
-            module.forward = orig
-            for attr in ("_orig_attention_forward", "_paged_attention_context"):
-                if hasattr(module, attr):
-                    delattr(module, attr)
+        holder.ctx = prev
 
 
 def _seq_field(seq: Any, name: str, default: Any = None) -> Any:
@@ -222,11 +280,112 @@ def _seq_field(seq: Any, name: str, default: Any = None) -> Any:
     return default
 
 
+def _bucket(n: int, cap: Optional[int] = None) -> int:
+    b = 1
+    while b < n:
+        b *= 2
+    return b if cap is None else min(b, cap)
+
+
+def _graphable(model: Any) -> bool:
+    """The decode forward can be replayed layer by layer from a CUDA graph:
+    a Qwen2-architecture causal LM (embed / rotary / layers / norm / lm_head,
+    attention with q/k/v/o projections) on a CUDA device."""
+    cfg = getattr(model, "config", None)
+    inner = getattr(model, "model", None)
+    if cfg is None or inner is None or getattr(cfg, "model_type", None) != "qwen2":
+        return False
+    if not all(hasattr(inner, a) for a in ("embed_tokens", "rotary_emb", "layers", "norm")):
+        return False
+    if not hasattr(model, "lm_head"):
+        return False
+    try:
+        dev = next(model.parameters()).device
+    except StopIteration:
+        return False
+    return dev.type == "cuda"
+
+
+class DecodeGraphs:
+    """CUDA graphs of one runner's decode forward, one per (padded batch,
+    padded table width).
+
+    The forward is the one the reference runs through the patched model
+    (integration.py:621-640): embedding, rotary table, and per layer input
+    norm, q/k/v projections, RoPE fused with the KV append through the slot
+    mapping, batched paged attention, o_proj and residual, post-attention norm,
+    MLP and residual; then the final norm, ``lm_head``, the greedy token and
+    the top-2 logit margin. The same module calls in the same order as the HF
+    decoder layer, so the logits are those of the patched forward. Inputs live
+    in two static device buffers per graph (int64 [B, 3]: token, position,
+    slot; int32 [B, 1 + W]: length, block table) filled by one host-to-device
+    copy each per step; padding rows have length 0 and slot -1 (no write,
+    zero attention output)."""
+
+    def __init__(self, model: Any, pool: Any) -> None:
+        self.model = model
+        self.pool = pool
+        self.dev = next(model.parameters()).device
+        self.graphs: Dict[Tuple[int, int], tuple] = {}
+        self.mempool = torch.cuda.graph_pool_handle()
+
+    def _forward(self, m64: torch.Tensor, m32: torch.Tensor):
+        m = self.model.model
+        ids, pos, slots = m64[:, 0], m64[:, 1], m64[:, 2]
+        lens, tables = m32[:, 0], m32[:, 1:]
+        b = ids.shape[0]
+        x = m.embed_tokens(ids[:, None])
+        cos, sin = m.rotary_emb(x, pos[:, None])
+        cos2, sin2 = cos[:, 0], sin[:, 0]
+        k_caches, v_caches = self.pool.k_cache, self.pool.v_cache
+        for li, layer in enumerate(m.layers):
+            attn = layer.self_attn
+            residual = x
+            h = layer.input_layernorm(x)
+            q = attn.q_proj(h).view(b, -1, attn.head_dim)
+            k = attn.k_proj(h).view(b, -1, attn.head_dim)
+            v = attn.v_proj(h).view(b, -1, attn.head_dim)
+            scale = attn.scaling if hasattr(attn, "scaling") else 1.0 / math.sqrt(attn.head_dim)
+            li_pool = attn.layer_idx if hasattr(attn, "layer_idx") else li
+            q_rot = kv_append_rope(q, k, v, cos2, sin2, k_caches[li_pool], v_caches[li_pool], slots)
+            o = paged_attention_decode_batched(q_rot, k_caches[li_pool], v_caches[li_pool], tables, lens, scale)
+            x = residual + attn.o_proj(o.reshape(b, 1, -1).contiguous())
+            residual = x
+            x = residual + layer.mlp(layer.post_attention_layernorm(x))
+        x = m.norm(x)
+        logits = self.model.lm_head(x[:, -1, :])
+        top2 = torch.topk(logits, k=2, dim=-1).values
+        return logits, torch.argmax(logits, dim=-1), top2[:, 0] - top2[:, 1]
+
+    def get(self, bsz: int, width: int) -> tuple:
+        key = (bsz, width)
+        hit = self.graphs.get(key)
+        if hit is None:
+            m64 = torch.zeros(bsz, 3, dtype=torch.int64, device=self.dev)
+            m64[:, 2] = -1
+            m32 = torch.zeros(bsz, 1 + width, dtype=torch.int32, device=self.dev)
+            h64 = torch.zeros(bsz, 3, dtype=torch.int64).pin_memory()
+            h32 = torch.zeros(bsz, 1 + width, dtype=torch.int32).pin_memory()
+            # Every row is padding here (length 0, slot -1): the warm-up and the
+            # capture write nothing into the pool. The warm-up runs size the
+            # kernels' cached workspace before capture.
+            for _ in range(2):
+                self._forward(m64, m32)
+            torch.cuda.synchronize(self.dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=self.mempool):
+                outs = self._forward(m64, m32)
+            hit = (g, m64, m32, h64, h32, outs)
+            self.graphs[key] = hit
+        return hit
+
+
 @torch.inference_mode()
 def decode_step(self: Any, seqs: List[Any], allocator: Any = None) -> List[int]:
     """``KernelPagedManualDecode.decode_step`` (integration.py:519-651) with the
-    same bookkeeping, asserts and results, and its host synchronisation
-    batched.
+    same bookkeeping, asserts and results, its host synchronisation batched
+    and, for a Qwen2 model on a CUDA device, its forward replayed from a CUDA
+    graph per padded batch size and table width.
 
     Per sequence, as the reference: the write slot is block
     ``num_tokens // block_size`` of its table, which must exist and must not be
@@ -238,18 +397,28 @@ def decode_step(self: Any, seqs: List[Any], allocator: Any = None) -> List[int]:
     from one top-2 over the batch and two device-to-host copies in all, instead
     of a ``.cpu()``, a ``topk`` and an ``.item()`` sync per sequence; each
     ``last_logits`` is a row of one host tensor of the batch's logits.
+
+    With copy-on-write enabled (``install(copy_on_write=True)``, or the
+    runner attribute ``_pagedkv_copy_on_write``), a write block shared with
+    another sequence is first copied to a fresh block for this sequence
+    (:func:`prepare_copy_on_write` + one :func:`pagedkv.copy_blocks` launch for
+    all layers) instead of failing the reference's shared-block assert.
     """
     n = len(seqs)
     if n == 0:
         return []
     allocator = allocator or self.allocator
-    seq_lens: List[int] = []
-    tables: List[Any] = []
-    last_tokens: List[int] = []
+    tables_bt: List[Any] = []
     for seq in seqs:
         bt = _seq_field(seq, "block_table")
         if bt is None:
             raise ValueError("Sequence must provide a block_table attribute or dict key.")
+        tables_bt.append(bt)
+    if getattr(self, "_pagedkv_copy_on_write", False):
+        copy_on_write(self.pool, prepare_copy_on_write(tables_bt, allocator, self.block_size))
+    seq_lens: List[int] = []
+    last_tokens: List[int] = []
+    for seq, bt in zip(seqs, tables_bt):
         write_idx = bt.num_tokens // self.block_size
         if write_idx >= len(bt.physical_block_ids):
             raise AssertionError(
@@ -264,7 +433,6 @@ def decode_step(self: Any, seqs: List[Any], allocator: Any = None) -> List[int]:
             )
         bt.num_tokens += 1
         seq_lens.append(bt.num_tokens)
-        tables.append(bt)
         tok = _seq_field(seq, "last_token_id")
         if tok is None:
             gen = _seq_field(seq, "generated_ids")
@@ -273,23 +441,50 @@ def decode_step(self: Any, seqs: List[Any], allocator: Any = None) -> List[int]:
             tok = gen[-1]
         last_tokens.append(int(tok))
 
-    # token ids and positions in one host->device copy
-    host = torch.tensor([last_tokens, [s - 1 for s in seq_lens]], dtype=torch.long)
-    if torch.device(self.device).type == "cuda":
-        host = host.pin_memory()
-    dev_ids = host.to(self.device, non_blocking=True)
-    input_ids, position_ids = dev_ids[0].unsqueeze(1), dev_ids[1].unsqueeze(1)
-    ctx = PagedAttentionContext(pool=self.pool, block_tables=tables, seq_lens=seq_lens,
-                                block_size=self.block_size, is_decode=True)
-    with patch_paged_attention(self.model, ctx):
-        step_out = self.model(input_ids=input_ids, position_ids=position_ids, use_cache=False)
-    logits = step_out.logits[:, -1, :]
-    next_t = torch.argmax(logits, dim=-1)
+    use_graphs = getattr(self, "_pagedkv_cuda_graphs", False) and _graphable(self.model)
+    if use_graphs:
+        graphs = self.__dict__.get("_pagedkv_graphs")
+        if graphs is None or graphs.model is not self.model or graphs.pool is not self.pool:
+            graphs = DecodeGraphs(self.model, self.pool)
+            self._pagedkv_graphs = graphs
+        width = max(len(bt.physical_block_ids) for bt in tables_bt)
+        g, m64, m32, h64, h32, (logits_s, next_s, margin_s) = graphs.get(_bucket(n), _bucket(max(1, width)))
+        bs = self.block_size
+        h64.zero_()
+        h32.zero_()
+        h64[:, 2] = -1
+        a64, a32 = h64.numpy(), h32.numpy()
+        for i, (bt, L, tok) in enumerate(zip(tables_bt, seq_lens, last_tokens)):
+            ids = bt.physical_block_ids
+            a64[i, 0] = tok
+            a64[i, 1] = L - 1
+            a64[i, 2] = ids[(L - 1) // bs] * bs + (L - 1) % bs
+            a32[i, 0] = L
+            a32[i, 1 : 1 + len(ids)] = ids
+        m64.copy_(h64, non_blocking=True)
+        m32.copy_(h32, non_blocking=True)
+        g.replay()
+        logits, next_t, margin = logits_s[:n], next_s[:n], margin_s[:n]
+    else:
+        # token ids and positions in one host->device copy
+        host = torch.tensor([last_tokens, [s - 1 for s in seq_lens]], dtype=torch.long)
+        if torch.device(self.device).type == "cuda":
+            host = host.pin_memory()
+        dev_ids = host.to(self.device, non_blocking=True)
+        input_ids, position_ids = dev_ids[0].unsqueeze(1), dev_ids[1].unsqueeze(1)
+        ctx = PagedAttentionContext(pool=self.pool, block_tables=tables_bt, seq_lens=seq_lens,
+                                    block_size=self.block_size, is_decode=True)
+        with patch_paged_attention(self.model, ctx):
+            step_out = self.model(input_ids=input_ids, position_ids=position_ids, use_cache=False)
+        logits = step_out.logits[:, -1, :]
+        next_t = torch.argmax(logits, dim=-1)
+        margin = None
     want = [i for i, s in enumerate(seqs) if hasattr(s, "last_logits") or isinstance(s, dict)]
     if not want:
         return next_t.tolist()
-    top2 = torch.topk(logits, k=2, dim=-1).values
-    margin = top2[:, 0] - top2[:, 1]  # in the logits' dtype, as the reference's per-row difference
+    if margin is None:
+        top2 = torch.topk(logits, k=2, dim=-1).values
+        margin = top2[:, 0] - top2[:, 1]  # in the logits' dtype, as the reference's per-row difference
     # float64 holds every token id and every 16/32-bit margin exactly
     packed = torch.cat([next_t.to(torch.float64), margin.to(torch.float64)]).tolist()
     host_logits = logits.detach().cpu()
@@ -396,8 +591,12 @@ _INSTALL_NAMES_KERNELS = (
 )
 
 
+_MISSING = object()
+
+
 def install(paged_attention_module: Any = None, integration_module: Any = None,
-            allocator_module: Any = None) -> dict:
+            allocator_module: Any = None, *, copy_on_write: bool = False,
+            cuda_graphs: bool = True) -> dict:
     """Install the B200 path into the reference's modules.
 
     ``paged_attention_module`` defaults to ``engine.kernels.paged_attention``,
@@ -406,6 +605,16 @@ def install(paged_attention_module: Any = None, integration_module: Any = None,
     given; the allocator is skipped when it cannot be imported). Returns the
     replaced symbols for :func:`uninstall`. The reference's
     ``naive_reference_paged_attention`` is left untouched.
+
+    ``copy_on_write``: the installed ``decode_step`` copies a shared write
+    block to a fresh block (for all layers, one launch) instead of raising the
+    reference's shared-block ``AssertionError`` (integration.py:587-592); off
+    by default, which keeps the reference's behaviour. ``cuda_graphs``: the
+    installed ``decode_step`` replays its forward from a CUDA graph per padded
+    batch size and table width when the runner's model is a Qwen2 causal LM on
+    a CUDA device (:class:`DecodeGraphs`); otherwise, or when off, it runs the
+    model eagerly with the attention modules bound once
+    (:func:`attach_paged_attention`).
     """
     if paged_attention_module is None:
         import importlib
@@ -437,6 +646,11 @@ def install(paged_attention_module: Any = None, integration_module: Any = None,
         if runner_cls is not None and hasattr(runner_cls, name):
             saved[(runner_cls, name)] = runner_cls.__dict__.get(name, getattr(runner_cls, name))
             setattr(runner_cls, name, fn)
+    if runner_cls is not None:
+        for name, value in (("_pagedkv_copy_on_write", bool(copy_on_write)),
+                            ("_pagedkv_cuda_graphs", bool(cuda_graphs))):
+            saved[(runner_cls, name)] = runner_cls.__dict__.get(name, _MISSING)
+            setattr(runner_cls, name, value)
     # The allocator's prefix lookup: a per-parent index instead of a full scan
     # of the cache per block (block_allocator.py:231-252).
     if allocator_module is None:
@@ -457,5 +671,10 @@ def uninstall(saved: dict) -> None:
     for (mod, name), fn in saved.items():
         if mod == "prefix_index":
             prefix_index.uninstall(fn)
+        elif fn is _MISSING:
+            if name in getattr(mod, "__dict__", {}):
+                delattr(mod, name)
         else:
             setattr(mod, name, fn)
+    for model in list(_attached):
+        detach_paged_attention(model)

@@ -22,6 +22,15 @@ no CPU path and no fallback: a CPU tensor or a missing library raises.
 
 Beyond the reference: bf16 pools are accepted as well as fp16, and q/out may
 be strided views (last dimension contiguous).
+
+Streams: every decode-attention call on a device uses ONE cached workspace
+of that device (the tensor-core kernel's cross-CTA completion flags and
+split-K partial sums; a CUDA graph captured through this module bakes the
+same buffer in). Decode-attention calls (or graph replays) that could run at
+the same time on one device — issued on two streams without an event between
+them — race on it and must not be made; calls from one stream, or ordered by
+events, are safe. Callers that need concurrent decodes on one device pass
+their own workspaces through the C ABI (``pagedkv_decode_attention``).
 """
 from __future__ import annotations
 
@@ -37,7 +46,8 @@ _DEBUG = os.environ.get("PAGEDKV_DEBUG", "0") not in ("", "0")
 
 _DTYPES = {torch.float16: _native.DTYPE_F16, torch.bfloat16: _native.DTYPE_BF16}
 
-# Split-K scratch, one cached buffer per device, grown on demand.
+# Split-K scratch, one cached buffer per device, grown on demand; shared by
+# every stream of the device (see the module docstring).
 _workspaces: dict[int, torch.Tensor] = {}
 # Workspace bytes per launch shape (the query is a host-side computation).
 _ws_sizes: dict[tuple, int] = {}
