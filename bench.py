@@ -1119,6 +1119,9 @@ def model_decode_trace(args, dist, rank: int, world: int, dev, requests: int, ra
     torch.cuda.synchronize(dev)
     replay_ms = sum(a.elapsed_time(b) for a, b in runner.timing)
     runner.timing = None
+    profile = None
+    if getattr(args, "profile_decode", 0) > 0 and rank == 0:
+        profile = profile_decode_steps(runner, prompts, out_tokens, args.profile_decode, dev)
     gen = n_req * out_tokens
     elapsed_max = _max_over_ranks(dist, elapsed)
     gen_all = _sum_over_ranks(dist, float(gen))
@@ -1161,6 +1164,60 @@ def model_decode_trace(args, dist, rank: int, world: int, dev, requests: int, ra
         "timing": "wall clock of the trace replay (max over ranks); decode steps are CUDA-graph replays whose "
                   "device time comes from CUDA events around each replay",
         "cpu_baseline": cpu,
+        **({"decode_step_profile": profile} if profile is not None else {}),
+    }
+
+
+def profile_decode_steps(runner, prompts, out_tokens: int, steps: int, dev, batch: int = 256) -> dict:
+    """Per-kernel device time of ``steps`` decode steps at a full batch
+    (``batch`` sequences prefilled from the trace's prompts), from the CUDA
+    activity records of torch.profiler (kernel durations as they ran, inside
+    the graph replays), grouped by kernel name; plus the CUDA-event time of
+    the same replays and the host wall time per step."""
+    from torch.profiler import ProfilerActivity, profile
+
+    seqs = []
+    i = 0
+    while len(seqs) < batch:
+        chunk = [prompts[(i + j) % len(prompts)] for j in range(8)]
+        seqs += runner.prefill_many(chunk, out_tokens)
+        i += 8
+    seqs = seqs[:batch]
+    runner.decode_step(seqs)  # warm
+    torch.cuda.synchronize(dev)
+    runner.timing = []
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            runner.decode_step(seqs)
+        torch.cuda.synchronize(dev)
+        wall = time.perf_counter() - t0
+    replay_ms = sum(a.elapsed_time(b) for a, b in runner.timing) / steps
+    runner.timing = None
+    ctx = float(np.mean([s_.num_tokens for s_ in seqs])) if seqs else 0.0
+    for s_ in seqs:
+        runner.release(s_)
+    rows = {}
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA:
+            r = rows.setdefault(ev.name, [0, 0.0])
+            r[0] += 1
+            r[1] += ev.device_time_total
+    total_us = sum(v[1] for v in rows.values())
+    top = sorted(rows.items(), key=lambda kv: -kv[1][1])
+    return {
+        "batch": batch,
+        "steps": steps,
+        "mean_context_tokens": round(ctx, 1),
+        "event_ms_per_step": round(replay_ms, 4),
+        "host_wall_ms_per_step": round(1e3 * wall / steps, 4),
+        "kernel_us_per_step": round(total_us / steps, 2),
+        "kernels_per_step": round(sum(v[0] for v in rows.values()) / steps, 1),
+        "by_kernel": [
+            {"kernel": k[:120], "launches_per_step": round(v[0] / steps, 2), "us_per_step": round(v[1] / steps, 2),
+             "share": round(v[1] / total_us, 4)}
+            for k, v in top[:25]
+        ],
     }
 
 
@@ -1312,6 +1369,9 @@ def main() -> None:
     ap.add_argument("--model-rate", type=float, default=1000.0,
                     help="cfg2 line: arrival rate per GPU (req/s) of that trace")
     ap.add_argument("--model-kv-gb", type=float, default=60.0, help="cfg2 line: KV budget per GPU of that trace")
+    ap.add_argument("--profile-decode", type=int, default=0,
+                    help="cfg5: after the trace, profile this many decode steps at batch 256 per kernel "
+                         "(torch.profiler CUDA activity)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
