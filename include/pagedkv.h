@@ -97,6 +97,44 @@ int pagedkv_decode_attention(
     int32_t max_blocks_per_seq, float scale, int32_t dtype,
     void *workspace, size_t workspace_bytes, void *stream);
 
+/*
+ * Decode attention with the decode append fused into the same launch.
+ *
+ * Replaces the append + kernel pair of one layer's decode forward
+ * (engine/kernels/paged_attention_integration.py:150-160, then the kernel
+ * call at :164-171 / engine/kernels/paged_attention.py:675-697): for every
+ * sequence s with L = seq_lens[s] > 0, first
+ *   k_cache[table_s[(L-1) / block_size], (L-1) % block_size] = k_new[s]
+ * (and v_new into v_cache), bit-exact, then decode attention over the L
+ * tokens exactly as pagedkv_decode_attention. With cos and sin (rows
+ * [num_seqs, head_dim], stride cos_sin_stride) both q and k_new are rotated
+ * first, rounded as transformers' apply_rotary_pos_emb
+ * (integration.py:108-109) and as pagedkv_kv_append_rope: the pool rows are
+ * bit-identical to that op's and the output to pagedkv_decode_attention on
+ * its rotated q. The rows are written by the CTA that reads that tile, just
+ * before it loads it, so the append costs no launch and no dependency of its
+ * own. k_new / v_new: [num_seqs, num_kv_heads, head_dim], 16-byte aligned,
+ * strides multiples of 8 elements. Shapes that run on the CUDA-core kernel
+ * (block_size < 8 or not a power of two), or unaligned k_new / v_new / cos /
+ * sin, return PAGEDKV_ERR_UNSUPPORTED without launching anything: call
+ * pagedkv_kv_append (or _rope) and pagedkv_decode_attention instead. Same
+ * workspace as pagedkv_decode_attention.
+ */
+int pagedkv_decode_attention_append(
+    void *out, int64_t out_stride_seq, int64_t out_stride_head,
+    const void *q, int64_t q_stride_seq, int64_t q_stride_head,
+    void *k_cache, void *v_cache,
+    const int32_t *block_tables, int64_t block_tables_stride,
+    const int32_t *seq_lens,
+    int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
+    int32_t head_dim, int64_t num_blocks, int32_t block_size,
+    int32_t max_blocks_per_seq,
+    const void *k_new, int64_t k_new_stride_seq, int64_t k_new_stride_head,
+    const void *v_new, int64_t v_new_stride_seq, int64_t v_new_stride_head,
+    const void *cos, const void *sin, int64_t cos_sin_stride,
+    float scale, int32_t dtype, void *workspace, size_t workspace_bytes,
+    void *stream);
+
 /* Bytes of workspace pagedkv_decode_attention needs for this shape on the
  * current device (0 when the launch needs none). */
 size_t pagedkv_decode_attention_workspace_size(

@@ -82,6 +82,19 @@ template <> struct Elem<__nv_bfloat16> {
   __device__ __forceinline__ static __nv_bfloat16 from_float(float x) { return __float2bfloat16_rn(x); }
 };
 
+// One element of transformers' apply_rotary_pos_emb, x * cos + rotate_half(x)
+// * sin, rounded exactly as its 16-bit tensor ops: r(r(a * c) + r(b * s)),
+// where b is the rotation partner (negated for the first half of the head).
+// The fp32 products of 16-bit inputs are exact; each is rounded to T, the sum
+// is formed in fp32 and rounded to T by the caller's store. Shared by every
+// kernel that rotates, so their results are bit-identical.
+template <typename T>
+__device__ __forceinline__ float rope_elem(float a, float c, float b, float s) {
+  const float p1 = Elem<T>::to_float(Elem<T>::from_float(a * c));
+  const float p2 = Elem<T>::to_float(Elem<T>::from_float(b * s));
+  return p1 + p2;
+}
+
 // log2(e): scores are kept in the base-2 domain so exp() becomes one exp2f.
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegInf = -__builtin_huge_valf();

@@ -114,6 +114,14 @@ struct TcParams {
   float *part_acc;      // [grid][H * GP][head_dim] published partial sums
   float2 *part_ml;      // [grid][H * GP] (reference max, denominator) of those
   uint32_t *flags;      // [grid] 1 = CTA's partial published; reset to 0 when consumed
+  // Decode append fused into the launch (k_new == nullptr: none). Sequence s's
+  // new K / V rows [hkv, head_dim] (strides in elements) are written into its
+  // pool slot at position len - 1 by the CTA that reads that tile, before its
+  // TMA load of the tile; with cos != nullptr, K and q are rotated first.
+  const void *k_new, *v_new;
+  int64_t kn_st, kn_sh, vn_st, vn_sh;
+  const void *cos, *sin;  // [num_seqs, head_dim] rows, stride cs_st
+  int64_t cs_st;
 };
 
 __device__ __forceinline__ int seq_len_clamped(const DecodeParams &p, int seq) {
@@ -206,6 +214,59 @@ struct Walker {
     return true;
   }
 };
+
+// The decode append of the tile row a segment reads, run by one producer warp
+// (K or V) just before it loads the segment's last tile: lane l owns elements
+// [8l, 8l + 8) of the 128 * D2-element slice of the new row (the H kv heads of
+// tile row prow), loads them from k_new / v_new, rotates K when RoPE is on
+// (the partner half of each head is D / 16 lanes away), and stores them into
+// the pool row of position len - 1. The generic-proxy stores are fenced
+// against the async proxy, so the TMA load issued after the warp barrier
+// reads the new row. Several query-head chunks of one tile row write the same
+// bytes; the writes are identical, so their order does not matter.
+template <typename T, int H, int D, int D2>
+__device__ __forceinline__ void append_row(const TcParams &tp, const Piece &pc, int prow, bool is_k,
+                                           int32_t blk, int lane) {
+  using E = Elem<T>;
+  const DecodeParams &p = tp.p;
+  const int e = lane * 8;                // element within the slice
+  const int hl = e / D, d = e - hl * D;  // kv head within the tile row, dim
+  const int kv = prow * H + hl;
+  const bool active = lane < 16 * D2 && kv < p.hkv;
+  const T *src = static_cast<const T *>(is_k ? tp.k_new : tp.v_new);
+  const int64_t st = is_k ? tp.kn_st : tp.vn_st, sh = is_k ? tp.kn_sh : tp.vn_sh;
+  uint4 x = make_uint4(0u, 0u, 0u, 0u);
+  if (active) x = ldg16(src + (int64_t)pc.seq * st + (int64_t)kv * sh + d);
+  if (is_k && tp.cos != nullptr) {
+    uint4 xp;  // the rotation partner chunk (all lanes shuffle)
+    xp.x = __shfl_xor_sync(0xffffffffu, x.x, D / 16);
+    xp.y = __shfl_xor_sync(0xffffffffu, x.y, D / 16);
+    xp.z = __shfl_xor_sync(0xffffffffu, x.z, D / 16);
+    xp.w = __shfl_xor_sync(0xffffffffu, x.w, D / 16);
+    if (active) {
+      const T *cs = static_cast<const T *>(tp.cos) + (int64_t)pc.seq * tp.cs_st + d;
+      const T *sn = static_cast<const T *>(tp.sin) + (int64_t)pc.seq * tp.cs_st + d;
+      float a[8], b[8], c[8], sv[8], o[8];
+      E::unpack8(x, a);
+      E::unpack8(xp, b);
+      E::unpack8(ldg16(cs), c);
+      E::unpack8(ldg16(sn), sv);
+      const bool lo = d < D / 2;  // rotate_half: -x[d + D/2] on the first half, x[d - D/2] on the second
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = rope_elem<T>(a[i], c[i], lo ? -b[i] : b[i], sv[i]);
+      x = E::pack8(o);
+    }
+  }
+  if (active && blk >= 0 && blk < p.num_blocks) {
+    const int pos = pc.len - 1;
+    T *pool = static_cast<T *>(const_cast<void *>(is_k ? p.k : p.v));
+    const int64_t row = (int64_t)blk * p.block_size + pos % p.block_size;
+    stg16(pool + row * ((int64_t)p.hkv * D) + (int64_t)prow * 128 * D2 + e, x);
+    fence_proxy_async_global();
+  }
+  __syncwarp();
+  fence_proxy_async_global();
+}
 
 // Running (sum, denominator, reference max) of one correction thread's
 // query columns.
@@ -564,6 +625,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     auto q_issue = [&](const Piece &q, uint32_t i) -> bool {
       if (!PKV_TW(0, mbar_wait(q_empty(i), ring_parity(i, kQSlots) ^ 1u, abort_flag, kTimeoutNs))) return false;
       const uint32_t qbuf = sbase + L::kOffQ + (i % kQSlots) * L::kQBytes;
+      const bool rope = tp.cos != nullptr;
 #pragma unroll
       for (int c = 0; c < kQChunks; ++c) {
         const int idx = lane + c * 32;
@@ -585,9 +647,35 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
                        (in ? (int64_t)q.seq * p.q_ss + (int64_t)(kv * p.group + gq) * p.q_sh + d : 0);
         const uint32_t addr =
             qbuf + sub * L::kQSubBytes + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
-        cp_async_16(addr, src, in ? 16u : 0u);
+        if (!rope) {
+          cp_async_16(addr, src, in ? 16u : 0u);
+        } else {
+          // rope(q) = q * cos + rotate_half(q) * sin, rounded as the append
+          // kernels round it, staged with plain shared stores
+          uint4 r = make_uint4(0u, 0u, 0u, 0u);
+          if (in) {
+            const bool lo = d < D / 2;
+            const T *cs = static_cast<const T *>(tp.cos) + (int64_t)q.seq * tp.cs_st + d;
+            const T *sn = static_cast<const T *>(tp.sin) + (int64_t)q.seq * tp.cs_st + d;
+            float a[8], b[8], cv[8], sv[8], o[8];
+            E::unpack8(ldg16(src), a);
+            E::unpack8(ldg16(src + (lo ? D / 2 : -(D / 2))), b);
+            E::unpack8(ldg16(cs), cv);
+            E::unpack8(ldg16(sn), sv);
+#pragma unroll
+            for (int k2 = 0; k2 < 8; ++k2) o[k2] = rope_elem<T>(a[k2], cv[k2], lo ? -b[k2] : b[k2], sv[k2]);
+            r = E::pack8(o);
+          }
+          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(r.x), "r"(r.y), "r"(r.z),
+                       "r"(r.w)
+                       : "memory");
+        }
       }
-      cp_async_mbar_arrive(q_full(i));
+      if (!rope) {
+        cp_async_mbar_arrive(q_full(i));
+      } else {
+        mbar_arrive(q_full(i));  // releases this lane's shared stores to the S issuer
+      }
       return true;
     };
 
@@ -614,6 +702,12 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         }
         const uint32_t slot = wk % 3u;
         if (wofs + bpt >= 32 || j + 1 == pc.ntiles) ++wk;  // last tile of this window
+        if (tp.k_new != nullptr && pc.t1 == pc.len && j + 1 == pc.ntiles) {
+          // The segment's last tile holds position len - 1: write the new row
+          // there first (block b of this tile's window entries).
+          const int b = (pc.len - 1) / p.block_size - (lb0 + j * bpt);
+          append_row<T, H, D, D2>(tp, pc, pc.hg / nch, is_k, win[slot * 32 + wofs + b], lane);
+        }
         for (int sub = 0; sub < D2; ++sub) {  // one ring stage per 128-element sub-row
           if (!PKV_TW(1, mbar_wait(is_k ? kempty(stage) : vempty(stage), sphase ^ 1u, abort_flag, kTimeoutNs))) {
             ok = false;
@@ -1321,7 +1415,7 @@ size_t tc_workspace_bytes(int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_
 }
 
 int tc_launch(DecodeParams &p, int dtype, void *workspace, size_t workspace_bytes, int32_t num_sms,
-              cudaStream_t stream, int *launches, std::string *error) {
+              cudaStream_t stream, int *launches, std::string *error, const AppendParams *append) {
   *launches = 0;
   const int32_t max_tokens = p.max_blocks * p.block_size;
   const TcPlan pl = make_plan(p.num_seqs, p.hq, p.hkv, p.head_dim, max_tokens, num_sms);
@@ -1358,6 +1452,17 @@ int tc_launch(DecodeParams &p, int dtype, void *workspace, size_t workspace_byte
   tp.part_ml = reinterpret_cast<float2 *>(ws);
   ws += align256(slots * hqs * sizeof(float2));
   tp.part_acc = reinterpret_cast<float *>(ws);
+  if (append != nullptr) {
+    tp.k_new = append->k_new;
+    tp.v_new = append->v_new;
+    tp.kn_st = append->k_st;
+    tp.kn_sh = append->k_sh;
+    tp.vn_st = append->v_st;
+    tp.vn_sh = append->v_sh;
+    tp.cos = append->cos;
+    tp.sin = append->sin;
+    tp.cs_st = append->cs_st;
+  }
   tp.p = p;
   cudaError_t e = dtype == PAGEDKV_DTYPE_BF16 ? dispatch_tc<__nv_bfloat16>(pl, mk, mv, tp, stream)
                                   : dispatch_tc<__half>(pl, mk, mv, tp, stream);

@@ -39,14 +39,6 @@ __device__ __forceinline__ void store8(T *p, bool vec, const float (&f)[8]) {
   }
 }
 
-// Rounded exactly as the tensor ops: r(r(a * c) + r(b * s)).
-template <typename T>
-__device__ __forceinline__ float rope_elem(float a, float c, float b, float s) {
-  const float p1 = Elem<T>::to_float(Elem<T>::from_float(a * c));
-  const float p2 = Elem<T>::to_float(Elem<T>::from_float(b * s));
-  return p1 + p2;  // rounded to T by the store
-}
-
 // I is the flat work index type: 32-bit whenever the launch has fewer than
 // 2^32 items (the divisions below are then the cheap 32-bit ones), else 64-bit.
 template <typename T, bool VEC, typename I>

@@ -128,16 +128,19 @@ size_t pagedkv_decode_attention_workspace_size(int32_t num_seqs, int32_t num_q_h
   return simt_workspace_bytes(num_seqs, num_q_heads, head_dim, plan);
 }
 
-int pagedkv_decode_attention(void *out, int64_t out_stride_seq, int64_t out_stride_head,
-                             const void *q, int64_t q_stride_seq, int64_t q_stride_head,
-                             const void *k_cache, const void *v_cache,
-                             const int32_t *block_tables, int64_t block_tables_stride,
-                             const int32_t *seq_lens, int32_t uniform_seq_len, int32_t num_seqs,
-                             int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
-                             int64_t num_blocks, int32_t block_size, int32_t max_blocks_per_seq,
-                             float scale, int32_t dtype, void *workspace, size_t workspace_bytes,
-                             void *stream) {
-  NvtxRange nvtx("pagedkv_decode_attention");
+}  // extern "C"
+
+namespace {
+
+// Decode attention, optionally with the decode append fused into the
+// tensor-core launch (`ap`); shared by the two entry points.
+int decode_entry(void *out, int64_t out_stride_seq, int64_t out_stride_head, const void *q,
+                 int64_t q_stride_seq, int64_t q_stride_head, const void *k_cache, const void *v_cache,
+                 const int32_t *block_tables, int64_t block_tables_stride, const int32_t *seq_lens,
+                 int32_t uniform_seq_len, int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
+                 int32_t head_dim, int64_t num_blocks, int32_t block_size, int32_t max_blocks_per_seq,
+                 float scale, int32_t dtype, void *workspace, size_t workspace_bytes, void *stream,
+                 const AppendParams *ap) {
   t_last_launches = 0;
   t_last_kernel = "none";
   if (num_seqs < 0) return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "num_seqs must be >= 0 (got %d)", num_seqs);
@@ -196,6 +199,11 @@ int pagedkv_decode_attention(void *out, int64_t out_stride_seq, int64_t out_stri
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int32_t max_tokens = max_blocks_per_seq * block_size;
 
+  if (ap != nullptr && !tc_eligible(num_q_heads, num_kv_heads, head_dim, block_size))
+    return fail(PAGEDKV_ERR_UNSUPPORTED,
+                "fused append: this shape (block_size %d) runs on the CUDA-core kernel, which has no fused "
+                "append; call pagedkv_kv_append then pagedkv_decode_attention",
+                block_size);
   if (tc_eligible(num_q_heads, num_kv_heads, head_dim, block_size)) {
     const size_t need = tc_workspace_bytes(num_seqs, num_q_heads, num_kv_heads, head_dim,
                                            max_tokens, di.num_sms);
@@ -203,7 +211,7 @@ int pagedkv_decode_attention(void *out, int64_t out_stride_seq, int64_t out_stri
       return fail(PAGEDKV_ERR_WORKSPACE, "workspace too small: need %zu bytes, got %zu", need,
                   workspace_bytes);
     int launches = 0;
-    rc = tc_launch(p, dtype, workspace, need, di.num_sms, st, &launches, &t_last_error);
+    rc = tc_launch(p, dtype, workspace, need, di.num_sms, st, &launches, &t_last_error, ap);
     if (rc != PAGEDKV_OK) return rc;
     t_last_launches = launches;
     t_last_kernel = "tc";
@@ -235,6 +243,56 @@ int pagedkv_decode_attention(void *out, int64_t out_stride_seq, int64_t out_stri
   t_last_launches = launches;
   t_last_kernel = "simt";
   return PAGEDKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pagedkv_decode_attention(void *out, int64_t out_stride_seq, int64_t out_stride_head,
+                             const void *q, int64_t q_stride_seq, int64_t q_stride_head,
+                             const void *k_cache, const void *v_cache,
+                             const int32_t *block_tables, int64_t block_tables_stride,
+                             const int32_t *seq_lens, int32_t uniform_seq_len, int32_t num_seqs,
+                             int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                             int64_t num_blocks, int32_t block_size, int32_t max_blocks_per_seq,
+                             float scale, int32_t dtype, void *workspace, size_t workspace_bytes,
+                             void *stream) {
+  NvtxRange nvtx("pagedkv_decode_attention");
+  return decode_entry(out, out_stride_seq, out_stride_head, q, q_stride_seq, q_stride_head, k_cache, v_cache,
+                      block_tables, block_tables_stride, seq_lens, uniform_seq_len, num_seqs, num_q_heads,
+                      num_kv_heads, head_dim, num_blocks, block_size, max_blocks_per_seq, scale, dtype,
+                      workspace, workspace_bytes, stream, nullptr);
+}
+
+int pagedkv_decode_attention_append(
+    void *out, int64_t out_stride_seq, int64_t out_stride_head, const void *q, int64_t q_stride_seq,
+    int64_t q_stride_head, void *k_cache, void *v_cache, const int32_t *block_tables,
+    int64_t block_tables_stride, const int32_t *seq_lens, int32_t num_seqs, int32_t num_q_heads,
+    int32_t num_kv_heads, int32_t head_dim, int64_t num_blocks, int32_t block_size,
+    int32_t max_blocks_per_seq, const void *k_new, int64_t k_new_stride_seq, int64_t k_new_stride_head,
+    const void *v_new, int64_t v_new_stride_seq, int64_t v_new_stride_head, const void *cos,
+    const void *sin, int64_t cos_sin_stride, float scale, int32_t dtype, void *workspace,
+    size_t workspace_bytes, void *stream) {
+  NvtxRange nvtx("pagedkv_decode_attention_append");
+  t_last_launches = 0;
+  t_last_kernel = "none";
+  if (!seq_lens) return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "fused append: seq_lens is required");
+  if (!k_new || !v_new) return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "fused append: null k_new / v_new");
+  if ((cos == nullptr) != (sin == nullptr))
+    return fail(PAGEDKV_ERR_INVALID_ARGUMENT, "fused append: pass both cos and sin, or neither");
+  if (!aligned16(k_new) || !aligned16(v_new) || (k_new_stride_seq % 8) || (k_new_stride_head % 8) ||
+      (v_new_stride_seq % 8) || (v_new_stride_head % 8) ||
+      (cos && (!aligned16(cos) || !aligned16(sin) || (cos_sin_stride % 8))))
+    return fail(PAGEDKV_ERR_UNSUPPORTED,
+                "fused append: k_new / v_new (and cos / sin) must be 16-byte aligned with strides that are "
+                "multiples of 8 elements");
+  AppendParams ap{k_new, k_new_stride_seq, k_new_stride_head, v_new, v_new_stride_seq, v_new_stride_head,
+                  cos, sin, cos_sin_stride};
+  return decode_entry(out, out_stride_seq, out_stride_head, q, q_stride_seq, q_stride_head, k_cache, v_cache,
+                      block_tables, block_tables_stride, seq_lens, 0, num_seqs, num_q_heads, num_kv_heads,
+                      head_dim, num_blocks, block_size, max_blocks_per_seq, scale, dtype, workspace,
+                      workspace_bytes, stream, &ap);
 }
 
 int pagedkv_kv_append(void *k_cache, void *v_cache, const void *k_new, int64_t k_new_stride_tok,

@@ -14,6 +14,7 @@ from .paged_attention import (
     last_decode_launch_info,
     pad_block_tables,
     paged_attention_decode,
+    paged_attention_decode_append,
     paged_attention_decode_batched,
     paged_attention_decode_v1,
     paged_attention_decode_v2,
@@ -28,6 +29,7 @@ __all__ = [
     "last_decode_launch_info",
     "pad_block_tables",
     "paged_attention_decode",
+    "paged_attention_decode_append",
     "paged_attention_decode_batched",
     "paged_attention_decode_v1",
     "paged_attention_decode_v2",

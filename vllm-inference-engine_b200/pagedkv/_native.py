@@ -62,6 +62,24 @@ _SIGNATURES = [
         ],
     ),
     (
+        "pagedkv_decode_attention_append",
+        ctypes.c_int,
+        [
+            _c_vp, _c_i64, _c_i64,          # out, strides
+            _c_vp, _c_i64, _c_i64,          # q, strides
+            _c_vp, _c_vp,                   # k_cache, v_cache
+            _c_vp, _c_i64,                  # block_tables, stride
+            _c_vp,                          # seq_lens
+            _c_i32, _c_i32, _c_i32, _c_i32,  # num_seqs, hq, hkv, head_dim
+            _c_i64, _c_i32, _c_i32,         # num_blocks, block_size, max_blocks_per_seq
+            _c_vp, _c_i64, _c_i64,          # k_new, strides
+            _c_vp, _c_i64, _c_i64,          # v_new, strides
+            _c_vp, _c_vp, _c_i64,           # cos, sin, row stride
+            _c_f32, _c_i32,                 # scale, dtype
+            _c_vp, _c_sz, _c_vp,            # workspace, bytes, stream
+        ],
+    ),
+    (
         "pagedkv_decode_attention_workspace_size",
         _c_sz,
         [_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32],

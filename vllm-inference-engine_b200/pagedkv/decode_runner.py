@@ -26,7 +26,7 @@ from typing import Dict, List, Optional, Sequence
 import numpy as np
 import torch
 
-from .paged_attention import kv_append_rope, kv_write_prefill, paged_attention_decode_batched
+from .paged_attention import kv_write_prefill, paged_attention_decode_append
 
 
 @dataclass
@@ -194,9 +194,9 @@ class PagedDecodeRunner:
             q = attn.q_proj(h).view(b, self.hq, self.head_dim)
             k = attn.k_proj(h).view(b, self.hkv, self.head_dim)
             v = attn.v_proj(h).view(b, self.hkv, self.head_dim)
-            q_rot = kv_append_rope(q, k, v, cos2, sin2, self.k_cache[li], self.v_cache[li], slots)
-            o = paged_attention_decode_batched(q_rot, self.k_cache[li], self.v_cache[li], tables, lens,
-                                               attn.scaling)
+            # RoPE of q and k, the append of k and v and the attention: one launch
+            o = paged_attention_decode_append(q, self.k_cache[li], self.v_cache[li], tables, lens, attn.scaling,
+                                              k, v, cos2, sin2, slot_mapping=slots)
             x = x + attn.o_proj(o.reshape(b, 1, -1))
             x = x + layer.mlp(layer.post_attention_layernorm(x))
         x = m.norm(x)

@@ -36,6 +36,7 @@ import torch
 from . import prefix_index
 from .paged_attention import (
     copy_blocks,
+    paged_attention_decode_append,
     kv_append_rope,
     kv_write_prefill,
     pad_block_tables,
@@ -175,21 +176,17 @@ def paged_decode_attention_forward(
     pool = ctx.pool
     k_cache = pool.k_cache[layer_idx]
     v_cache = pool.v_cache[layer_idx]
-    # RoPE on q and k fused with the append of k and v through the slot
-    # mapping: one launch instead of the rotary tensor ops plus the append.
+    # RoPE on q and k and the append of k and v fused into the attention
+    # launch: one kernel instead of the rotary tensor ops, the append loop and
+    # the attention kernel.
     bsz = query_states.shape[0]
     cos2 = cos.reshape(-1, cos.shape[-1])  # [B, 1, D] (or a broadcast [1, 1, D]) -> rows
     sin2 = sin.reshape(-1, sin.shape[-1])
     if cos2.shape[0] != bsz:
         cos2, sin2 = cos2.expand(bsz, -1), sin2.expand(bsz, -1)
-    q_rot = kv_append_rope(query_states, key_states, value_states, cos2, sin2, k_cache, v_cache, ctx.slot_mapping)
-    attn_output = paged_attention_decode_batched(
-        q=q_rot,
-        k_cache=k_cache,
-        v_cache=v_cache,
-        block_tables=ctx.padded_block_tables,
-        seq_lens=ctx.seq_lens_tensor,
-        scale=scale,
+    attn_output = paged_attention_decode_append(
+        query_states, k_cache, v_cache, ctx.padded_block_tables, ctx.seq_lens_tensor, scale,
+        key_states, value_states, cos2, sin2, slot_mapping=ctx.slot_mapping,
     )
     attn_output = attn_output.reshape(*input_shape, -1).contiguous()
     attn_output = self.o_proj(attn_output)
@@ -347,8 +344,8 @@ class DecodeGraphs:
             v = attn.v_proj(h).view(b, -1, attn.head_dim)
             scale = attn.scaling if hasattr(attn, "scaling") else 1.0 / math.sqrt(attn.head_dim)
             li_pool = attn.layer_idx if hasattr(attn, "layer_idx") else li
-            q_rot = kv_append_rope(q, k, v, cos2, sin2, k_caches[li_pool], v_caches[li_pool], slots)
-            o = paged_attention_decode_batched(q_rot, k_caches[li_pool], v_caches[li_pool], tables, lens, scale)
+            o = paged_attention_decode_append(q, k_caches[li_pool], v_caches[li_pool], tables, lens, scale, k, v,
+                                              cos2, sin2, slot_mapping=slots)
             x = residual + attn.o_proj(o.reshape(b, 1, -1).contiguous())
             residual = x
             x = residual + layer.mlp(layer.post_attention_layernorm(x))

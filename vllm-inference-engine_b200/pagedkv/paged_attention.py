@@ -573,6 +573,122 @@ def kv_write_prefill(
     _debug_check(dev, "kv_write_prefill")
 
 
+def _decode_slots(block_tables: torch.Tensor, seq_lens: torch.Tensor, block_size: int) -> torch.Tensor:
+    """int64 slot of position len - 1 of every sequence (-1 for length 0),
+    computed on the device from the tables and lengths."""
+    pos = seq_lens.to(torch.int64) - 1
+    p0 = pos.clamp(min=0)
+    blk = block_tables.gather(1, (p0 // block_size).view(-1, 1)).view(-1).to(torch.int64)
+    return torch.where(pos >= 0, blk * block_size + p0 % block_size, torch.full_like(pos, -1))
+
+
+def paged_attention_decode_append(
+    q: torch.Tensor,             # [num_seqs, num_q_heads, head_dim]
+    k_cache: torch.Tensor,       # [num_blocks, block_size, num_kv_heads, head_dim]
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,  # [num_seqs, max_blocks_per_seq] int32
+    seq_lens: torch.Tensor,      # [num_seqs] int32, lengths AFTER this step's token
+    scale: float,
+    k_new: torch.Tensor,         # [num_seqs, num_kv_heads, head_dim]
+    v_new: torch.Tensor,
+    cos: torch.Tensor | None = None,  # [num_seqs, head_dim] (or [num_seqs, 1, head_dim])
+    sin: torch.Tensor | None = None,
+    slot_mapping: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """One layer's decode step in ONE launch: the KV append of each sequence's
+    new K / V row at position ``seq_len - 1`` of its block table, then batched
+    decode attention over the ``seq_len`` tokens (the reference's append,
+    paged_attention_integration.py:150-160, followed by its kernel call,
+    :164-171). With ``cos`` / ``sin``, q and k are first rotated as
+    transformers' ``apply_rotary_pos_emb`` (integration.py:108-109) rounds
+    them, as :func:`kv_append_rope` does.
+
+    The pool rows written are bit-identical to :func:`kv_append` /
+    :func:`kv_append_rope` at those slots, and the output to
+    :func:`paged_attention_decode_batched` on the (rotated) q. Shapes served
+    by the CUDA-core kernel (block_size < 8) or unaligned new rows run those
+    two operations as separate launches (``slot_mapping``, if given, must be
+    the slots of position ``seq_len - 1``; else it is computed on the device).
+    """
+    assert q.is_cuda and k_cache.is_cuda and v_cache.is_cuda and block_tables.is_cuda and seq_lens.is_cuda
+    assert q.dtype in _DTYPES and k_cache.dtype == q.dtype and v_cache.dtype == q.dtype
+    assert k_new.dtype == q.dtype and v_new.dtype == q.dtype
+    assert block_tables.dtype == torch.int32 and seq_lens.dtype == torch.int32
+    assert k_cache.is_contiguous() and v_cache.is_contiguous() and v_cache.shape == k_cache.shape
+    num_seqs, num_q_heads, head_dim = q.shape
+    num_blocks, block_size, num_kv_heads, head_dim_k = k_cache.shape
+    assert head_dim == head_dim_k, f"Head dimensions must match: {head_dim} vs {head_dim_k}"
+    assert num_q_heads % num_kv_heads == 0
+    assert block_tables.shape[0] == num_seqs and seq_lens.shape[0] == num_seqs
+    row = (num_kv_heads, head_dim)
+    k3 = k_new if k_new.dim() == 3 and k_new.shape[1:] == row else k_new.reshape(-1, num_kv_heads, head_dim)
+    v3 = v_new if v_new.dim() == 3 and v_new.shape[1:] == row else v_new.reshape(-1, num_kv_heads, head_dim)
+    assert k3.shape[0] == num_seqs and v3.shape[0] == num_seqs
+    rope = cos is not None
+    assert rope == (sin is not None), "pass both cos and sin, or neither"
+    if rope:
+        c2 = cos.reshape(num_seqs, head_dim) if cos.dim() != 2 else cos
+        s2 = sin.reshape(num_seqs, head_dim) if sin.dim() != 2 else sin
+        assert c2.dtype == q.dtype and s2.dtype == q.dtype and c2.shape == (num_seqs, head_dim)
+        if c2.stride() != s2.stride() or c2.stride(-1) != 1:
+            c2, s2 = c2.contiguous(), s2.contiguous()
+    out = torch.empty_like(q)
+    if num_seqs == 0:
+        return out
+    if block_tables.stride(-1) != 1:
+        block_tables = block_tables.contiguous()
+    if not seq_lens.is_contiguous():
+        seq_lens = seq_lens.contiguous()
+    if k3.stride(2) != 1:
+        k3 = k3.contiguous()
+    if v3.stride(2) != 1:
+        v3 = v3.contiguous()
+    qq = q if _qo_ok(q) else q.contiguous()
+    dtype = _DTYPES[q.dtype]
+    max_blocks = block_tables.shape[1]
+    idx = q.get_device()
+    lib = _native.lib()
+    key = (idx, num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks, dtype)
+    nbytes = _ws_sizes.get(key)
+    if nbytes is None:
+        nbytes = lib.pagedkv_decode_attention_workspace_size(
+            num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks, dtype
+        )
+        _ws_sizes[key] = nbytes
+    ws = _workspace(idx, nbytes)
+    qs, os_, ks, vs = qq.stride(), out.stride(), k3.stride(), v3.stride()
+    rc = _launch(
+        idx, lib.pagedkv_decode_attention_append,
+        out.data_ptr(), os_[0], os_[1],
+        qq.data_ptr(), qs[0], qs[1],
+        k_cache.data_ptr(), v_cache.data_ptr(),
+        block_tables.data_ptr(), block_tables.stride(0),
+        seq_lens.data_ptr(),
+        num_seqs, num_q_heads, num_kv_heads, head_dim,
+        num_blocks, block_size, max_blocks,
+        k3.data_ptr(), ks[0], ks[1],
+        v3.data_ptr(), vs[0], vs[1],
+        c2.data_ptr() if rope else None, s2.data_ptr() if rope else None, c2.stride(0) if rope else 0,
+        float(scale), dtype,
+        ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+    )
+    if rc == _native.PAGEDKV_ERR_UNSUPPORTED:
+        # nothing was launched: the append and the attention as two launches
+        slots = slot_mapping if slot_mapping is not None else _decode_slots(block_tables, seq_lens, block_size)
+        if rope:
+            q_rot = kv_append_rope(q, k3, v3, c2, s2, k_cache, v_cache, slots)
+        else:
+            kv_append(k3, v3, k_cache, v_cache, slots)
+            q_rot = q
+        _decode_into(out, q_rot, k_cache, v_cache, block_tables, seq_lens, 0, scale)
+        return out
+    if rc:
+        _native.check(rc, "pagedkv_decode_attention_append")
+    if _DEBUG:
+        _debug_check(q.device, "paged decode attention + append")
+    return out
+
+
 def last_decode_launch_info() -> tuple[int, str]:
     """(kernel launches, kernel family) of the last decode call on this thread."""
     lib = _native.lib()
