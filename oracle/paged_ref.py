@@ -105,10 +105,15 @@ def paged_attention_ref_f64(
 
 def decode_slots(block_tables: Sequence[Sequence[int]], seq_lens: Sequence[int], block_size: int) -> np.ndarray:
     """Slot of the token a decode step writes for each sequence, whose
-    ``seq_len`` already counts that token (integration.py:150-155)."""
+    ``seq_len`` already counts that token (integration.py:150-155); -1 (no
+    write) for a sequence of length 0, which holds no token (the reference's
+    decode step never sees one: it bumps the length before the write)."""
     slots = np.empty(len(seq_lens), dtype=np.int64)
     for b, n in enumerate(seq_lens):
         pos = int(n) - 1
+        if pos < 0:
+            slots[b] = -1
+            continue
         slots[b] = int(block_tables[b][pos // block_size]) * block_size + pos % block_size
     return slots
 
