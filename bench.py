@@ -237,6 +237,31 @@ def make_workload(name: str, rank: int, gqa: int = 7) -> Workload:
             f"{hq}q/{hkv}kv heads (GQA {gqa}), block_size 16, q x30, shuffled tables",
             hq, hkv, d, bs, nb, tables, lens, _slots_for(tables, lens, bs), q, k_new, v_new, None,
         )
+    if name == "cfg5l":
+        # one layer of a config-5 decode step at its saturated batch: 256
+        # sequences of the Qwen2.5-0.5B shape, prompts U[64, 1024] plus up to
+        # 128 generated tokens
+        n, hq, hkv, d, bs = 256, 14, 2, 64, 16
+        rng = np.random.default_rng(3500 + rank)
+        lens_l = [int(x) for x in rng.integers(64, 1025, n) + rng.integers(1, 129, n)]
+        need = [(x + bs - 1) // bs for x in lens_l]
+        nb = sum(need) + 64
+        perm = list(range(nb))
+        random.Random(47 + rank).shuffle(perm)
+        rows, at = [], 0
+        for c in need:
+            rows.append(perm[at : at + c])
+            at += c
+        tables = _tables_from_lists(rows)
+        lens = torch.tensor(lens_l, dtype=torch.int32)
+        g = torch.Generator().manual_seed(1400 + rank)
+        q, k_new, v_new = _qkv(g, n, hq, hkv, d)
+        return Workload(
+            "cfg5l",
+            "cfg5l: one layer of a config-5 decode step at batch 256 (14q/2kv, head_dim 64, block_size 16, "
+            "lengths = prompt U[64,1024] + U[1,128] generated), KV append + decode attention",
+            hq, hkv, d, bs, nb, tables, lens, _slots_for(tables, lens, bs), q, k_new, v_new, None,
+        )
     if name == "d256":
         # beyond the BASELINE configs: the head_dim-256 mode (Gemma-2-9B-like
         # 8 query / 4 kv heads per shard), 64 sequences x 2048 tokens
@@ -713,6 +738,15 @@ def run_ours(args) -> None:
         vcs.append(pl["v_cache"])
     # per-layer step inputs: distinct buffers holding the same seeded values
     qs = [wl.q.to(dev) for _ in range(L)]
+    # --rope: the step rotates q and k as the model's decode forward does
+    # (cos / sin rows of each sequence's position, fused into the launch)
+    if args.rope:
+        inv = 1.0 / (1000000.0 ** (torch.arange(0, wl.head_dim, 2, dtype=torch.float32) / wl.head_dim))
+        ang = (wl.lens.to(torch.float32) - 1)[:, None] * inv[None]
+        emb = torch.cat([ang, ang], dim=-1)
+        cos_t, sin_t = emb.cos().half().to(dev), emb.sin().half().to(dev)
+    else:
+        cos_t = sin_t = None
     kns = [wl.k_new.to(dev) for _ in range(L)]
     vns = [wl.v_new.to(dev) for _ in range(L)]
     tables = wl.tables.to(dev)
@@ -728,7 +762,8 @@ def run_ours(args) -> None:
         # the decode attention (pagedkv.paged_attention_decode_append)
         for layer in range(L):
             outs[layer] = pagedkv.paged_attention_decode_append(qs[layer], kcs[layer], vcs[layer], tables, lens,
-                                                                scale, kns[layer], vns[layer], slot_mapping=slots)
+                                                                scale, kns[layer], vns[layer], cos_t, sin_t,
+                                                                slot_mapping=slots)
 
     def step():
         if pairs is not None:
@@ -740,8 +775,12 @@ def run_ours(args) -> None:
             pagedkv.paged_attention_decode_batched(qs[layer], kcs[layer], vcs[layer], tables, lens, scale)
 
     # correctness spot-check of this shard against the oracle (first and last
-    # sequence of the first and last layer)
+    # sequence of the first and last layer; with --rope on the rotated q)
     step()
+    if args.rope:
+        qs_chk = [paged_ref.rope_ref(qs[layer].cpu(), cos_t.cpu(), sin_t.cpu()) for layer in range(L)]
+    else:
+        qs_chk = qs
     torch.cuda.synchronize(dev)
     sel = [0, wl.num_seqs - 1]
     nbk = [(int(wl.lens[s_]) + wl.block_size - 1) // wl.block_size for s_ in sel]
@@ -751,7 +790,7 @@ def run_ours(args) -> None:
     max_err = 0.0
     for layer in sorted({0, L - 1}):
         ref = paged_ref.paged_attention_ref(
-            qs[layer][sel].float().cpu(), kcs[layer][idx].float().cpu(), vcs[layer][idx].float().cpu(),
+            qs_chk[layer][sel].float().cpu(), kcs[layer][idx].float().cpu(), vcs[layer][idx].float().cpu(),
             [[remap[int(b)] for b in wl.tables[s_, :n].tolist()] for s_, n in zip(sel, nbk)],
             [int(wl.lens[s_]) for s_ in sel], scale,
         )
@@ -845,8 +884,8 @@ def run_ours(args) -> None:
             pagedkv.copy_blocks(kcs, vcs, pairs)
         for layer in range(L):
             dq, dk, dv = views[3 + 3 * layer : 6 + 3 * layer]
-            o = pagedkv.paged_attention_decode_append(dq, kcs[layer], vcs[layer], dt, dl, scale, dk, dv,
-                                                      slot_mapping=ds)
+            o = pagedkv.paged_attention_decode_append(dq, kcs[layer], vcs[layer], dt, dl, scale, dk, dv, cos_t,
+                                                      sin_t, slot_mapping=ds)
             out_buf[layer].copy_(o)
 
     d_in = torch.empty(offs[-1], dtype=torch.uint8, device=dev)
@@ -995,7 +1034,8 @@ def run_ours(args) -> None:
             "layers_per_step": L,
             "step": f"one decode step of the paged path over {L} layers (one pool per layer): "
                     + ("the copy-on-write copy over all layers, then " if pairs is not None else "")
-                    + "per layer the KV append and the decode attention, fused into one launch",
+                    + ("per layer the RoPE of q and k, " if args.rope else "per layer ")
+                    + "the KV append and the decode attention, fused into one launch",
             "num_seqs_per_gpu": wl.num_seqs,
             "total_context_tokens_per_gpu": int(wl.lens.to(torch.int64).sum()),
             "heads": f"{wl.num_q_heads}q/{wl.num_kv_heads}kv",
@@ -1373,12 +1413,14 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg4-cow", "cfg5", "ops", "d256"],
+    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg4-cow", "cfg5", "cfg5l", "ops", "d256"],
                     default="cfg2")
     ap.add_argument("--requests", type=int, default=2000, help="cfg5: requests per GPU")
     ap.add_argument("--rate", type=float, default=32.0, help="cfg5: Poisson arrival rate per GPU (req/s)")
     ap.add_argument("--kv-budget-gb", type=float, default=60.0, help="cfg5: KV pool budget per GPU")
     ap.add_argument("--gqa", type=int, default=7, help="GQA group for --workload cfg3 (1, 2, 4 or 7)")
+    ap.add_argument("--rope", action="store_true",
+                    help="the step also rotates q and k (RoPE fused into the launch, as the model's forward)")
     ap.add_argument("--layers", type=int, default=24,
                     help="layers per decode step (one pool each; Qwen2.5-0.5B has 24)")
     ap.add_argument("--model-requests", type=int, default=256,

@@ -216,27 +216,52 @@ struct Walker {
 };
 
 // The decode append of the tile row a segment reads, run by one producer warp
-// (K or V) just before it loads the segment's last tile: lane l owns elements
-// [8l, 8l + 8) of the 128 * D2-element slice of the new row (the H kv heads of
-// tile row prow), loads them from k_new / v_new, rotates K when RoPE is on
-// (the partner half of each head is D / 16 lanes away), and stores them into
-// the pool row of position len - 1. The generic-proxy stores are fenced
-// against the async proxy, so the TMA load issued after the warp barrier
-// reads the new row. Several query-head chunks of one tile row write the same
-// bytes; the writes are identical, so their order does not matter.
+// (K or V) for the segment's last tile: lane l owns elements [8l, 8l + 8) of
+// the 128 * D2-element slice of the new row (the H kv heads of tile row prow).
+// append_fetch issues the global loads of the new row (and of the cos / sin
+// chunks for K with RoPE) one piece ahead, so the data sits in registers when
+// the tile comes up; append_store rotates K when RoPE is on (the partner half
+// of each head is D / 16 lanes away), stores the slice into the pool row of
+// position len - 1 and fences the generic-proxy stores against the async
+// proxy, so the TMA load issued after the warp barrier reads the new row.
+// Several query-head chunks of one tile row write the same bytes; the writes
+// are identical, so their order does not matter.
+struct NewRow {
+  uint4 x, c, s;  // row chunk; cos / sin chunks (K with RoPE)
+};
+
 template <typename T, int H, int D, int D2>
-__device__ __forceinline__ void append_row(const TcParams &tp, const Piece &pc, int prow, bool is_k,
-                                           int32_t blk, int lane) {
-  using E = Elem<T>;
+__device__ __forceinline__ NewRow append_fetch(const TcParams &tp, const Piece &pc, int nch, bool is_k, int lane) {
+  NewRow r;
+  r.x = r.c = r.s = make_uint4(0u, 0u, 0u, 0u);
+  if (tp.k_new == nullptr || pc.t1 != pc.len) return r;
   const DecodeParams &p = tp.p;
+  const int prow = pc.hg / nch;
   const int e = lane * 8;                // element within the slice
   const int hl = e / D, d = e - hl * D;  // kv head within the tile row, dim
   const int kv = prow * H + hl;
+  if (lane < 16 * D2 && kv < p.hkv) {
+    const T *src = static_cast<const T *>(is_k ? tp.k_new : tp.v_new);
+    const int64_t st = is_k ? tp.kn_st : tp.vn_st, sh = is_k ? tp.kn_sh : tp.vn_sh;
+    r.x = ldg16(src + (int64_t)pc.seq * st + (int64_t)kv * sh + d);
+    if (is_k && tp.cos != nullptr) {
+      r.c = ldg16(static_cast<const T *>(tp.cos) + (int64_t)pc.seq * tp.cs_st + d);
+      r.s = ldg16(static_cast<const T *>(tp.sin) + (int64_t)pc.seq * tp.cs_st + d);
+    }
+  }
+  return r;
+}
+
+template <typename T, int H, int D, int D2>
+__device__ __forceinline__ void append_store(const TcParams &tp, const Piece &pc, int prow, bool is_k,
+                                             int32_t blk, int lane, const NewRow &r) {
+  using E = Elem<T>;
+  const DecodeParams &p = tp.p;
+  const int e = lane * 8;
+  const int hl = e / D, d = e - hl * D;
+  const int kv = prow * H + hl;
   const bool active = lane < 16 * D2 && kv < p.hkv;
-  const T *src = static_cast<const T *>(is_k ? tp.k_new : tp.v_new);
-  const int64_t st = is_k ? tp.kn_st : tp.vn_st, sh = is_k ? tp.kn_sh : tp.vn_sh;
-  uint4 x = make_uint4(0u, 0u, 0u, 0u);
-  if (active) x = ldg16(src + (int64_t)pc.seq * st + (int64_t)kv * sh + d);
+  uint4 x = r.x;
   if (is_k && tp.cos != nullptr) {
     uint4 xp;  // the rotation partner chunk (all lanes shuffle)
     xp.x = __shfl_xor_sync(0xffffffffu, x.x, D / 16);
@@ -244,13 +269,11 @@ __device__ __forceinline__ void append_row(const TcParams &tp, const Piece &pc, 
     xp.z = __shfl_xor_sync(0xffffffffu, x.z, D / 16);
     xp.w = __shfl_xor_sync(0xffffffffu, x.w, D / 16);
     if (active) {
-      const T *cs = static_cast<const T *>(tp.cos) + (int64_t)pc.seq * tp.cs_st + d;
-      const T *sn = static_cast<const T *>(tp.sin) + (int64_t)pc.seq * tp.cs_st + d;
       float a[8], b[8], c[8], sv[8], o[8];
       E::unpack8(x, a);
       E::unpack8(xp, b);
-      E::unpack8(ldg16(cs), c);
-      E::unpack8(ldg16(sn), sv);
+      E::unpack8(r.c, c);
+      E::unpack8(r.s, sv);
       const bool lo = d < D / 2;  // rotate_half: -x[d + D/2] on the first half, x[d - D/2] on the second
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = rope_elem<T>(a[i], c[i], lo ? -b[i] : b[i], sv[i]);
@@ -682,11 +705,15 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     Piece pc;
     bool have = walk.next(tp, pc);
     if (have && is_k) ok = q_issue(pc, qi++);
+    // The new row of the current piece's segment (when it holds the segment's
+    // last tile and the append is fused), loaded one piece ahead.
+    NewRow row_cur = append_fetch<T, H, D, D2>(tp, pc, nch, is_k, lane);
     while (ok && have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
       // The next piece's Q, landing while this piece's tiles stream.
       if (is_k && have_nx && !q_issue(nx, qi++)) break;
+      const NewRow row_nxt = have_nx ? append_fetch<T, H, D, D2>(tp, nx, nch, is_k, lane) : row_cur;
       const int lb0 = pc.t0 / p.block_size;
       const int need = (pc.t1 + p.block_size - 1) / p.block_size;
       const int x0 = pc.hg / nch * 128 * D2;  // this tile row's first element
@@ -706,7 +733,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           // The segment's last tile holds position len - 1: write the new row
           // there first (block b of this tile's window entries).
           const int b = (pc.len - 1) / p.block_size - (lb0 + j * bpt);
-          append_row<T, H, D, D2>(tp, pc, pc.hg / nch, is_k, win[slot * 32 + wofs + b], lane);
+          append_store<T, H, D, D2>(tp, pc, pc.hg / nch, is_k, win[slot * 32 + wofs + b], lane, row_cur);
         }
         for (int sub = 0; sub < D2; ++sub) {  // one ring stage per 128-element sub-row
           if (!PKV_TW(1, mbar_wait(is_k ? kempty(stage) : vempty(stage), sphase ^ 1u, abort_flag, kTimeoutNs))) {
@@ -743,6 +770,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       }
       pc = nx;
       have = have_nx;
+      row_cur = row_nxt;
     }
     cp_async_wait<0>();  // no copy into shared memory outlives this role
     // Drain: the last min(issued, ring size) tiles' loads must have landed
