@@ -42,12 +42,15 @@
 //     lower-numbered blocks, so a combining CTA only ever waits on CTAs
 //     dispatched before it — no second launch, equal tiles per SM.
 //   * Warp roles (12 warps): 0 K-tile TMA producer (also copies each piece's
-//     Q), 6 V-tile TMA producer, 1 S-MMA issuer (TMEM owner), 11 O-MMA issuer,
-//     2-5 softmax, 7-10 correction / epilogue. Each tcgen05.mma costs its
-//     issuing thread tens of nanoseconds, so S and O are issued from two
-//     warps. K and V have separate smem rings: a K tile is freed once the S
-//     MMA has read it, so K prefetch runs deeper than V. Block-table entries
-//     and Q are copied ahead with cp.async, so no TMA issue waits on L2.
+//     Q; with RoPE, warp 7 stages the rotated Q instead), 6 V-tile TMA
+//     producer, 1 S-MMA issuer (TMEM owner), 11 O-MMA issuer, 2-5 softmax,
+//     7-10 correction / epilogue. With the fused decode append, the two MMA
+//     issuers patch the new K / V row into the landed tile (and the pool).
+//     Each tcgen05.mma costs its issuing thread tens of nanoseconds, so S and
+//     O are issued from two warps. K and V have separate smem rings: a K tile
+//     is freed once the S MMA has read it, so K prefetch runs deeper than V.
+//     Block-table entries and Q are copied ahead with cp.async, so no TMA
+//     issue waits on L2.
 //   * Every mbarrier wait is bounded (2 s): on timeout the kernel sets
 //     PAGEDKV_EFLAG_PIPE_TIMEOUT, unwinds every role, drains its own TMA loads
 //     and MMAs, frees TMEM and returns.
@@ -215,31 +218,36 @@ struct Walker {
   }
 };
 
-// The decode append of the tile row a segment reads, run by one producer warp
-// (K or V) for the segment's last tile: lane l owns elements [8l, 8l + 8) of
-// the 128 * D2-element slice of the new row (the H kv heads of tile row prow).
-// append_fetch issues the global loads of the new row (and of the cos / sin
-// chunks for K with RoPE) one piece ahead, so the data sits in registers when
-// the tile comes up; append_store rotates K when RoPE is on (the partner half
-// of each head is D / 16 lanes away), stores the slice into the pool row of
-// position len - 1 and fences the generic-proxy stores against the async
-// proxy, so the TMA load issued after the warp barrier reads the new row.
-// Several query-head chunks of one tile row write the same bytes; the writes
-// are identical, so their order does not matter.
+// The decode append fused into the launch. The new K / V row of a sequence
+// lands in the tile that holds position len - 1, the last tile of each of its
+// segments. The MMA issuer that consumes that tile (warp 1 for K, warp 11 for
+// V) patches the row into the shared-memory tile after its TMA load landed
+// and before the MMA reads it (a CTA-scope proxy fence, as for the stale rows
+// it zeroes), and stores it into the pool row for later steps (a plain global
+// store: no load in this launch reads the pool through it, every consumer of
+// the tile patches its own copy). Lane l owns elements [8l, 8l + 8) of the
+// 128 * D2-element slice of the row (the H kv heads of tile row prow).
+// append_fetch issues the global loads one piece ahead (the row, its block
+// id, and the cos / sin chunks for K with RoPE), so the data sits in
+// registers when the tile comes up. Query-head chunks of one tile row (wide
+// groups) are separate segments that store the same bytes, which is harmless.
 struct NewRow {
   uint4 x, c, s;  // row chunk; cos / sin chunks (K with RoPE)
+  int32_t blk;    // pool block of position len - 1
 };
 
 template <typename T, int H, int D, int D2>
 __device__ __forceinline__ NewRow append_fetch(const TcParams &tp, const Piece &pc, int nch, bool is_k, int lane) {
   NewRow r;
   r.x = r.c = r.s = make_uint4(0u, 0u, 0u, 0u);
+  r.blk = -1;
   if (tp.k_new == nullptr || pc.t1 != pc.len) return r;
   const DecodeParams &p = tp.p;
   const int prow = pc.hg / nch;
   const int e = lane * 8;                // element within the slice
   const int hl = e / D, d = e - hl * D;  // kv head within the tile row, dim
   const int kv = prow * H + hl;
+  r.blk = __ldg(p.bt + (int64_t)pc.seq * p.bt_s + (pc.len - 1) / p.block_size);
   if (lane < 16 * D2 && kv < p.hkv) {
     const T *src = static_cast<const T *>(is_k ? tp.k_new : tp.v_new);
     const int64_t st = is_k ? tp.kn_st : tp.vn_st, sh = is_k ? tp.kn_sh : tp.vn_sh;
@@ -252,43 +260,115 @@ __device__ __forceinline__ NewRow append_fetch(const TcParams &tp, const Piece &
   return r;
 }
 
-template <typename T, int H, int D, int D2>
-__device__ __forceinline__ void append_store(const TcParams &tp, const Piece &pc, int prow, bool is_k,
-                                             int32_t blk, int lane, const NewRow &r) {
+// The lane's chunk of the new row as stored: K rotated when RoPE is on (the
+// partner half of each head is D / 16 lanes away; every lane shuffles).
+template <typename T, int D>
+__device__ __forceinline__ uint4 append_chunk(const TcParams &tp, const NewRow &r, bool is_k, int lane) {
   using E = Elem<T>;
-  const DecodeParams &p = tp.p;
-  const int e = lane * 8;
-  const int hl = e / D, d = e - hl * D;
-  const int kv = prow * H + hl;
-  const bool active = lane < 16 * D2 && kv < p.hkv;
   uint4 x = r.x;
   if (is_k && tp.cos != nullptr) {
-    uint4 xp;  // the rotation partner chunk (all lanes shuffle)
+    uint4 xp;
     xp.x = __shfl_xor_sync(0xffffffffu, x.x, D / 16);
     xp.y = __shfl_xor_sync(0xffffffffu, x.y, D / 16);
     xp.z = __shfl_xor_sync(0xffffffffu, x.z, D / 16);
     xp.w = __shfl_xor_sync(0xffffffffu, x.w, D / 16);
-    if (active) {
-      float a[8], b[8], c[8], sv[8], o[8];
-      E::unpack8(x, a);
-      E::unpack8(xp, b);
-      E::unpack8(r.c, c);
-      E::unpack8(r.s, sv);
-      const bool lo = d < D / 2;  // rotate_half: -x[d + D/2] on the first half, x[d - D/2] on the second
+    const int d = (lane * 8) % D;
+    float a[8], b[8], c[8], sv[8], o[8];
+    E::unpack8(x, a);
+    E::unpack8(xp, b);
+    E::unpack8(r.c, c);
+    E::unpack8(r.s, sv);
+    const bool lo = d < D / 2;  // rotate_half: -x[d + D/2] on the first half, x[d - D/2] on the second
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = rope_elem<T>(a[i], c[i], lo ? -b[i] : b[i], sv[i]);
-      x = E::pack8(o);
+    for (int i = 0; i < 8; ++i) o[i] = rope_elem<T>(a[i], c[i], lo ? -b[i] : b[i], sv[i]);
+    x = E::pack8(o);
+  }
+  return x;
+}
+
+// Patch the lane's chunk into sub-row `sub` of the tile staged at `stage`
+// (SW128 halves of 128 token rows x 128 B) and, with sub 0, store the whole
+// slice into the pool. The caller fences the shared stores against the async
+// proxy before the MMA.
+template <typename T, int H, int D, int D2>
+__device__ __forceinline__ void append_patch(const TcParams &tp, const Piece &pc, int nch, uint32_t stage,
+                                             int tile_t0, int sub, bool is_k, const NewRow &r, uint4 x,
+                                             int lane) {
+  const DecodeParams &p = tp.p;
+  const int prow = pc.hg / nch;
+  const int e = lane * 8;
+  const int kv = prow * H + e / D;
+  if (lane >= 16 * D2 || kv >= p.hkv || r.blk < 0 || r.blk >= p.num_blocks) return;
+  const int pos = pc.len - 1;
+  const int es = e - sub * 128;
+  if (es >= 0 && es < 128) {
+    const int tr = pos - tile_t0;  // token row within the tile
+    const int c = (es & 63) >> 3;
+    const uint32_t addr = stage + (es >> 6) * kHalfBytes + tr * 128 + ((c ^ (tr & 7)) << 4);
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(x.x), "r"(x.y), "r"(x.z), "r"(x.w)
+                 : "memory");
+  }
+  if (sub == 0) {
+    T *pool = static_cast<T *>(const_cast<void *>(is_k ? p.k : p.v));
+    const int64_t row = (int64_t)r.blk * p.block_size + pos % p.block_size;
+    stg16(pool + row * ((int64_t)p.hkv * D) + (int64_t)prow * 128 * D2 + e, x);
+  }
+}
+
+// Q of piece q into the Q ring slot at qbuf as the block-diagonal B operand
+// [N rows x 128 * D2], K-major SW128; padding rows and halves are zero. Plain
+// copies go by cp.async; with RoPE each chunk is rotated (q * cos +
+// rotate_half(q) * sin, rounded as the append kernels round it) from plain
+// loads and stored with a shared store.
+template <typename T, int H, int GP, int N, int D, int D2>
+__device__ __forceinline__ void stage_q(const TcParams &tp, const Piece &q, int nch, uint32_t qbuf, bool rope,
+                                        int lane) {
+  using E = Elem<T>;
+  const DecodeParams &p = tp.p;
+  constexpr int kQChunks = 16 * N * D2 / 32;  // Q 16-byte chunks per lane
+  constexpr int kQSubBytes = 2 * N * 128;     // one 128-element sub-row operand
+#pragma unroll
+  for (int c = 0; c < kQChunks; ++c) {
+    const int idx = lane + c * 32;
+    const int sub = idx / (16 * N);  // 128-element sub-row of the head
+    const int ix = idx - sub * 16 * N;
+    const int xh = ix / (8 * N);
+    const int rem = ix - xh * 8 * N;
+    const int n = rem >> 3, ch = rem & 7;
+    const int hl = n / GP, g = n - hl * GP;
+    const int qrow = q.hg / nch;
+    const int kv = qrow * H + hl;
+    const int gq = (q.hg - qrow * nch) * GP + g;  // query head within the kv head's group
+    // Element e of the 128-wide row belongs to kv head e / D of the group:
+    // query column n (head hl) is nonzero only on its own head's D elements.
+    const int e = sub * 128 + xh * 64 + ch * 8;
+    const bool in = hl < H && gq < p.group && kv < p.hkv && e / D == hl;
+    const int d = e - hl * D;
+    const T *src = reinterpret_cast<const T *>(p.q) +
+                   (in ? (int64_t)q.seq * p.q_ss + (int64_t)(kv * p.group + gq) * p.q_sh + d : 0);
+    const uint32_t addr =
+        qbuf + sub * kQSubBytes + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
+    if (!rope) {
+      cp_async_16(addr, src, in ? 16u : 0u);
+    } else {
+      uint4 r = make_uint4(0u, 0u, 0u, 0u);
+      if (in) {
+        const bool lo = d < D / 2;
+        const T *cs = static_cast<const T *>(tp.cos) + (int64_t)q.seq * tp.cs_st + d;
+        const T *sn = static_cast<const T *>(tp.sin) + (int64_t)q.seq * tp.cs_st + d;
+        float a[8], b[8], cv[8], sv[8], o[8];
+        E::unpack8(ldg16(src), a);
+        E::unpack8(ldg16(src + (lo ? D / 2 : -(D / 2))), b);
+        E::unpack8(ldg16(cs), cv);
+        E::unpack8(ldg16(sn), sv);
+#pragma unroll
+        for (int k2 = 0; k2 < 8; ++k2) o[k2] = rope_elem<T>(a[k2], cv[k2], lo ? -b[k2] : b[k2], sv[k2]);
+        r = E::pack8(o);
+      }
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(r.x), "r"(r.y), "r"(r.z), "r"(r.w)
+                   : "memory");
     }
   }
-  if (active && blk >= 0 && blk < p.num_blocks) {
-    const int pos = pc.len - 1;
-    T *pool = static_cast<T *>(const_cast<void *>(is_k ? p.k : p.v));
-    const int64_t row = (int64_t)blk * p.block_size + pos % p.block_size;
-    stg16(pool + row * ((int64_t)p.hkv * D) + (int64_t)prow * 128 * D2 + e, x);
-    fence_proxy_async_global();
-  }
-  __syncwarp();
-  fence_proxy_async_global();
 }
 
 // Running (sum, denominator, reference max) of one correction thread's
@@ -645,75 +725,27 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 
     // Q of piece q into ring slot i as the block-diagonal B operand
     // [N rows x 128], K-major SW128; padding rows and halves are zero-filled.
+    // Q of each piece goes into a Q ring slot one piece ahead by cp.async,
+    // completing on the slot's q_full barrier. With RoPE the rotated Q is
+    // staged by correction warp 7 instead (plain loads would stall the TMA
+    // issue here).
+    const bool q_here = tp.cos == nullptr;
     auto q_issue = [&](const Piece &q, uint32_t i) -> bool {
+      if (!q_here) return true;
       if (!PKV_TW(0, mbar_wait(q_empty(i), ring_parity(i, kQSlots) ^ 1u, abort_flag, kTimeoutNs))) return false;
-      const uint32_t qbuf = sbase + L::kOffQ + (i % kQSlots) * L::kQBytes;
-      const bool rope = tp.cos != nullptr;
-#pragma unroll
-      for (int c = 0; c < kQChunks; ++c) {
-        const int idx = lane + c * 32;
-        const int sub = idx / (16 * N);  // 128-element sub-row of the head
-        const int ix = idx - sub * 16 * N;
-        const int xh = ix / (8 * N);
-        const int rem = ix - xh * 8 * N;
-        const int n = rem >> 3, ch = rem & 7;
-        const int hl = n / GP, g = n - hl * GP;
-        const int qrow = q.hg / nch;
-        const int kv = qrow * H + hl;
-        const int gq = (q.hg - qrow * nch) * GP + g;  // query head within the kv head's group
-        // Element e of the 128-wide row belongs to kv head e / D of the group:
-        // query column n (head hl) is nonzero only on its own head's D elements.
-        const int e = sub * 128 + xh * 64 + ch * 8;
-        const bool in = hl < H && gq < p.group && kv < p.hkv && e / D == hl;
-        const int d = e - hl * D;
-        const T *src = reinterpret_cast<const T *>(p.q) +
-                       (in ? (int64_t)q.seq * p.q_ss + (int64_t)(kv * p.group + gq) * p.q_sh + d : 0);
-        const uint32_t addr =
-            qbuf + sub * L::kQSubBytes + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
-        if (!rope) {
-          cp_async_16(addr, src, in ? 16u : 0u);
-        } else {
-          // rope(q) = q * cos + rotate_half(q) * sin, rounded as the append
-          // kernels round it, staged with plain shared stores
-          uint4 r = make_uint4(0u, 0u, 0u, 0u);
-          if (in) {
-            const bool lo = d < D / 2;
-            const T *cs = static_cast<const T *>(tp.cos) + (int64_t)q.seq * tp.cs_st + d;
-            const T *sn = static_cast<const T *>(tp.sin) + (int64_t)q.seq * tp.cs_st + d;
-            float a[8], b[8], cv[8], sv[8], o[8];
-            E::unpack8(ldg16(src), a);
-            E::unpack8(ldg16(src + (lo ? D / 2 : -(D / 2))), b);
-            E::unpack8(ldg16(cs), cv);
-            E::unpack8(ldg16(sn), sv);
-#pragma unroll
-            for (int k2 = 0; k2 < 8; ++k2) o[k2] = rope_elem<T>(a[k2], cv[k2], lo ? -b[k2] : b[k2], sv[k2]);
-            r = E::pack8(o);
-          }
-          asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(r.x), "r"(r.y), "r"(r.z),
-                       "r"(r.w)
-                       : "memory");
-        }
-      }
-      if (!rope) {
-        cp_async_mbar_arrive(q_full(i));
-      } else {
-        mbar_arrive(q_full(i));  // releases this lane's shared stores to the S issuer
-      }
+      stage_q<T, H, GP, N, D, D2>(tp, q, nch, sbase + L::kOffQ + (i % kQSlots) * L::kQBytes, false, lane);
+      cp_async_mbar_arrive(q_full(i));
       return true;
     };
 
     Piece pc;
     bool have = walk.next(tp, pc);
     if (have && is_k) ok = q_issue(pc, qi++);
-    // The new row of the current piece's segment (when it holds the segment's
-    // last tile and the append is fused), loaded one piece ahead.
-    NewRow row_cur = append_fetch<T, H, D, D2>(tp, pc, nch, is_k, lane);
     while (ok && have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
       // The next piece's Q, landing while this piece's tiles stream.
       if (is_k && have_nx && !q_issue(nx, qi++)) break;
-      const NewRow row_nxt = have_nx ? append_fetch<T, H, D, D2>(tp, nx, nch, is_k, lane) : row_cur;
       const int lb0 = pc.t0 / p.block_size;
       const int need = (pc.t1 + p.block_size - 1) / p.block_size;
       const int x0 = pc.hg / nch * 128 * D2;  // this tile row's first element
@@ -729,12 +761,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         }
         const uint32_t slot = wk % 3u;
         if (wofs + bpt >= 32 || j + 1 == pc.ntiles) ++wk;  // last tile of this window
-        if (tp.k_new != nullptr && pc.t1 == pc.len && j + 1 == pc.ntiles) {
-          // The segment's last tile holds position len - 1: write the new row
-          // there first (block b of this tile's window entries).
-          const int b = (pc.len - 1) / p.block_size - (lb0 + j * bpt);
-          append_store<T, H, D, D2>(tp, pc, pc.hg / nch, is_k, win[slot * 32 + wofs + b], lane, row_cur);
-        }
         for (int sub = 0; sub < D2; ++sub) {  // one ring stage per 128-element sub-row
           if (!PKV_TW(1, mbar_wait(is_k ? kempty(stage) : vempty(stage), sphase ^ 1u, abort_flag, kTimeoutNs))) {
             ok = false;
@@ -770,7 +796,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       }
       pc = nx;
       have = have_nx;
-      row_cur = row_nxt;
     }
     cp_async_wait<0>();  // no copy into shared memory outlives this role
     // Drain: the last min(issued, ring size) tiles' loads must have landed
@@ -793,19 +818,32 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     bool ok = true;
     Piece pc;
     bool have = walk.next(tp, pc);
+    // The new K row of the current piece's segment (fused append), loaded
+    // one piece ahead.
+    NewRow row_cur = append_fetch<T, H, D, D2>(tp, pc, nch, true, lane);
     while (ok && have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
+      const NewRow row_nxt = have_nx ? append_fetch<T, H, D, D2>(tp, nx, nch, true, lane) : row_cur;
       if (!PKV_TW(0, mbar_wait(q_full(qi), ring_parity(qi, kQSlots), abort_flag, kTimeoutNs))) break;
       fence_proxy_async_smem();  // Q landed through cp.async (generic proxy); the MMA reads it
       const uint32_t qbuf = sbase + L::kOffQ + (qi % kQSlots) * L::kQBytes;
       for (int j = 0; j < pc.ntiles; ++j) {
         const uint32_t b = gt & 1u;
+        const bool patch = tp.k_new != nullptr && pc.t1 == pc.len && j + 1 == pc.ntiles;
+        const uint4 xk = patch ? append_chunk<T, D>(tp, row_cur, true, lane) : row_cur.x;
         for (int sub = 0; sub < D2; ++sub) {  // S sums the sub-rows' products
           if (!PKV_TW(1, mbar_wait(kfull(kst), kph, abort_flag, kTimeoutNs))) { ok = false; break; }
           if (sub == 0 && !PKV_TW(2, mbar_wait(bar2(1, b), ((gt >> 1) & 1u) ^ 1u, abort_flag, kTimeoutNs))) {
             ok = false;
             break;
+          }
+          if (patch) {
+            // the new K row of position len - 1, into the landed tile and the pool
+            append_patch<T, H, D, D2>(tp, pc, nch, sbase + L::kOffK + kst * kOperandBytes, pc.t0 + j * kTile, sub,
+                                      true, row_cur, xk, lane);
+            fence_proxy_async_smem();
+            __syncwarp();
           }
           tc_fence_after();
           if (lane == 0) {
@@ -833,6 +871,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       ++qi;
       pc = nx;
       have = have_nx;
+      row_cur = row_nxt;
     }
     // Every MMA this thread issued has completed before TMEM is released.
     if (lane == 0) mma_commit(mma_done);
@@ -848,18 +887,32 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     bool ok = true;
     Piece pc;
     bool have = walk.next(tp, pc);
+    // The new V row of the current piece's segment (fused append), loaded
+    // one piece ahead.
+    NewRow row_cur = append_fetch<T, H, D, D2>(tp, pc, nch, false, lane);
     while (ok && have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
+      const NewRow row_nxt = have_nx ? append_fetch<T, H, D, D2>(tp, nx, nch, false, lane) : row_cur;
       for (int j = 0; j < pc.ntiles; ++j) {
         const uint32_t b = gt & 1u;
         const uint32_t bph = (gt >> 1) & 1u;
+        const bool patch = tp.k_new != nullptr && pc.t1 == pc.len && j + 1 == pc.ntiles;
         for (int sub = 0; sub < D2; ++sub) {  // one O accumulator per sub-row
           if (!PKV_TW(3, mbar_wait(vfull(vst), vph, abort_flag, kTimeoutNs))) { ok = false; break; }
           const uint32_t va = sbase + L::kOffV + vst * kOperandBytes;
+          const int tile_t0 = pc.t0 + j * kTile;
+          if (patch) {
+            // the new V row of position len - 1, into the landed tile and the
+            // pool (fenced with the stale-row zeroing below)
+            append_patch<T, H, D, D2>(tp, pc, nch, va, tile_t0, sub, false, row_cur, row_cur.x, lane);
+            if (pc.len % p.block_size == 0) {
+              fence_proxy_async_smem();
+              __syncwarp();
+            }
+          }
           // Rows of the last block past the sequence end hold stale pool data:
           // zero them so 0 * (non-finite stale value) never reaches the sum.
-          const int tile_t0 = pc.t0 + j * kTile;
           if (pc.t1 == pc.len && tile_t0 + kTile >= pc.len && (pc.len % p.block_size) != 0) {
             const int r0 = pc.len - tile_t0;  // first stale row in the tile
             const int r1 = ((pc.len + p.block_size - 1) / p.block_size) * p.block_size - tile_t0;
@@ -903,6 +956,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       }
       pc = nx;
       have = have_nx;
+      row_cur = row_nxt;
     }
     if (lane == 0) mma_commit(mma_done);
     __syncwarp();
@@ -1071,6 +1125,21 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     const int HQS = H * GP;  // partial slots per CTA (query columns of a segment)
     uint32_t gt = 0, pi = 0;
 
+    // With RoPE, warp 7 stages each piece's rotated Q into its ring slot one
+    // piece ahead (its own plain loads; the TMA producer keeps streaming).
+    const bool q_stager = tp.cos != nullptr && warp == 7;
+    uint32_t qs_i = 0;
+    auto stage_rope_q = [&](const Piece &q) {
+      if (mbar_wait(q_empty(qs_i), ring_parity(qs_i, kQSlots) ^ 1u, abort_flag, kTimeoutNs)) {
+        stage_q<T, H, GP, N, D, D2>(tp, q, nch, sbase + L::kOffQ + (qs_i % kQSlots) * L::kQBytes, true, lane);
+        mbar_arrive(q_full(qs_i));  // releases this lane's shared stores to the S issuer
+      }
+      ++qs_i;
+    };
+    Piece pc;
+    bool have = walk.next(tp, pc);
+    if (q_stager && have) stage_rope_q(pc);
+
     // Sequences of length 0 own no tiles: CTA (seq % grid) writes their zeros.
     for (int s = blockIdx.x; s < p.num_seqs; s += gridDim.x) {
       const int raw = p.lens ? __ldg(p.lens + s) : p.uniform_len;
@@ -1082,11 +1151,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       }
     }
 
-    Piece pc;
-    bool have = walk.next(tp, pc);
     while (have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
+      if (q_stager && have_nx) stage_rope_q(nx);
       float acc[D2][GP], msel[GP];  // acc[sub]: dims sub * 128 + dim
 #pragma unroll
       for (int g = 0; g < GP; ++g) {
