@@ -316,10 +316,15 @@ __device__ __forceinline__ void append_patch(const TcParams &tp, const Piece &pc
 }
 
 // Q of piece q into the Q ring slot at qbuf as the block-diagonal B operand
-// [N rows x 128 * D2], K-major SW128; padding rows and halves are zero. Plain
-// copies go by cp.async; with RoPE each chunk is rotated (q * cos +
-// rotate_half(q) * sin, rounded as the append kernels round it) from plain
-// loads and stored with a shared store.
+// [N rows x 128 * D2], K-major SW128; padding rows and halves are zero. Lane
+// `lane` owns chunks idx = lane + 32 c (16 bytes each); its chunk column
+// within 8 is lane & 7. Plain copies go by cp.async. With RoPE (q * cos +
+// rotate_half(q) * sin, rounded as the append kernels round it) every load is
+// issued first: the lane's q chunks, and cos / sin once per distinct head
+// dimension (one for head_dim <= 64, 2 * D2 above); a chunk's rotation
+// partner, D / 2 elements away in the same head, is then a shuffle of the
+// same chunk (lane ^ D / 16, head_dim <= 64) or another of the lane's own
+// chunks (c ^ N / 4 at head_dim 128, c ^ N / 2 at 256).
 template <typename T, int H, int GP, int N, int D, int D2>
 __device__ __forceinline__ void stage_q(const TcParams &tp, const Piece &q, int nch, uint32_t qbuf, bool rope,
                                         int lane) {
@@ -327,8 +332,9 @@ __device__ __forceinline__ void stage_q(const TcParams &tp, const Piece &q, int 
   const DecodeParams &p = tp.p;
   constexpr int kQChunks = 16 * N * D2 / 32;  // Q 16-byte chunks per lane
   constexpr int kQSubBytes = 2 * N * 128;     // one 128-element sub-row operand
-#pragma unroll
-  for (int c = 0; c < kQChunks; ++c) {
+  constexpr int kDV = D >= 128 ? 2 * D2 : 1;  // distinct head dimensions of a lane's chunks
+  const int qrow = q.hg / nch;
+  auto chunk = [&](int c, bool &in, int &d, uint32_t &addr, const T *&src) {
     const int idx = lane + c * 32;
     const int sub = idx / (16 * N);  // 128-element sub-row of the head
     const int ix = idx - sub * 16 * N;
@@ -336,36 +342,84 @@ __device__ __forceinline__ void stage_q(const TcParams &tp, const Piece &q, int 
     const int rem = ix - xh * 8 * N;
     const int n = rem >> 3, ch = rem & 7;
     const int hl = n / GP, g = n - hl * GP;
-    const int qrow = q.hg / nch;
     const int kv = qrow * H + hl;
     const int gq = (q.hg - qrow * nch) * GP + g;  // query head within the kv head's group
     // Element e of the 128-wide row belongs to kv head e / D of the group:
     // query column n (head hl) is nonzero only on its own head's D elements.
     const int e = sub * 128 + xh * 64 + ch * 8;
-    const bool in = hl < H && gq < p.group && kv < p.hkv && e / D == hl;
-    const int d = e - hl * D;
-    const T *src = reinterpret_cast<const T *>(p.q) +
-                   (in ? (int64_t)q.seq * p.q_ss + (int64_t)(kv * p.group + gq) * p.q_sh + d : 0);
-    const uint32_t addr =
-        qbuf + sub * kQSubBytes + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
-    if (!rope) {
+    in = hl < H && gq < p.group && kv < p.hkv && e / D == hl;
+    d = e - hl * D;
+    src = reinterpret_cast<const T *>(p.q) + (in ? (int64_t)q.seq * p.q_ss + (int64_t)(kv * p.group + gq) * p.q_sh + d : 0);
+    addr = qbuf + sub * kQSubBytes + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
+  };
+  if (!rope) {
+#pragma unroll
+    for (int c = 0; c < kQChunks; ++c) {
+      bool in;
+      int d;
+      uint32_t addr;
+      const T *src;
+      chunk(c, in, d, addr, src);
       cp_async_16(addr, src, in ? 16u : 0u);
-    } else {
+    }
+    return;
+  }
+  // cos / sin chunks of the lane's distinct dimensions, then the chunks in
+  // groups of four closed under the rotation partner: four consecutive chunks
+  // at head_dim <= 64 (partner: a shuffle of the same chunk), chunks
+  // {b, b + 1, b + kp, b + 1 + kp} above (partner: entry i ^ 2 of the group)
+  uint4 cs[kDV], sn[kDV];
+#pragma unroll
+  for (int v = 0; v < kDV; ++v) {
+    // dimension of the lane's chunks with (sub, half) = (v / 2, v % 2)
+    const int d = (kDV == 1 ? (lane & 7) * 8 : (v >> 1) * 128 + (v & 1) * 64 + (lane & 7) * 8) % D;
+    cs[v] = ldg16(static_cast<const T *>(tp.cos) + (int64_t)q.seq * tp.cs_st + d);
+    sn[v] = ldg16(static_cast<const T *>(tp.sin) + (int64_t)q.seq * tp.cs_st + d);
+  }
+  static_assert(kQChunks % 4 == 0, "rotation groups of four chunks");
+  constexpr int kp = kQChunks / 2;  // partner distance in chunks at head_dim >= 128
+#pragma unroll
+  for (int grp = 0; grp < kQChunks / 4; ++grp) {
+    int cl[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) cl[i] = D <= 64 ? grp * 4 + i : grp * 2 + (i & 1) + (i >> 1) * kp;
+    uint4 xs[4];
+    bool in[4];
+    int dd[4];
+    uint32_t addr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const T *src;
+      chunk(cl[i], in[i], dd[i], addr[i], src);
+      xs[i] = in[i] ? ldg16(src) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 xp;
+      if constexpr (D <= 64) {
+        xp.x = __shfl_xor_sync(0xffffffffu, xs[i].x, D / 16);
+        xp.y = __shfl_xor_sync(0xffffffffu, xs[i].y, D / 16);
+        xp.z = __shfl_xor_sync(0xffffffffu, xs[i].z, D / 16);
+        xp.w = __shfl_xor_sync(0xffffffffu, xs[i].w, D / 16);
+      } else {
+        xp = xs[i ^ 2];
+      }
       uint4 r = make_uint4(0u, 0u, 0u, 0u);
-      if (in) {
-        const bool lo = d < D / 2;
-        const T *cs = static_cast<const T *>(tp.cos) + (int64_t)q.seq * tp.cs_st + d;
-        const T *sn = static_cast<const T *>(tp.sin) + (int64_t)q.seq * tp.cs_st + d;
+      if (in[i]) {
+        const int idx = lane + cl[i] * 32;
+        const int v = kDV == 1 ? 0 : (idx / (16 * N)) * 2 + (idx % (16 * N)) / (8 * N);
+        const bool lo = dd[i] < D / 2;
         float a[8], b[8], cv[8], sv[8], o[8];
-        E::unpack8(ldg16(src), a);
-        E::unpack8(ldg16(src + (lo ? D / 2 : -(D / 2))), b);
-        E::unpack8(ldg16(cs), cv);
-        E::unpack8(ldg16(sn), sv);
+        E::unpack8(xs[i], a);
+        E::unpack8(xp, b);
+        E::unpack8(cs[v], cv);
+        E::unpack8(sn[v], sv);
 #pragma unroll
         for (int k2 = 0; k2 < 8; ++k2) o[k2] = rope_elem<T>(a[k2], cv[k2], lo ? -b[k2] : b[k2], sv[k2]);
         r = E::pack8(o);
       }
-      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(r.x), "r"(r.y), "r"(r.z), "r"(r.w)
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr[i]), "r"(r.x), "r"(r.y), "r"(r.z),
+                   "r"(r.w)
                    : "memory");
     }
   }
@@ -575,9 +629,16 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     tmem_relinquish();
   }
 
-  // Everything above touched only shared memory and TMEM, so it overlaps the
-  // tail of the preceding kernel; global inputs are read only after it ends.
-  grid_dependency_wait();
+  // Programmatic dependent launch. The next kernel may start as SMs free up.
+  // This CTA's set-up, the prologue scan of the sequence lengths and the
+  // first block-table windows overlap the tail of the preceding kernel: the
+  // lengths and block tables are read before waiting for it (the contract of
+  // include/pagedkv.h: the kernel launched right before this one on the
+  // stream must not write them after signalling its dependents, which no
+  // pagedkv kernel does and a kernel that does not signal early cannot do).
+  // Every other global access (q, the new rows, cos / sin, the pool, the
+  // outputs and the workspace) waits: each role calls grid_dependency_wait()
+  // before its first one.
   grid_launch_dependents();
 
   // ---- prologue: total cost units and the start of this CTA's range ----------
@@ -722,6 +783,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     issue_window();
     issue_window();
     uint32_t wk = 0;  // windows consumed
+    grid_dependency_wait();  // q and the pool may be written by the preceding kernel
 
     // Q of piece q into ring slot i as the block-diagonal B operand
     // [N rows x 128], K-major SW128; padding rows and halves are zero-filled.
@@ -816,6 +878,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     int kst = 0;
     uint32_t kph = 0, gt = 0, qi = 0;
     bool ok = true;
+    grid_dependency_wait();  // the new K rows, cos / sin and the pool
     Piece pc;
     bool have = walk.next(tp, pc);
     // The new K row of the current piece's segment (fused append), loaded
@@ -885,6 +948,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     int vst = 0;
     uint32_t vph = 0, gt = 0;
     bool ok = true;
+    grid_dependency_wait();  // the new V rows and the pool
     Piece pc;
     bool have = walk.next(tp, pc);
     // The new V row of the current piece's segment (fused append), loaded
@@ -1124,6 +1188,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     const uint32_t tl = tmem + ((uint32_t)(q4 * 32) << 16);
     const int HQS = H * GP;  // partial slots per CTA (query columns of a segment)
     uint32_t gt = 0, pi = 0;
+    grid_dependency_wait();  // q (RoPE staging), the outputs and the workspace
 
     // With RoPE, warp 7 stages each piece's rotated Q into its ring slot one
     // piece ahead (its own plain loads; the TMA producer keeps streaming).
