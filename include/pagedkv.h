@@ -135,19 +135,6 @@ int pagedkv_decode_attention_append(
     float scale, int32_t dtype, void *workspace, size_t workspace_bytes,
     void *stream);
 
-/*
- * Stream ordering of the two decode-attention entries above: the tensor-core
- * kernel is launched as a programmatic dependent of the kernel before it on
- * `stream`, and it reads seq_lens and block_tables while that kernel may
- * still be finishing (q, the new rows, cos / sin, the pool, the outputs and
- * the workspace are touched only after it completed). So seq_lens and
- * block_tables must not be written by the kernel launched immediately before
- * on the stream AFTER it signals its dependents early
- * (griddepcontrol.launch_dependents). Copies, kernels that do not signal
- * early (which become visible at their completion) and every pagedkv kernel
- * (none writes them) satisfy this.
- */
-
 /* Bytes of workspace pagedkv_decode_attention needs for this shape on the
  * current device (0 when the launch needs none). */
 size_t pagedkv_decode_attention_workspace_size(

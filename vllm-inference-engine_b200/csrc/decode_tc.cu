@@ -443,12 +443,19 @@ struct PieceAcc {
 // even when other work holds part of the GPU and not every CTA of the grid
 // is resident at once.
 template <typename T, int GP, int D, int D2>
-__device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP, D2> a, int64_t vb, int64_t b1, int hl,
-                                            int dim, int gn, bool have_kv, T *out, volatile int *abort_flag,
-                                            int row) {
+__device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP, D2> a, int64_t vb, int64_t b1,
+                                               int64_t G, int hl, int dim, int gn, bool have_kv, T *out,
+                                               volatile int *abort_flag, int row) {
   using E = Elem<T>;
   const DecodeParams &p = tp.p;
   const int HQS = (128 * D2 / D) * GP;  // partial slots per CTA
+  // The partners lie inside the effective grid by construction (every role
+  // derives its pieces from the same lengths); a range past it would index
+  // flags and partials the workspace does not hold, so it is refused.
+  if (b1 >= G) {
+    if (row == 0) set_error(p.err, PAGEDKV_EFLAG_SEQ_LEN_RANGE);
+    b1 = G - 1;
+  }
   if (row == 0) {
     for (int64_t bb = vb + 1; bb <= b1; ++bb) {
       const uint64_t t0 = globaltimer_ns();
@@ -629,16 +636,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     tmem_relinquish();
   }
 
-  // Programmatic dependent launch. The next kernel may start as SMs free up.
-  // This CTA's set-up, the prologue scan of the sequence lengths and the
-  // first block-table windows overlap the tail of the preceding kernel: the
-  // lengths and block tables are read before waiting for it (the contract of
-  // include/pagedkv.h: the kernel launched right before this one on the
-  // stream must not write them after signalling its dependents, which no
-  // pagedkv kernel does and a kernel that does not signal early cannot do).
-  // Every other global access (q, the new rows, cos / sin, the pool, the
-  // outputs and the workspace) waits: each role calls grid_dependency_wait()
-  // before its first one.
+  // Everything above touched only shared memory and TMEM, so it overlaps the
+  // tail of the preceding kernel; global inputs are read only after it ends.
+  grid_dependency_wait();
   grid_launch_dependents();
 
   // ---- prologue: total cost units and the start of this CTA's range ----------
@@ -783,7 +783,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     issue_window();
     issue_window();
     uint32_t wk = 0;  // windows consumed
-    grid_dependency_wait();  // q and the pool may be written by the preceding kernel
 
     // Q of piece q into ring slot i as the block-diagonal B operand
     // [N rows x 128], K-major SW128; padding rows and halves are zero-filled.
@@ -878,7 +877,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     int kst = 0;
     uint32_t kph = 0, gt = 0, qi = 0;
     bool ok = true;
-    grid_dependency_wait();  // the new K rows, cos / sin and the pool
     Piece pc;
     bool have = walk.next(tp, pc);
     // The new K row of the current piece's segment (fused append), loaded
@@ -948,7 +946,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     int vst = 0;
     uint32_t vph = 0, gt = 0;
     bool ok = true;
-    grid_dependency_wait();  // the new V rows and the pool
     Piece pc;
     bool have = walk.next(tp, pc);
     // The new V row of the current piece's segment (fused append), loaded
@@ -1188,7 +1185,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     const uint32_t tl = tmem + ((uint32_t)(q4 * 32) << 16);
     const int HQS = H * GP;  // partial slots per CTA (query columns of a segment)
     uint32_t gt = 0, pi = 0;
-    grid_dependency_wait();  // q (RoPE staging), the outputs and the workspace
 
     // With RoPE, warp 7 stages each piece's rotated Q into its ring slot one
     // piece ahead (its own plain loads; the TMA producer keeps streaming).
@@ -1327,8 +1323,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           pa.lsum[g] = lsum[g];
           pa.msel[g] = msel[g];
         }
-        combine_pieces<T, GP, D, D2>(tp, pa, vcta, owner_of(pc.seg_units + kSegUnits + (int64_t)pc.seg_tiles * kTileUnits - 1, U_total, G), hl, dim, gn,
-                                 have_kv, out, abort_flag, row);
+        const int64_t b1 = owner_of(pc.seg_units + kSegUnits + (int64_t)pc.seg_tiles * kTileUnits - 1, U_total, G);
+        combine_pieces<T, GP, D, D2>(tp, pa, vcta, b1, G, hl, dim, gn, have_kv, out, abort_flag, row);
       }
 #ifdef PAGEDKV_TRACE
       tw[4] += clock64() - t_epi0;
