@@ -376,25 +376,29 @@ __device__ __forceinline__ void stage_q(const TcParams &tp, const Piece &q, int 
     cs[v] = ldg16(static_cast<const T *>(tp.cos) + (int64_t)q.seq * tp.cs_st + d);
     sn[v] = ldg16(static_cast<const T *>(tp.sin) + (int64_t)q.seq * tp.cs_st + d);
   }
-  static_assert(kQChunks % 4 == 0, "rotation groups of four chunks");
+  // Groups of GS chunks, all loads of a group in flight at once: the whole
+  // operand when it is 8 chunks per lane (N = 16, one round trip), else four.
+  constexpr int GS = kQChunks <= 8 ? kQChunks : 4;
+  static_assert(kQChunks % GS == 0 && GS % 4 == 0, "rotation groups");
   constexpr int kp = kQChunks / 2;  // partner distance in chunks at head_dim >= 128
 #pragma unroll
-  for (int grp = 0; grp < kQChunks / 4; ++grp) {
-    int cl[4];
+  for (int grp = 0; grp < kQChunks / GS; ++grp) {
+    int cl[GS];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) cl[i] = D <= 64 ? grp * 4 + i : grp * 2 + (i & 1) + (i >> 1) * kp;
-    uint4 xs[4];
-    bool in[4];
-    int dd[4];
-    uint32_t addr[4];
+    for (int i = 0; i < GS; ++i)
+      cl[i] = D <= 64 ? grp * GS + i : grp * (GS / 2) + (i % (GS / 2)) + (i / (GS / 2)) * kp;
+    uint4 xs[GS];
+    bool in[GS];
+    int dd[GS];
+    uint32_t addr[GS];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < GS; ++i) {
       const T *src;
       chunk(cl[i], in[i], dd[i], addr[i], src);
       xs[i] = in[i] ? ldg16(src) : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < GS; ++i) {
       uint4 xp;
       if constexpr (D <= 64) {
         xp.x = __shfl_xor_sync(0xffffffffu, xs[i].x, D / 16);
@@ -402,7 +406,7 @@ __device__ __forceinline__ void stage_q(const TcParams &tp, const Piece &q, int 
         xp.z = __shfl_xor_sync(0xffffffffu, xs[i].z, D / 16);
         xp.w = __shfl_xor_sync(0xffffffffu, xs[i].w, D / 16);
       } else {
-        xp = xs[i ^ 2];
+        xp = xs[i ^ (GS / 2)];
       }
       uint4 r = make_uint4(0u, 0u, 0u, 0u);
       if (in[i]) {
