@@ -42,8 +42,8 @@
 //     lower-numbered blocks, so a combining CTA only ever waits on CTAs
 //     dispatched before it — no second launch, equal tiles per SM.
 //   * Warp roles (12 warps): 0 K-tile TMA producer (also copies each piece's
-//     Q; with RoPE, warp 7 stages the rotated Q instead), 6 V-tile TMA
-//     producer, 1 S-MMA issuer (TMEM owner), 11 O-MMA issuer, 2-5 softmax,
+//     Q), 6 V-tile TMA producer, 1 S-MMA issuer (TMEM owner; with RoPE it
+//     rotates each piece's landed Q in place), 11 O-MMA issuer, 2-5 softmax,
 //     7-10 correction / epilogue. With the fused decode append, the two MMA
 //     issuers patch the new K / V row into the landed tile (and the pool).
 //     Each tcgen05.mma costs its issuing thread tens of nanoseconds, so S and
@@ -315,70 +315,88 @@ __device__ __forceinline__ void append_patch(const TcParams &tp, const Piece &pc
   }
 }
 
-// Q of piece q into the Q ring slot at qbuf as the block-diagonal B operand
-// [N rows x 128 * D2], K-major SW128; padding rows and halves are zero. Lane
-// `lane` owns chunks idx = lane + 32 c (16 bytes each); its chunk column
-// within 8 is lane & 7. Plain copies go by cp.async. With RoPE (q * cos +
-// rotate_half(q) * sin, rounded as the append kernels round it) every load is
-// issued first: the lane's q chunks, and cos / sin once per distinct head
-// dimension (one for head_dim <= 64, 2 * D2 above); a chunk's rotation
-// partner, D / 2 elements away in the same head, is then a shuffle of the
-// same chunk (lane ^ D / 16, head_dim <= 64) or another of the lane's own
-// chunks (c ^ N / 4 at head_dim 128, c ^ N / 2 at 256).
-template <typename T, int H, int GP, int N, int D, int D2>
-__device__ __forceinline__ void stage_q(const TcParams &tp, const Piece &q, int nch, uint32_t qbuf, bool rope,
-                                        int lane) {
-  using E = Elem<T>;
-  const DecodeParams &p = tp.p;
-  constexpr int kQChunks = 16 * N * D2 / 32;  // Q 16-byte chunks per lane
-  constexpr int kQSubBytes = 2 * N * 128;     // one 128-element sub-row operand
-  constexpr int kDV = D >= 128 ? 2 * D2 : 1;  // distinct head dimensions of a lane's chunks
+// Chunk c of lane `lane` of the Q operand of piece q (the block-diagonal B
+// operand [N rows x 128 * D2], K-major SW128; padding rows and halves stay
+// zero): whether it holds query data, its head dimension d, its shared-memory
+// address in the slot at qbuf and its source in q. A lane owns chunks
+// idx = lane + 32 c (16 bytes each); its chunk column within 8 is lane & 7.
+template <typename T, int H, int GP, int N, int D>
+__device__ __forceinline__ void q_chunk(const DecodeParams &p, const Piece &q, int nch, uint32_t qbuf, int lane,
+                                        int c, bool &in, int &d, uint32_t &addr, const T *&src) {
+  constexpr int kQSubBytes = 2 * N * 128;  // one 128-element sub-row operand
   const int qrow = q.hg / nch;
-  auto chunk = [&](int c, bool &in, int &d, uint32_t &addr, const T *&src) {
-    const int idx = lane + c * 32;
-    const int sub = idx / (16 * N);  // 128-element sub-row of the head
-    const int ix = idx - sub * 16 * N;
-    const int xh = ix / (8 * N);
-    const int rem = ix - xh * 8 * N;
-    const int n = rem >> 3, ch = rem & 7;
-    const int hl = n / GP, g = n - hl * GP;
-    const int kv = qrow * H + hl;
-    const int gq = (q.hg - qrow * nch) * GP + g;  // query head within the kv head's group
-    // Element e of the 128-wide row belongs to kv head e / D of the group:
-    // query column n (head hl) is nonzero only on its own head's D elements.
-    const int e = sub * 128 + xh * 64 + ch * 8;
-    in = hl < H && gq < p.group && kv < p.hkv && e / D == hl;
-    d = e - hl * D;
-    src = reinterpret_cast<const T *>(p.q) + (in ? (int64_t)q.seq * p.q_ss + (int64_t)(kv * p.group + gq) * p.q_sh + d : 0);
-    addr = qbuf + sub * kQSubBytes + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
-  };
-  if (!rope) {
+  const int idx = lane + c * 32;
+  const int sub = idx / (16 * N);  // 128-element sub-row of the head
+  const int ix = idx - sub * 16 * N;
+  const int xh = ix / (8 * N);
+  const int rem = ix - xh * 8 * N;
+  const int n = rem >> 3, ch = rem & 7;
+  const int hl = n / GP, g = n - hl * GP;
+  const int kv = qrow * H + hl;
+  const int gq = (q.hg - qrow * nch) * GP + g;  // query head within the kv head's group
+  // Element e of the 128-wide row belongs to kv head e / D of the group:
+  // query column n (head hl) is nonzero only on its own head's D elements.
+  const int e = sub * 128 + xh * 64 + ch * 8;
+  in = hl < H && gq < p.group && kv < p.hkv && e / D == hl;
+  d = e - hl * D;
+  src = reinterpret_cast<const T *>(p.q) + (in ? (int64_t)q.seq * p.q_ss + (int64_t)(kv * p.group + gq) * p.q_sh + d : 0);
+  addr = qbuf + sub * kQSubBytes + xh * (N * 128) + (n >> 3) * 1024 + (n & 7) * 128 + ((ch ^ (n & 7)) << 4);
+}
+
+// Q of piece q into the Q ring slot at qbuf by cp.async (16-byte chunks;
+// padding chunks are zero-filled).
+template <typename T, int H, int GP, int N, int D, int D2>
+__device__ __forceinline__ void stage_q(const TcParams &tp, const Piece &q, int nch, uint32_t qbuf, int lane) {
+  constexpr int kQChunks = 16 * N * D2 / 32;  // Q 16-byte chunks per lane
 #pragma unroll
-    for (int c = 0; c < kQChunks; ++c) {
-      bool in;
-      int d;
-      uint32_t addr;
-      const T *src;
-      chunk(c, in, d, addr, src);
-      cp_async_16(addr, src, in ? 16u : 0u);
+  for (int c = 0; c < kQChunks; ++c) {
+    bool in;
+    int d;
+    uint32_t addr;
+    const T *src;
+    q_chunk<T, H, GP, N, D>(tp.p, q, nch, qbuf, lane, c, in, d, addr, src);
+    cp_async_16(addr, src, in ? 16u : 0u);
+  }
+}
+
+// RoPE of a piece's staged Q. A lane's chunks have kDV distinct head
+// dimensions (one for head_dim <= 64, (sub-row, half) pairs above); their
+// cos / sin chunks are loaded one piece ahead (q_rope_fetch) and the S issuer
+// rotates the landed operand in place before the piece's first MMA
+// (rotate_q): q * cos + rotate_half(q) * sin, rounded as the append kernels
+// round it. A chunk's rotation partner, D / 2 elements away in the same head,
+// is a shuffle of the same chunk (lane ^ D / 16, head_dim <= 64: every lane
+// reads its chunk before any lane writes) or another of the lane's own chunks
+// (c ^ N / 4 at head_dim 128, c ^ N / 2 at 256, read and written together).
+template <int D, int D2>
+struct QRope {
+  static constexpr int kDV = D >= 128 ? 2 * D2 : 1;
+  uint4 c[kDV], s[kDV];
+};
+
+template <typename T, int D, int D2>
+__device__ __forceinline__ QRope<D, D2> q_rope_fetch(const TcParams &tp, const Piece &q, int lane) {
+  QRope<D, D2> r;
+#pragma unroll
+  for (int v = 0; v < QRope<D, D2>::kDV; ++v) {
+    r.c[v] = r.s[v] = make_uint4(0u, 0u, 0u, 0u);
+    if (tp.cos != nullptr) {
+      // dimension of the lane's chunks with (sub-row, half) = (v / 2, v % 2)
+      const int d = (QRope<D, D2>::kDV == 1 ? (lane & 7) * 8 : (v >> 1) * 128 + (v & 1) * 64 + (lane & 7) * 8) % D;
+      r.c[v] = ldg16(static_cast<const T *>(tp.cos) + (int64_t)q.seq * tp.cs_st + d);
+      r.s[v] = ldg16(static_cast<const T *>(tp.sin) + (int64_t)q.seq * tp.cs_st + d);
     }
-    return;
   }
-  // cos / sin chunks of the lane's distinct dimensions, then the chunks in
-  // groups of four closed under the rotation partner: four consecutive chunks
-  // at head_dim <= 64 (partner: a shuffle of the same chunk), chunks
-  // {b, b + 1, b + kp, b + 1 + kp} above (partner: entry i ^ 2 of the group)
-  uint4 cs[kDV], sn[kDV];
-#pragma unroll
-  for (int v = 0; v < kDV; ++v) {
-    // dimension of the lane's chunks with (sub, half) = (v / 2, v % 2)
-    const int d = (kDV == 1 ? (lane & 7) * 8 : (v >> 1) * 128 + (v & 1) * 64 + (lane & 7) * 8) % D;
-    cs[v] = ldg16(static_cast<const T *>(tp.cos) + (int64_t)q.seq * tp.cs_st + d);
-    sn[v] = ldg16(static_cast<const T *>(tp.sin) + (int64_t)q.seq * tp.cs_st + d);
-  }
-  // Groups of GS chunks, all loads of a group in flight at once: the whole
-  // operand when it is 8 chunks per lane (N = 16, one round trip), else four.
-  constexpr int GS = kQChunks <= 8 ? kQChunks : 4;
+  return r;
+}
+
+template <typename T, int H, int GP, int N, int D, int D2>
+__device__ __forceinline__ void rotate_q(const TcParams &tp, const Piece &q, int nch, uint32_t qbuf,
+                                         const QRope<D, D2> &rp, int lane) {
+  using E = Elem<T>;
+  constexpr int kQChunks = 16 * N * D2 / 32;
+  constexpr int kDV = QRope<D, D2>::kDV;
+  constexpr int GS = kQChunks <= 8 ? kQChunks : 4;  // chunks in flight per group
   static_assert(kQChunks % GS == 0 && GS % 4 == 0, "rotation groups");
   constexpr int kp = kQChunks / 2;  // partner distance in chunks at head_dim >= 128
 #pragma unroll
@@ -394,8 +412,11 @@ __device__ __forceinline__ void stage_q(const TcParams &tp, const Piece &q, int 
 #pragma unroll
     for (int i = 0; i < GS; ++i) {
       const T *src;
-      chunk(cl[i], in[i], dd[i], addr[i], src);
-      xs[i] = in[i] ? ldg16(src) : make_uint4(0u, 0u, 0u, 0u);
+      q_chunk<T, H, GP, N, D>(tp.p, q, nch, qbuf, lane, cl[i], in[i], dd[i], addr[i], src);
+      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(xs[i].x), "=r"(xs[i].y), "=r"(xs[i].z), "=r"(xs[i].w)
+                   : "r"(addr[i])
+                   : "memory");
     }
 #pragma unroll
     for (int i = 0; i < GS; ++i) {
@@ -408,7 +429,6 @@ __device__ __forceinline__ void stage_q(const TcParams &tp, const Piece &q, int 
       } else {
         xp = xs[i ^ (GS / 2)];
       }
-      uint4 r = make_uint4(0u, 0u, 0u, 0u);
       if (in[i]) {
         const int idx = lane + cl[i] * 32;
         const int v = kDV == 1 ? 0 : (idx / (16 * N)) * 2 + (idx % (16 * N)) / (8 * N);
@@ -416,15 +436,15 @@ __device__ __forceinline__ void stage_q(const TcParams &tp, const Piece &q, int 
         float a[8], b[8], cv[8], sv[8], o[8];
         E::unpack8(xs[i], a);
         E::unpack8(xp, b);
-        E::unpack8(cs[v], cv);
-        E::unpack8(sn[v], sv);
+        E::unpack8(rp.c[v], cv);
+        E::unpack8(rp.s[v], sv);
 #pragma unroll
         for (int k2 = 0; k2 < 8; ++k2) o[k2] = rope_elem<T>(a[k2], cv[k2], lo ? -b[k2] : b[k2], sv[k2]);
-        r = E::pack8(o);
+        const uint4 r = E::pack8(o);
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr[i]), "r"(r.x), "r"(r.y), "r"(r.z),
+                     "r"(r.w)
+                     : "memory");
       }
-      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr[i]), "r"(r.x), "r"(r.y), "r"(r.z),
-                   "r"(r.w)
-                   : "memory");
     }
   }
 }
@@ -791,14 +811,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     // Q of piece q into ring slot i as the block-diagonal B operand
     // [N rows x 128], K-major SW128; padding rows and halves are zero-filled.
     // Q of each piece goes into a Q ring slot one piece ahead by cp.async,
-    // completing on the slot's q_full barrier. With RoPE the rotated Q is
-    // staged by correction warp 7 instead (plain loads would stall the TMA
-    // issue here).
-    const bool q_here = tp.cos == nullptr;
+    // completing on the slot's q_full barrier (with RoPE the S issuer rotates
+    // it in place when it lands).
     auto q_issue = [&](const Piece &q, uint32_t i) -> bool {
-      if (!q_here) return true;
       if (!PKV_TW(0, mbar_wait(q_empty(i), ring_parity(i, kQSlots) ^ 1u, abort_flag, kTimeoutNs))) return false;
-      stage_q<T, H, GP, N, D, D2>(tp, q, nch, sbase + L::kOffQ + (i % kQSlots) * L::kQBytes, false, lane);
+      stage_q<T, H, GP, N, D, D2>(tp, q, nch, sbase + L::kOffQ + (i % kQSlots) * L::kQBytes, lane);
       cp_async_mbar_arrive(q_full(i));
       return true;
     };
@@ -886,13 +903,20 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     // The new K row of the current piece's segment (fused append), loaded
     // one piece ahead.
     NewRow row_cur = append_fetch<T, H, D, D2>(tp, pc, nch, true, lane);
+    // cos / sin of the current piece's Q chunks (RoPE), loaded one piece ahead
+    QRope<D, D2> rope_cur = q_rope_fetch<T, D, D2>(tp, pc, lane);
     while (ok && have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
       const NewRow row_nxt = have_nx ? append_fetch<T, H, D, D2>(tp, nx, nch, true, lane) : row_cur;
+      const QRope<D, D2> rope_nxt = have_nx ? q_rope_fetch<T, D, D2>(tp, nx, lane) : rope_cur;
       if (!PKV_TW(0, mbar_wait(q_full(qi), ring_parity(qi, kQSlots), abort_flag, kTimeoutNs))) break;
-      fence_proxy_async_smem();  // Q landed through cp.async (generic proxy); the MMA reads it
       const uint32_t qbuf = sbase + L::kOffQ + (qi % kQSlots) * L::kQBytes;
+      if (tp.cos != nullptr) {
+        rotate_q<T, H, GP, N, D, D2>(tp, pc, nch, qbuf, rope_cur, lane);
+        __syncwarp();
+      }
+      fence_proxy_async_smem();  // Q landed through cp.async / was rotated (generic proxy); the MMA reads it
       for (int j = 0; j < pc.ntiles; ++j) {
         const uint32_t b = gt & 1u;
         const bool patch = tp.k_new != nullptr && pc.t1 == pc.len && j + 1 == pc.ntiles;
@@ -937,6 +961,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       pc = nx;
       have = have_nx;
       row_cur = row_nxt;
+      rope_cur = rope_nxt;
     }
     // Every MMA this thread issued has completed before TMEM is released.
     if (lane == 0) mma_commit(mma_done);
@@ -1190,20 +1215,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     const int HQS = H * GP;  // partial slots per CTA (query columns of a segment)
     uint32_t gt = 0, pi = 0;
 
-    // With RoPE, warp 7 stages each piece's rotated Q into its ring slot one
-    // piece ahead (its own plain loads; the TMA producer keeps streaming).
-    const bool q_stager = tp.cos != nullptr && warp == 7;
-    uint32_t qs_i = 0;
-    auto stage_rope_q = [&](const Piece &q) {
-      if (mbar_wait(q_empty(qs_i), ring_parity(qs_i, kQSlots) ^ 1u, abort_flag, kTimeoutNs)) {
-        stage_q<T, H, GP, N, D, D2>(tp, q, nch, sbase + L::kOffQ + (qs_i % kQSlots) * L::kQBytes, true, lane);
-        mbar_arrive(q_full(qs_i));  // releases this lane's shared stores to the S issuer
-      }
-      ++qs_i;
-    };
     Piece pc;
     bool have = walk.next(tp, pc);
-    if (q_stager && have) stage_rope_q(pc);
 
     // Sequences of length 0 own no tiles: CTA (seq % grid) writes their zeros.
     for (int s = blockIdx.x; s < p.num_seqs; s += gridDim.x) {
@@ -1219,7 +1232,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     while (have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
-      if (q_stager && have_nx) stage_rope_q(nx);
       float acc[D2][GP], msel[GP];  // acc[sub]: dims sub * 128 + dim
 #pragma unroll
       for (int g = 0; g < GP; ++g) {
