@@ -179,3 +179,16 @@ def test_cuda_core_shapes_and_unaligned_rows_run_as_two_launches(cuda_ready):
             case = dict(case, k_new=kn_odd)  # stays a device view: .to(dev) keeps it
         out_f, kf, vf, out_u, ku, vu, _, _ = _run(case, dev, rope)
         assert torch.equal(kf, ku) and torch.equal(vf, vu) and torch.equal(out_f, out_u)
+
+
+@pytest.mark.parametrize("rope", [False, True])
+@pytest.mark.parametrize("lens", [[0, 0, 0, 0], [1], [0, 5, 0], [3000]])
+def test_fused_append_batches_that_leave_ctas_without_work(cuda_ready, lens, rope):
+    """Batches whose tiles do not reach every CTA of the launch (all padding
+    rows, one token, a single long sequence): the idle CTAs must read nothing,
+    and the result is still the two separate launches'."""
+    c = _case(31 + len(lens) + sum(lens), 14, 2, 64, 16, lens)
+    out_f, kf, vf, out_u, ku, vu, _, _ = _run(c, cuda_ready, rope)
+    torch.cuda.synchronize()
+    assert torch.equal(kf, ku) and torch.equal(vf, vu) and torch.equal(out_f, out_u)
+    assert pagedkv.read_error_flags(cuda_ready) == 0

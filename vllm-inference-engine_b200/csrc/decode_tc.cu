@@ -156,12 +156,12 @@ __device__ __forceinline__ int64_t owner_of(int64_t u, int64_t U, int64_t G) {
 // hg is tile row hg / chunks (H kv heads at x offset row * 128 of the pool
 // row) and query-head chunk hg % chunks (GP query heads of each of them).
 struct Piece {
-  int seq, hg, len;
-  int t0, t1;         // token range [t0, t1)
-  int ntiles;         // tiles in this piece
-  int seg_tiles;      // tiles in the whole segment
-  int64_t seg_units;  // first cost unit of the segment
-  bool first;         // first piece of this CTA
+  int seq = 0, hg = 0, len = 0;
+  int t0 = 0, t1 = 0;     // token range [t0, t1)
+  int ntiles = 0;         // tiles in this piece
+  int seg_tiles = 0;      // tiles in the whole segment
+  int64_t seg_units = 0;  // first cost unit of the segment
+  bool first = false;     // first piece of this CTA
 };
 
 // Walks this CTA's tile range segment by segment. Every role runs its own copy
@@ -241,7 +241,7 @@ __device__ __forceinline__ NewRow append_fetch(const TcParams &tp, const Piece &
   NewRow r;
   r.x = r.c = r.s = make_uint4(0u, 0u, 0u, 0u);
   r.blk = -1;
-  if (tp.k_new == nullptr || pc.t1 != pc.len) return r;
+  if (tp.k_new == nullptr || pc.len <= 0 || pc.t1 != pc.len) return r;
   const DecodeParams &p = tp.p;
   const int prow = pc.hg / nch;
   const int e = lane * 8;                // element within the slice
@@ -380,7 +380,7 @@ __device__ __forceinline__ QRope<D, D2> q_rope_fetch(const TcParams &tp, const P
 #pragma unroll
   for (int v = 0; v < QRope<D, D2>::kDV; ++v) {
     r.c[v] = r.s[v] = make_uint4(0u, 0u, 0u, 0u);
-    if (tp.cos != nullptr) {
+    if (tp.cos != nullptr && q.len > 0) {
       // dimension of the lane's chunks with (sub-row, half) = (v / 2, v % 2)
       const int d = (QRope<D, D2>::kDV == 1 ? (lane & 7) * 8 : (v >> 1) * 128 + (v & 1) * 64 + (lane & 7) * 8) % D;
       r.c[v] = ldg16(static_cast<const T *>(tp.cos) + (int64_t)q.seq * tp.cs_st + d);
@@ -902,9 +902,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     bool have = walk.next(tp, pc);
     // The new K row of the current piece's segment (fused append), loaded
     // one piece ahead.
-    NewRow row_cur = append_fetch<T, H, D, D2>(tp, pc, nch, true, lane);
+    // (a CTA may own no piece at all: nothing is fetched then)
+    NewRow row_cur = append_fetch<T, H, D, D2>(tp, have ? pc : Piece{}, nch, true, lane);
     // cos / sin of the current piece's Q chunks (RoPE), loaded one piece ahead
-    QRope<D, D2> rope_cur = q_rope_fetch<T, D, D2>(tp, pc, lane);
+    QRope<D, D2> rope_cur = q_rope_fetch<T, D, D2>(tp, have ? pc : Piece{}, lane);
     while (ok && have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
@@ -979,7 +980,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     bool have = walk.next(tp, pc);
     // The new V row of the current piece's segment (fused append), loaded
     // one piece ahead.
-    NewRow row_cur = append_fetch<T, H, D, D2>(tp, pc, nch, false, lane);
+    NewRow row_cur = append_fetch<T, H, D, D2>(tp, have ? pc : Piece{}, nch, false, lane);
     while (ok && have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
