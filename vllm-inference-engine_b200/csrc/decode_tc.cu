@@ -360,14 +360,15 @@ __device__ __forceinline__ void stage_q(const TcParams &tp, const Piece &q, int 
 }
 
 // RoPE of a piece's staged Q. A lane's chunks have kDV distinct head
-// dimensions (one for head_dim <= 64, (sub-row, half) pairs above); their
-// cos / sin chunks are loaded one piece ahead (q_rope_fetch) and the S issuer
-// rotates the landed operand in place before the piece's first MMA
-// (rotate_q): q * cos + rotate_half(q) * sin, rounded as the append kernels
-// round it. A chunk's rotation partner, D / 2 elements away in the same head,
-// is a shuffle of the same chunk (lane ^ D / 16, head_dim <= 64: every lane
-// reads its chunk before any lane writes) or another of the lane's own chunks
-// (c ^ N / 4 at head_dim 128, c ^ N / 2 at 256, read and written together).
+// dimensions (one for head_dim <= 64, (sub-row, half) pairs above); the four
+// correction warps load their cos / sin chunks (q_rope_fetch) and rotate the
+// landed operand in place (rotate_q), a quarter of the chunks each, before the
+// S issuer's first MMA of the piece: q * cos + rotate_half(q) * sin, rounded as
+// the append kernels round it. A chunk's rotation partner, D / 2 elements away
+// in the same head, is a shuffle of the same chunk (lane ^ D / 16, head_dim
+// <= 64: every lane reads its chunk before any lane writes) or another of the
+// lane's own chunks (c ^ N / 4 at head_dim 128, c ^ N / 2 at 256, read and
+// written together).
 template <int D, int D2>
 struct QRope {
   static constexpr int kDV = D >= 128 ? 2 * D2 : 1;
@@ -392,59 +393,64 @@ __device__ __forceinline__ QRope<D, D2> q_rope_fetch(const TcParams &tp, const P
 
 template <typename T, int H, int GP, int N, int D, int D2>
 __device__ __forceinline__ void rotate_q(const TcParams &tp, const Piece &q, int nch, uint32_t qbuf,
-                                         const QRope<D, D2> &rp, int lane) {
+                                         const QRope<D, D2> &rp, int lane, int cw) {
+  // Warp cw of the four correction warps rotates chunks c = cw + 4 i of every
+  // lane; a chunk's partner at head_dim >= 128 (c ^ kp, kp a multiple of 4)
+  // falls in the same warp and lane.
   using E = Elem<T>;
   constexpr int kQChunks = 16 * N * D2 / 32;
   constexpr int kDV = QRope<D, D2>::kDV;
-  constexpr int GS = kQChunks <= 8 ? kQChunks : 4;  // chunks in flight per group
-  static_assert(kQChunks % GS == 0 && GS % 4 == 0, "rotation groups");
+  constexpr int NC = kQChunks / 4;
   constexpr int kp = kQChunks / 2;  // partner distance in chunks at head_dim >= 128
+  static_assert(kQChunks % 4 == 0 && kp % 4 == 0, "rotation chunks per warp");
+  uint4 xs[NC];
+  bool in[NC];
+  int dd[NC];
+  uint32_t addr[NC];
 #pragma unroll
-  for (int grp = 0; grp < kQChunks / GS; ++grp) {
-    int cl[GS];
+  for (int i = 0; i < NC; ++i) {
+    const T *src;
+    q_chunk<T, H, GP, N, D>(tp.p, q, nch, qbuf, lane, cw + 4 * i, in[i], dd[i], addr[i], src);
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(xs[i].x), "=r"(xs[i].y), "=r"(xs[i].z), "=r"(xs[i].w)
+                 : "r"(addr[i])
+                 : "memory");
+  }
 #pragma unroll
-    for (int i = 0; i < GS; ++i)
-      cl[i] = D <= 64 ? grp * GS + i : grp * (GS / 2) + (i % (GS / 2)) + (i / (GS / 2)) * kp;
-    uint4 xs[GS];
-    bool in[GS];
-    int dd[GS];
-    uint32_t addr[GS];
-#pragma unroll
-    for (int i = 0; i < GS; ++i) {
-      const T *src;
-      q_chunk<T, H, GP, N, D>(tp.p, q, nch, qbuf, lane, cl[i], in[i], dd[i], addr[i], src);
-      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                   : "=r"(xs[i].x), "=r"(xs[i].y), "=r"(xs[i].z), "=r"(xs[i].w)
-                   : "r"(addr[i])
-                   : "memory");
+  for (int i = 0; i < NC; ++i) {
+    uint4 xp;
+    if constexpr (D <= 64) {
+      xp.x = __shfl_xor_sync(0xffffffffu, xs[i].x, D / 16);
+      xp.y = __shfl_xor_sync(0xffffffffu, xs[i].y, D / 16);
+      xp.z = __shfl_xor_sync(0xffffffffu, xs[i].z, D / 16);
+      xp.w = __shfl_xor_sync(0xffffffffu, xs[i].w, D / 16);
+    } else {
+      xp = xs[i ^ (kp / 4)];
     }
+    if (in[i]) {
+      const int idx = lane + (cw + 4 * i) * 32;
+      const int v = kDV == 1 ? 0 : (idx / (16 * N)) * 2 + (idx % (16 * N)) / (8 * N);
+      const bool lo = dd[i] < D / 2;
+      float a[8], b[8], cv[8], sv[8], o[8];
+      E::unpack8(xs[i], a);
+      E::unpack8(xp, b);
+      // select the cos / sin registers of dimension set v (no local-memory indexing)
+      uint4 cvv = rp.c[0], svv = rp.s[0];
 #pragma unroll
-    for (int i = 0; i < GS; ++i) {
-      uint4 xp;
-      if constexpr (D <= 64) {
-        xp.x = __shfl_xor_sync(0xffffffffu, xs[i].x, D / 16);
-        xp.y = __shfl_xor_sync(0xffffffffu, xs[i].y, D / 16);
-        xp.z = __shfl_xor_sync(0xffffffffu, xs[i].z, D / 16);
-        xp.w = __shfl_xor_sync(0xffffffffu, xs[i].w, D / 16);
-      } else {
-        xp = xs[i ^ (GS / 2)];
+      for (int u = 1; u < kDV; ++u) {
+        if (v == u) {
+          cvv = rp.c[u];
+          svv = rp.s[u];
+        }
       }
-      if (in[i]) {
-        const int idx = lane + cl[i] * 32;
-        const int v = kDV == 1 ? 0 : (idx / (16 * N)) * 2 + (idx % (16 * N)) / (8 * N);
-        const bool lo = dd[i] < D / 2;
-        float a[8], b[8], cv[8], sv[8], o[8];
-        E::unpack8(xs[i], a);
-        E::unpack8(xp, b);
-        E::unpack8(rp.c[v], cv);
-        E::unpack8(rp.s[v], sv);
+      E::unpack8(cvv, cv);
+      E::unpack8(svv, sv);
 #pragma unroll
-        for (int k2 = 0; k2 < 8; ++k2) o[k2] = rope_elem<T>(a[k2], cv[k2], lo ? -b[k2] : b[k2], sv[k2]);
-        const uint4 r = E::pack8(o);
-        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr[i]), "r"(r.x), "r"(r.y), "r"(r.z),
-                     "r"(r.w)
-                     : "memory");
-      }
+      for (int k2 = 0; k2 < 8; ++k2) o[k2] = rope_elem<T>(a[k2], cv[k2], lo ? -b[k2] : b[k2], sv[k2]);
+      const uint4 r = E::pack8(o);
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr[i]), "r"(r.x), "r"(r.y), "r"(r.z),
+                   "r"(r.w)
+                   : "memory");
     }
   }
 }
@@ -551,7 +557,7 @@ struct SmemLayout {
   // kfull, kempty [SK]; vfull, vempty [SV]; s_full, s_empty, p_full, p_empty,
   // o_full, o_empty [2]; mma_done [1]; a_full [kRescaleSlots]; q_full, q_empty
   // [kQSlots]; l_full [kLSlots]
-  static constexpr int kNumBars = 2 * SK + 2 * SV + 6 * 2 + 1 + kRescaleSlots + 2 * kQSlots + kLSlots;
+  static constexpr int kNumBars = 2 * SK + 2 * SV + 6 * 2 + 1 + kRescaleSlots + 2 * kQSlots + kLSlots + kQSlots;
   static constexpr int kOffMisc = kOffBars + kNumBars * 8;  // see MiscSmem
   static constexpr int kBytes = kOffMisc + (int)sizeof(MiscSmem);
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
@@ -610,6 +616,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
   auto q_full = [&](uint32_t i) { return bars + 8u * (kBarTail + 1 + kRescaleSlots + i % kQSlots); };
   auto q_empty = [&](uint32_t i) { return bars + 8u * (kBarTail + 1 + kRescaleSlots + kQSlots + i % kQSlots); };
   auto l_full = [&](uint32_t i) { return bars + 8u * (kBarTail + 1 + kRescaleSlots + 2 * kQSlots + i % kLSlots); };
+  // q_rot: with RoPE, the Q of slot i % kQSlots has been rotated in place
+  auto q_rot = [&](uint32_t i) {
+    return bars + 8u * (kBarTail + 1 + kRescaleSlots + 2 * kQSlots + kLSlots + i % kQSlots);
+  };
   // Phase parity of the (i / ring)-th use of ring slot i % ring.
   auto ring_parity = [](uint32_t i, uint32_t ring) { return (i / ring) & 1u; };
   MiscSmem *misc = reinterpret_cast<MiscSmem *>(smem + L::kOffMisc);
@@ -652,6 +662,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       mbar_init(q_empty(s), 1);  // MMA commit after the piece's last S
     }
     for (int s = 0; s < kLSlots; ++s) mbar_init(l_full(s), 4);  // lane 0 of each softmax warp
+    for (int s = 0; s < kQSlots; ++s) mbar_init(q_rot(s), 128);  // every correction thread (RoPE)
     misc->abort = 0;
     fence_mbarrier_init();
   }
@@ -904,20 +915,15 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     // one piece ahead.
     // (a CTA may own no piece at all: nothing is fetched then)
     NewRow row_cur = append_fetch<T, H, D, D2>(tp, have ? pc : Piece{}, nch, true, lane);
-    // cos / sin of the current piece's Q chunks (RoPE), loaded one piece ahead
-    QRope<D, D2> rope_cur = q_rope_fetch<T, D, D2>(tp, have ? pc : Piece{}, lane);
     while (ok && have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
       const NewRow row_nxt = have_nx ? append_fetch<T, H, D, D2>(tp, nx, nch, true, lane) : row_cur;
-      const QRope<D, D2> rope_nxt = have_nx ? q_rope_fetch<T, D, D2>(tp, nx, lane) : rope_cur;
-      if (!PKV_TW(0, mbar_wait(q_full(qi), ring_parity(qi, kQSlots), abort_flag, kTimeoutNs))) break;
+      // Q landed (cp.async), and with RoPE the correction warps rotated it
+      const uint32_t qbar = tp.cos != nullptr ? q_rot(qi) : q_full(qi);
+      if (!PKV_TW(0, mbar_wait(qbar, ring_parity(qi, kQSlots), abort_flag, kTimeoutNs))) break;
       const uint32_t qbuf = sbase + L::kOffQ + (qi % kQSlots) * L::kQBytes;
-      if (tp.cos != nullptr) {
-        rotate_q<T, H, GP, N, D, D2>(tp, pc, nch, qbuf, rope_cur, lane);
-        __syncwarp();
-      }
-      fence_proxy_async_smem();  // Q landed through cp.async / was rotated (generic proxy); the MMA reads it
+      fence_proxy_async_smem();  // Q written through the generic proxy; the MMA reads it
       for (int j = 0; j < pc.ntiles; ++j) {
         const uint32_t b = gt & 1u;
         const bool patch = tp.k_new != nullptr && pc.t1 == pc.len && j + 1 == pc.ntiles;
@@ -962,7 +968,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       pc = nx;
       have = have_nx;
       row_cur = row_nxt;
-      rope_cur = rope_nxt;
     }
     // Every MMA this thread issued has completed before TMEM is released.
     if (lane == 0) mma_commit(mma_done);
@@ -1218,6 +1223,21 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 
     Piece pc;
     bool have = walk.next(tp, pc);
+    // With RoPE the four correction warps rotate each piece's landed Q in
+    // place (q_rot tells the S issuer): the first piece's now, each next
+    // piece's after the current piece's first tile is folded, its cos / sin
+    // loaded at the top of the current piece.
+    const bool rope_q = tp.cos != nullptr;
+    uint32_t qr = 0;
+    auto rotate_piece_q = [&](const Piece &q, const QRope<D, D2> &rr) {
+      if (mbar_wait(q_full(qr), ring_parity(qr, kQSlots), abort_flag, kTimeoutNs)) {
+        rotate_q<T, H, GP, N, D, D2>(tp, q, nch, sbase + L::kOffQ + (qr % kQSlots) * L::kQBytes, rr, lane, warp - 7);
+        fence_proxy_async_smem();
+        mbar_arrive(q_rot(qr));
+      }
+      ++qr;
+    };
+    if (rope_q && have) rotate_piece_q(pc, q_rope_fetch<T, D, D2>(tp, pc, lane));
 
     // Sequences of length 0 own no tiles: CTA (seq % grid) writes their zeros.
     for (int s = blockIdx.x; s < p.num_seqs; s += gridDim.x) {
@@ -1233,6 +1253,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     while (have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
+      const QRope<D, D2> rope_nx = rope_q && have_nx ? q_rope_fetch<T, D, D2>(tp, nx, lane) : QRope<D, D2>{};
       float acc[D2][GP], msel[GP];  // acc[sub]: dims sub * 128 + dim
 #pragma unroll
       for (int g = 0; g < GP; ++g) {
@@ -1273,6 +1294,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           }
         }
         ++gt;
+        // the next piece's Q, once this piece's first tile is folded (its
+        // cos / sin have landed meanwhile)
+        if (j == 0 && rope_q && have_nx) rotate_piece_q(nx, rope_nx);
       }
       // Denominators of this thread's query columns: the four warp partials.
       float lsum[GP];
