@@ -87,6 +87,13 @@ constexpr float kRescaleLog2 = 8.f;            // lazy-rescale threshold (log2 u
 constexpr int kTraceSlots = 16;
 constexpr int kTraceCtas = 160;
 __device__ unsigned long long g_trace[kTraceCtas][7][kTraceSlots];
+// Timeline of the last kTraceRecs CTA runs, indexed by a ticket every CTA
+// takes at entry (launch = ticket / grid: a launch's CTAs all start before
+// the next launch may): ticket, %smid, entry, after the dependency wait,
+// first S tile ready, exit (globaltimer ns).
+constexpr int kTraceRecs = 160 * 48;
+__device__ unsigned long long g_tl[kTraceRecs][6];
+__device__ unsigned long long g_tl_ctr;
 #define PKV_TW(slot, expr)             \
   ([&]() {                              \
     const uint64_t _t0 = clock64();     \
@@ -532,6 +539,9 @@ __device__ __forceinline__ void combine_pieces(const TcParams &tp, PieceAcc<GP, 
 }
 
 struct MiscSmem {
+#ifdef PAGEDKV_TRACE
+  unsigned long long tl_ticket;
+#endif
   uint32_t tmem;
   int abort;
   int len0, len1;  // clamped lengths of seq0 and seq0 + 1
@@ -638,6 +648,17 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
   const uint64_t c_kernel0 = clock64();
 #endif
 
+#ifdef PAGEDKV_TRACE
+  if (threadIdx.x == 0) {
+    const unsigned long long tk = atomicAdd(&g_tl_ctr, 1ull);
+    misc->tl_ticket = tk;
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    g_tl[tk % kTraceRecs][0] = tk;
+    g_tl[tk % kTraceRecs][1] = smid;
+    g_tl[tk % kTraceRecs][2] = t_kernel0;
+  }
+#endif
   if (threadIdx.x == 0) {
     for (int s = 0; s < SK; ++s) {
       mbar_init(kfull(s), 1);   // producer arrive.expect_tx + TMA bytes
@@ -675,6 +696,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
   // tail of the preceding kernel; global inputs are read only after it ends.
   grid_dependency_wait();
   grid_launch_dependents();
+#ifdef PAGEDKV_TRACE
+  if (threadIdx.x == 0) g_tl[misc->tl_ticket % kTraceRecs][3] = globaltimer_ns();
+#endif
 
   // ---- prologue: total cost units and the start of this CTA's range ----------
   {
@@ -1083,6 +1107,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         const uint32_t b = gt & 1u;
         const uint32_t bph = (gt >> 1) & 1u;
         PKV_TW(0, mbar_wait(bar2(0, b), bph, abort_flag, kTimeoutNs));
+#ifdef PAGEDKV_TRACE
+        if (gt == 0 && warp == 2 && lane == 0) g_tl[misc->tl_ticket % kTraceRecs][4] = globaltimer_ns();
+#endif
         PKV_TADD(5, 1);
         tc_fence_after();
         float s[N];
@@ -1397,6 +1424,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
     g_trace[blockIdx.x][3][5] = smid;
   }
+  if (threadIdx.x == 0) g_tl[misc->tl_ticket % kTraceRecs][5] = globaltimer_ns();
 #endif
   if (threadIdx.x == 0 && *abort_flag) set_error(p.err, PAGEDKV_EFLAG_PIPE_TIMEOUT);
   tc_fence_before();
@@ -1588,6 +1616,12 @@ cudaError_t dispatch_tc(const TcPlan &pl, const CUtensorMap &mk, const CUtensorM
 extern "C" int pagedkv_trace_read(unsigned long long *host, size_t count) {
   const size_t n = sizeof(g_trace) / sizeof(unsigned long long);
   return cudaMemcpyFromSymbol(host, g_trace, (count < n ? count : n) * sizeof(unsigned long long)) == cudaSuccess ? 0 : 3;
+}
+// The CTA timeline records (kTraceRecs x 6) and the ticket counter.
+extern "C" int pagedkv_trace_timeline(unsigned long long *host, size_t count, unsigned long long *tickets) {
+  const size_t n = sizeof(g_tl) / sizeof(unsigned long long);
+  if (cudaMemcpyFromSymbol(tickets, g_tl_ctr, sizeof(unsigned long long)) != cudaSuccess) return 3;
+  return cudaMemcpyFromSymbol(host, g_tl, (count < n ? count : n) * sizeof(unsigned long long)) == cudaSuccess ? 0 : 3;
 }
 #endif
 
