@@ -884,9 +884,8 @@ def run_ours(args) -> None:
             pagedkv.copy_blocks(kcs, vcs, pairs)
         for layer in range(L):
             dq, dk, dv = views[3 + 3 * layer : 6 + 3 * layer]
-            o = pagedkv.paged_attention_decode_append(dq, kcs[layer], vcs[layer], dt, dl, scale, dk, dv, cos_t,
-                                                      sin_t, slot_mapping=ds)
-            out_buf[layer].copy_(o)
+            pagedkv.paged_attention_decode_append(dq, kcs[layer], vcs[layer], dt, dl, scale, dk, dv, cos_t,
+                                                  sin_t, slot_mapping=ds, out=out_buf[layer])
 
     d_in = torch.empty(offs[-1], dtype=torch.uint8, device=dev)
     views = make_views(d_in)

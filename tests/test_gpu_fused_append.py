@@ -192,3 +192,19 @@ def test_fused_append_batches_that_leave_ctas_without_work(cuda_ready, lens, rop
     torch.cuda.synchronize()
     assert torch.equal(kf, ku) and torch.equal(vf, vu) and torch.equal(out_f, out_u)
     assert pagedkv.read_error_flags(cuda_ready) == 0
+
+
+def test_fused_append_writes_into_a_given_output(cuda_ready):
+    """``out=`` receives the result in place of a new tensor (a row of a
+    larger buffer, as a caller batching several layers' outputs passes it)."""
+    c = _case(77, 14, 2, 64, 16, [40, 700, 2048])
+    dev = cuda_ready
+    out_f, _, _, _, _, _, _, _ = _run(c, dev, False)
+    buf = torch.full((3,) + tuple(c["q"].shape), float("nan"), dtype=torch.float16, device=dev)
+    kf, vf = c["k"].to(dev), c["v"].to(dev)
+    got = pagedkv.paged_attention_decode_append(
+        c["q"].to(dev), kf, vf, c["tables"].to(dev), torch.tensor(c["lens"], dtype=torch.int32, device=dev),
+        1.0 / 8, c["k_new"].to(dev), c["v_new"].to(dev), out=buf[1])
+    assert got.data_ptr() == buf[1].data_ptr()
+    assert torch.equal(buf[1], out_f)
+    assert torch.isnan(buf[0]).all() and torch.isnan(buf[2]).all()

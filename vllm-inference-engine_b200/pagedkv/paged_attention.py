@@ -594,6 +594,7 @@ def paged_attention_decode_append(
     cos: torch.Tensor | None = None,  # [num_seqs, head_dim] (or [num_seqs, 1, head_dim])
     sin: torch.Tensor | None = None,
     slot_mapping: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """One layer's decode step in ONE launch: the KV append of each sequence's
     new K / V row at position ``seq_len - 1`` of its block table, then batched
@@ -609,6 +610,8 @@ def paged_attention_decode_append(
     by the CUDA-core kernel (block_size < 8) or unaligned new rows run those
     two operations as separate launches (``slot_mapping``, if given, must be
     the slots of position ``seq_len - 1``; else it is computed on the device).
+    ``out`` (optional, [num_seqs, num_q_heads, head_dim] in q's dtype, last
+    dimension contiguous) receives the output in place of a new tensor.
     """
     assert q.is_cuda and k_cache.is_cuda and v_cache.is_cuda and block_tables.is_cuda and seq_lens.is_cuda
     assert q.dtype in _DTYPES and k_cache.dtype == q.dtype and v_cache.dtype == q.dtype
@@ -632,13 +635,19 @@ def paged_attention_decode_append(
         assert c2.dtype == q.dtype and s2.dtype == q.dtype and c2.shape == (num_seqs, head_dim)
         if c2.stride() != s2.stride() or c2.stride(-1) != 1:
             c2, s2 = c2.contiguous(), s2.contiguous()
-    out = torch.empty_like(q)
+    if out is None:
+        out = torch.empty_like(q)
+    else:
+        assert out.shape == q.shape and out.dtype == q.dtype and out.device == q.device
     if num_seqs == 0:
         return out
     if block_tables.stride(-1) != 1:
         block_tables = block_tables.contiguous()
     if not seq_lens.is_contiguous():
         seq_lens = seq_lens.contiguous()
+    given_out = out
+    if not _qo_ok(out):
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     if k3.stride(2) != 1:
         k3 = k3.contiguous()
     if v3.stride(2) != 1:
@@ -681,12 +690,14 @@ def paged_attention_decode_append(
             kv_append(k3, v3, k_cache, v_cache, slots)
             q_rot = q
         _decode_into(out, q_rot, k_cache, v_cache, block_tables, seq_lens, 0, scale)
-        return out
-    if rc:
-        _native.check(rc, "pagedkv_decode_attention_append")
-    if _DEBUG:
-        _debug_check(q.device, "paged decode attention + append")
-    return out
+    else:
+        if rc:
+            _native.check(rc, "pagedkv_decode_attention_append")
+        if _DEBUG:
+            _debug_check(q.device, "paged decode attention + append")
+    if out is not given_out:
+        given_out.copy_(out)
+    return given_out
 
 
 def last_decode_launch_info() -> tuple[int, str]:
