@@ -121,6 +121,41 @@ def test_fused_append_bf16(cuda_ready):
     assert torch.equal(kf, ku) and torch.equal(vf, vu) and torch.equal(out_f, out_u)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(14, 2, 64, 16, [33, 700, 129]), (16, 8, 256, 16, [17, 300])])
+def test_fused_rope_rounding_at_extreme_magnitudes(cuda_ready, shape, dtype):
+    """Q and the new K row scaled element-wise by powers of two down to the
+    16-bit subnormals (and, for bf16, products below fp32's normal range),
+    with some cos / sin entries tiny as well: the in-kernel rotation still
+    equals transformers' op sequence bit for bit (the pool row against the
+    oracle, the output against the separate RoPE + append launches)."""
+    hq, hkv, d, bs, lens = shape
+    c = _case(11, hq, hkv, d, bs, lens, dtype=dtype)
+    g = torch.Generator().manual_seed(12)
+    lo_exp = -30 if dtype == torch.float16 else -130
+
+    def spread(x):
+        e = torch.randint(lo_exp, 1, x.shape, generator=g).float()
+        return (x.float() * torch.pow(2.0, e)).to(dtype)
+
+    c["q"], c["k_new"] = spread(c["q"]), spread(c["k_new"])
+    tiny = torch.rand(c["sin"].shape, generator=g) < 0.25
+    c["sin"] = torch.where(tiny, spread(c["sin"]), c["sin"])
+    c["cos"] = torch.where(~tiny, spread(c["cos"]), c["cos"])
+    out_f, kf, vf, out_u, ku, vu, _, _ = _run(c, cuda_ready, True)
+    torch.cuda.synchronize()
+    assert torch.equal(kf, ku) and torch.equal(vf, vu)
+    assert torch.equal(out_f, out_u)
+    slots = paged_ref.decode_slots(c["rows"], c["lens"], bs)
+    kr, vr = c["k"].clone(), c["v"].clone()
+    k_rows = paged_ref.rope_ref(c["k_new"], c["cos"], c["sin"])
+    paged_ref.kv_append_ref(kr.view(torch.int16).numpy(), vr.view(torch.int16).numpy(),
+                            k_rows.view(torch.int16).numpy(), c["v_new"].view(torch.int16).numpy(), slots)
+    assert torch.equal(kf.cpu().view(torch.int16), kr.view(torch.int16))
+    assert torch.equal(vf.cpu().view(torch.int16), vr.view(torch.int16))
+    assert pagedkv.read_error_flags(cuda_ready) == 0
+
+
 def test_fused_append_config2_full_size(cuda_ready):
     """256 x 2048 tokens, 40960-block pool, the append of
     the 2048th token fused into the attention."""

@@ -95,6 +95,45 @@ __device__ __forceinline__ float rope_elem(float a, float c, float b, float s) {
   return p1 + p2;
 }
 
+// Eight elements of the same rotation on packed 16-bit pairs: r(r(x * c) +
+// r(xp' * s)) with xp' = xp negated when `lo` (the first half of the head).
+// Each op is one correctly rounded f16x2 / bf16x2 instruction (explicit .rn,
+// so nothing is contracted into an fma), which equals rope_elem: the product
+// of two 16-bit values is exact in fp32 (for bf16 products below fp32's
+// normal range the significand product has under 16 bits, so rounding it to
+// fp32 first changes no bf16 rounding), and an fp32 sum rounded to 16 bits is
+// the correctly rounded 16-bit sum (24 >= 2 * 11 + 2).
+template <typename T>
+__device__ __forceinline__ uint32_t mul2_rn(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (Elem<T>::kDtype == PAGEDKV_DTYPE_F16)
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t add2_rn(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (Elem<T>::kDtype == PAGEDKV_DTYPE_F16)
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 rope8(const uint4 &x, const uint4 &xp, const uint4 &c, const uint4 &s, bool lo) {
+  const uint32_t neg = lo ? 0x80008000u : 0u;  // sign bits of both halves
+  uint4 r;
+  r.x = add2_rn<T>(mul2_rn<T>(x.x, c.x), mul2_rn<T>(xp.x ^ neg, s.x));
+  r.y = add2_rn<T>(mul2_rn<T>(x.y, c.y), mul2_rn<T>(xp.y ^ neg, s.y));
+  r.z = add2_rn<T>(mul2_rn<T>(x.z, c.z), mul2_rn<T>(xp.z ^ neg, s.z));
+  r.w = add2_rn<T>(mul2_rn<T>(x.w, c.w), mul2_rn<T>(xp.w ^ neg, s.w));
+  return r;
+}
+
 // log2(e): scores are kept in the base-2 domain so exp() becomes one exp2f.
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegInf = -__builtin_huge_valf();

@@ -42,9 +42,9 @@
 //     lower-numbered blocks, so a combining CTA only ever waits on CTAs
 //     dispatched before it — no second launch, equal tiles per SM.
 //   * Warp roles (12 warps): 0 K-tile TMA producer (also copies each piece's
-//     Q), 6 V-tile TMA producer, 1 S-MMA issuer (TMEM owner; with RoPE it
-//     rotates each piece's landed Q in place), 11 O-MMA issuer, 2-5 softmax,
-//     7-10 correction / epilogue. With the fused decode append, the two MMA
+//     Q; with RoPE it rotates the landed Q in place), 6 V-tile TMA producer,
+//     1 S-MMA issuer (TMEM owner), 11 O-MMA issuer, 2-5 softmax, 7-10
+//     correction / epilogue. With the fused decode append, the two MMA
 //     issuers patch the new K / V row into the landed tile (and the pool).
 //     Each tcgen05.mma costs its issuing thread tens of nanoseconds, so S and
 //     O are issued from two warps. K and V have separate smem rings: a K tile
@@ -243,7 +243,7 @@ struct NewRow {
   int32_t blk;    // pool block of position len - 1
 };
 
-template <typename T, int H, int D, int D2>
+template <typename T, int H, int D, int D2, bool RP>
 __device__ __forceinline__ NewRow append_fetch(const TcParams &tp, const Piece &pc, int nch, bool is_k, int lane) {
   NewRow r;
   r.x = r.c = r.s = make_uint4(0u, 0u, 0u, 0u);
@@ -259,7 +259,7 @@ __device__ __forceinline__ NewRow append_fetch(const TcParams &tp, const Piece &
     const T *src = static_cast<const T *>(is_k ? tp.k_new : tp.v_new);
     const int64_t st = is_k ? tp.kn_st : tp.vn_st, sh = is_k ? tp.kn_sh : tp.vn_sh;
     r.x = ldg16(src + (int64_t)pc.seq * st + (int64_t)kv * sh + d);
-    if (is_k && tp.cos != nullptr) {
+    if (RP && is_k) {
       r.c = ldg16(static_cast<const T *>(tp.cos) + (int64_t)pc.seq * tp.cs_st + d);
       r.s = ldg16(static_cast<const T *>(tp.sin) + (int64_t)pc.seq * tp.cs_st + d);
     }
@@ -269,26 +269,17 @@ __device__ __forceinline__ NewRow append_fetch(const TcParams &tp, const Piece &
 
 // The lane's chunk of the new row as stored: K rotated when RoPE is on (the
 // partner half of each head is D / 16 lanes away; every lane shuffles).
-template <typename T, int D>
-__device__ __forceinline__ uint4 append_chunk(const TcParams &tp, const NewRow &r, bool is_k, int lane) {
-  using E = Elem<T>;
+template <typename T, int D, bool RP>
+__device__ __forceinline__ uint4 append_chunk(const NewRow &r, bool is_k, int lane) {
   uint4 x = r.x;
-  if (is_k && tp.cos != nullptr) {
+  if (RP && is_k) {
     uint4 xp;
     xp.x = __shfl_xor_sync(0xffffffffu, x.x, D / 16);
     xp.y = __shfl_xor_sync(0xffffffffu, x.y, D / 16);
     xp.z = __shfl_xor_sync(0xffffffffu, x.z, D / 16);
     xp.w = __shfl_xor_sync(0xffffffffu, x.w, D / 16);
-    const int d = (lane * 8) % D;
-    float a[8], b[8], c[8], sv[8], o[8];
-    E::unpack8(x, a);
-    E::unpack8(xp, b);
-    E::unpack8(r.c, c);
-    E::unpack8(r.s, sv);
-    const bool lo = d < D / 2;  // rotate_half: -x[d + D/2] on the first half, x[d - D/2] on the second
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = rope_elem<T>(a[i], c[i], lo ? -b[i] : b[i], sv[i]);
-    x = E::pack8(o);
+    // rotate_half: -x[d + D/2] on the first half, x[d - D/2] on the second
+    x = rope8<T>(x, xp, r.c, r.s, (lane * 8) % D < D / 2);
   }
   return x;
 }
@@ -366,98 +357,75 @@ __device__ __forceinline__ void stage_q(const TcParams &tp, const Piece &q, int 
   }
 }
 
-// RoPE of a piece's staged Q. A lane's chunks have kDV distinct head
-// dimensions (one for head_dim <= 64, (sub-row, half) pairs above); the four
-// correction warps load their cos / sin chunks (q_rope_fetch) and rotate the
-// landed operand in place (rotate_q), a quarter of the chunks each, before the
-// S issuer's first MMA of the piece: q * cos + rotate_half(q) * sin, rounded as
-// the append kernels round it. A chunk's rotation partner, D / 2 elements away
-// in the same head, is a shuffle of the same chunk (lane ^ D / 16, head_dim
-// <= 64: every lane reads its chunk before any lane writes) or another of the
-// lane's own chunks (c ^ N / 4 at head_dim 128, c ^ N / 2 at 256, read and
-// written together).
-template <int D, int D2>
-struct QRope {
-  static constexpr int kDV = D >= 128 ? 2 * D2 : 1;
-  uint4 c[kDV], s[kDV];
-};
-
+// RoPE of a piece's Q (q * cos + rotate_half(q) * sin, rounded as the append
+// kernels round it), done by the K producer on the landed operand in shared
+// memory. stage_cs copies the cos and sin rows of the piece's position beside
+// its Q slot (cp.async, completing on the same q_full barrier); rotate_q
+// rotates every chunk of the lane in place. A chunk's rotation partner, D / 2
+// elements away in the same head, is a shuffle of the same chunk (lane ^ D /
+// 16, head_dim <= 64: every lane reads its chunk before any lane writes) or
+// another of the lane's own chunks (c ^ kp: N / 4 chunks away at head_dim 128,
+// N / 2 at 256, read and written together).
 template <typename T, int D, int D2>
-__device__ __forceinline__ QRope<D, D2> q_rope_fetch(const TcParams &tp, const Piece &q, int lane) {
-  QRope<D, D2> r;
+__device__ __forceinline__ void stage_cs(const TcParams &tp, const Piece &q, uint32_t csbuf, int lane) {
+  constexpr int kChunks = D / 8;  // 16-byte chunks of one row
 #pragma unroll
-  for (int v = 0; v < QRope<D, D2>::kDV; ++v) {
-    r.c[v] = r.s[v] = make_uint4(0u, 0u, 0u, 0u);
-    if (tp.cos != nullptr && q.len > 0) {
-      // dimension of the lane's chunks with (sub-row, half) = (v / 2, v % 2)
-      const int d = (QRope<D, D2>::kDV == 1 ? (lane & 7) * 8 : (v >> 1) * 128 + (v & 1) * 64 + (lane & 7) * 8) % D;
-      r.c[v] = ldg16(static_cast<const T *>(tp.cos) + (int64_t)q.seq * tp.cs_st + d);
-      r.s[v] = ldg16(static_cast<const T *>(tp.sin) + (int64_t)q.seq * tp.cs_st + d);
-    }
+  for (int k = lane; k < 2 * kChunks; k += 32) {
+    const bool is_sin = k >= kChunks;
+    const int ch = is_sin ? k - kChunks : k;
+    const T *src = static_cast<const T *>(is_sin ? tp.sin : tp.cos) + (int64_t)q.seq * tp.cs_st + ch * 8;
+    cp_async_16(csbuf + (is_sin ? 128u * D2 * 2u : 0u) + ch * 16, src, 16u);
   }
-  return r;
 }
 
 template <typename T, int H, int GP, int N, int D, int D2>
-__device__ __forceinline__ void rotate_q(const TcParams &tp, const Piece &q, int nch, uint32_t qbuf,
-                                         const QRope<D, D2> &rp, int lane, int cw) {
-  // Warp cw of the four correction warps rotates chunks c = cw + 4 i of every
-  // lane; a chunk's partner at head_dim >= 128 (c ^ kp, kp a multiple of 4)
-  // falls in the same warp and lane.
-  using E = Elem<T>;
-  constexpr int kQChunks = 16 * N * D2 / 32;
-  constexpr int kDV = QRope<D, D2>::kDV;
-  constexpr int NC = kQChunks / 4;
-  constexpr int kp = kQChunks / 2;  // partner distance in chunks at head_dim >= 128
-  static_assert(kQChunks % 4 == 0 && kp % 4 == 0, "rotation chunks per warp");
-  uint4 xs[NC];
-  bool in[NC];
-  int dd[NC];
-  uint32_t addr[NC];
+__device__ __forceinline__ void rotate_q(const DecodeParams &p, const Piece &q, int nch, uint32_t qbuf,
+                                         uint32_t csbuf, int lane) {
+  constexpr int kQChunks = 16 * N * D2 / 32;  // Q 16-byte chunks per lane
+  constexpr int kp = kQChunks / 2;            // partner distance in chunks at head_dim >= 128
+  constexpr int kG = D <= 64 ? 1 : 2;         // chunks rotated together: a chunk and its partner
+  constexpr uint32_t kSinOff = 128u * D2 * 2u;
 #pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    const T *src;
-    q_chunk<T, H, GP, N, D>(tp.p, q, nch, qbuf, lane, cw + 4 * i, in[i], dd[i], addr[i], src);
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(xs[i].x), "=r"(xs[i].y), "=r"(xs[i].z), "=r"(xs[i].w)
-                 : "r"(addr[i])
-                 : "memory");
-  }
+  for (int g = 0; g < kQChunks / kG; ++g) {
+    uint4 xs[kG];
+    bool in[kG];
+    int dd[kG];
+    uint32_t addr[kG];
 #pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    uint4 xp;
-    if constexpr (D <= 64) {
-      xp.x = __shfl_xor_sync(0xffffffffu, xs[i].x, D / 16);
-      xp.y = __shfl_xor_sync(0xffffffffu, xs[i].y, D / 16);
-      xp.z = __shfl_xor_sync(0xffffffffu, xs[i].z, D / 16);
-      xp.w = __shfl_xor_sync(0xffffffffu, xs[i].w, D / 16);
-    } else {
-      xp = xs[i ^ (kp / 4)];
-    }
-    if (in[i]) {
-      const int idx = lane + (cw + 4 * i) * 32;
-      const int v = kDV == 1 ? 0 : (idx / (16 * N)) * 2 + (idx % (16 * N)) / (8 * N);
-      const bool lo = dd[i] < D / 2;
-      float a[8], b[8], cv[8], sv[8], o[8];
-      E::unpack8(xs[i], a);
-      E::unpack8(xp, b);
-      // select the cos / sin registers of dimension set v (no local-memory indexing)
-      uint4 cvv = rp.c[0], svv = rp.s[0];
-#pragma unroll
-      for (int u = 1; u < kDV; ++u) {
-        if (v == u) {
-          cvv = rp.c[u];
-          svv = rp.s[u];
-        }
-      }
-      E::unpack8(cvv, cv);
-      E::unpack8(svv, sv);
-#pragma unroll
-      for (int k2 = 0; k2 < 8; ++k2) o[k2] = rope_elem<T>(a[k2], cv[k2], lo ? -b[k2] : b[k2], sv[k2]);
-      const uint4 r = E::pack8(o);
-      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr[i]), "r"(r.x), "r"(r.y), "r"(r.z),
-                   "r"(r.w)
+    for (int k = 0; k < kG; ++k) {
+      const T *src;
+      q_chunk<T, H, GP, N, D>(p, q, nch, qbuf, lane, g + k * kp, in[k], dd[k], addr[k], src);
+      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(xs[k].x), "=r"(xs[k].y), "=r"(xs[k].z), "=r"(xs[k].w)
+                   : "r"(addr[k])
                    : "memory");
+    }
+#pragma unroll
+    for (int k = 0; k < kG; ++k) {
+      uint4 xp;
+      if constexpr (D <= 64) {
+        xp.x = __shfl_xor_sync(0xffffffffu, xs[k].x, D / 16);
+        xp.y = __shfl_xor_sync(0xffffffffu, xs[k].y, D / 16);
+        xp.z = __shfl_xor_sync(0xffffffffu, xs[k].z, D / 16);
+        xp.w = __shfl_xor_sync(0xffffffffu, xs[k].w, D / 16);
+      } else {
+        xp = xs[k ^ 1];
+      }
+      if (in[k]) {
+        uint4 c, sn;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(c.x), "=r"(c.y), "=r"(c.z), "=r"(c.w)
+                     : "r"(csbuf + dd[k] * 2)
+                     : "memory");
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(sn.x), "=r"(sn.y), "=r"(sn.z), "=r"(sn.w)
+                     : "r"(csbuf + kSinOff + dd[k] * 2)
+                     : "memory");
+        const uint4 r = rope8<T>(xs[k], xp, c, sn, dd[k] < D / 2);
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr[k]), "r"(r.x), "r"(r.y), "r"(r.z),
+                     "r"(r.w)
+                     : "memory");
+      }
     }
   }
 }
@@ -549,7 +517,7 @@ struct MiscSmem {
   long long lo, hi, total, grid, u0;
 };
 
-template <int N, int SK, int SV, int D2 = 1>
+template <int N, int SK, int SV, int D2 = 1, bool RP = false>
 struct SmemLayout {
   static constexpr int kQSubBytes = 2 * N * 128;     // B operand [N x 128], two K-halves
   static constexpr int kQBytes = D2 * kQSubBytes;    // one per 128-element sub-row of a head
@@ -569,7 +537,10 @@ struct SmemLayout {
   // [kQSlots]; l_full [kLSlots]
   static constexpr int kNumBars = 2 * SK + 2 * SV + 6 * 2 + 1 + kRescaleSlots + 2 * kQSlots + kLSlots + kQSlots;
   static constexpr int kOffMisc = kOffBars + kNumBars * 8;  // see MiscSmem
-  static constexpr int kBytes = kOffMisc + (int)sizeof(MiscSmem);
+  // RoPE only: the cos and sin rows of each Q slot's position (stage_cs)
+  static constexpr int kCSBytes = 2 * 128 * D2 * 2;
+  static constexpr int kOffCS = (kOffMisc + (int)sizeof(MiscSmem) + 15) / 16 * 16;
+  static constexpr int kBytes = RP ? kOffCS + kQSlots * kCSBytes : kOffMisc + (int)sizeof(MiscSmem);
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
   static_assert(2 * 4 * N * 4 >= 8 * (kThreads / 32), "prologue scan scratch fits the max-reduction buffer");
   static_assert(kOffSlots % 16 == 0 && kSlotBytes % 16 == 0 && kOffL % 16 == 0 && kOffBars % 8 == 0, "alignment");
@@ -590,11 +561,12 @@ struct RescaleSlot {
 // separate instantiation, so the single-chunk kernels carry none of it).
 // D2: 128-element sub-rows per head (2 for head_dim 256: every tile is two K
 // and two V ring stages, S sums both, O has one accumulator per sub-row).
-template <typename T, int H, int GP, int N, int SK, int SV, bool CH, int D2>
+// RP: RoPE fused (tp.cos / tp.sin given), a separate instantiation as well.
+template <typename T, int H, int GP, int N, int SK, int SV, bool CH, int D2, bool RP>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
                  const __grid_constant__ CUtensorMap tmap_v, const __grid_constant__ TcParams tp) {
-  using L = SmemLayout<N, SK, SV, D2>;
+  using L = SmemLayout<N, SK, SV, D2, RP>;
   using E = Elem<T>;
   using Slot = RescaleSlot<N>;
   constexpr int D = 128 * D2 / H;                     // head_dim
@@ -683,7 +655,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       mbar_init(q_empty(s), 1);  // MMA commit after the piece's last S
     }
     for (int s = 0; s < kLSlots; ++s) mbar_init(l_full(s), 4);  // lane 0 of each softmax warp
-    for (int s = 0; s < kQSlots; ++s) mbar_init(q_rot(s), 128);  // every correction thread (RoPE)
+    if (RP)
+      for (int s = 0; s < kQSlots; ++s) mbar_init(q_rot(s), 32);  // every K-producer lane, once rotated
     misc->abort = 0;
     fence_mbarrier_init();
   }
@@ -846,23 +819,43 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     // Q of piece q into ring slot i as the block-diagonal B operand
     // [N rows x 128], K-major SW128; padding rows and halves are zero-filled.
     // Q of each piece goes into a Q ring slot one piece ahead by cp.async,
-    // completing on the slot's q_full barrier (with RoPE the S issuer rotates
-    // it in place when it lands).
+    // completing on the slot's q_full barrier. With RoPE the cos / sin rows
+    // come along (same barrier), and this warp rotates the landed Q in place
+    // once the piece's first tile is issued (the whole first ring fill for
+    // the CTA's first piece), where it would otherwise wait for a free stage;
+    // q_rot then hands it to the S issuer.
     auto q_issue = [&](const Piece &q, uint32_t i) -> bool {
       if (!PKV_TW(0, mbar_wait(q_empty(i), ring_parity(i, kQSlots) ^ 1u, abort_flag, kTimeoutNs))) return false;
       stage_q<T, H, GP, N, D, D2>(tp, q, nch, sbase + L::kOffQ + (i % kQSlots) * L::kQBytes, lane);
+      if constexpr (RP) stage_cs<T, D, D2>(tp, q, sbase + L::kOffCS + (i % kQSlots) * L::kCSBytes, lane);
       cp_async_mbar_arrive(q_full(i));
+      return true;
+    };
+    auto q_rotate = [&](const Piece &q, uint32_t i) -> bool {
+      // every lane takes part in the rotation's shuffles, or none does
+      const bool landed = mbar_wait(q_full(i), ring_parity(i, kQSlots), abort_flag, kTimeoutNs);
+      if (!__all_sync(0xffffffffu, landed)) return false;
+      rotate_q<T, H, GP, N, D, D2>(p, q, nch, sbase + L::kOffQ + (i % kQSlots) * L::kQBytes,
+                                   sbase + L::kOffCS + (i % kQSlots) * L::kCSBytes, lane);
+      fence_proxy_async_smem();  // the MMA reads the rotated operand through the async proxy
+      mbar_arrive(q_rot(i));
       return true;
     };
 
     Piece pc;
     bool have = walk.next(tp, pc);
+    uint32_t qcur = qi;  // Q slot index of pc
     if (have && is_k) ok = q_issue(pc, qi++);
+    bool first_piece = true;
     while (ok && have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
       // The next piece's Q, landing while this piece's tiles stream.
+      const uint32_t qnx = qi;
       if (is_k && have_nx && !q_issue(nx, qi++)) break;
+      // RoPE: tiles of this piece issued before its Q is rotated
+      const int rot_at = RP && is_k ? min(pc.ntiles, first_piece ? nst / D2 : 1) : 0;
+      first_piece = false;
       const int lb0 = pc.t0 / p.block_size;
       const int need = (pc.t1 + p.block_size - 1) / p.block_size;
       const int x0 = pc.hg / nch * 128 * D2;  // this tile row's first element
@@ -910,8 +903,15 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           }
         }
         if (!ok) break;
+        if constexpr (RP) {
+          if (j + 1 == rot_at && !q_rotate(pc, qcur)) {
+            ok = false;
+            break;
+          }
+        }
       }
       pc = nx;
+      qcur = qnx;
       have = have_nx;
     }
     cp_async_wait<0>();  // no copy into shared memory outlives this role
@@ -938,20 +938,20 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     // The new K row of the current piece's segment (fused append), loaded
     // one piece ahead.
     // (a CTA may own no piece at all: nothing is fetched then)
-    NewRow row_cur = append_fetch<T, H, D, D2>(tp, have ? pc : Piece{}, nch, true, lane);
+    NewRow row_cur = append_fetch<T, H, D, D2, RP>(tp, have ? pc : Piece{}, nch, true, lane);
     while (ok && have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
-      const NewRow row_nxt = have_nx ? append_fetch<T, H, D, D2>(tp, nx, nch, true, lane) : row_cur;
-      // Q landed (cp.async), and with RoPE the correction warps rotated it
-      const uint32_t qbar = tp.cos != nullptr ? q_rot(qi) : q_full(qi);
+      const NewRow row_nxt = have_nx ? append_fetch<T, H, D, D2, RP>(tp, nx, nch, true, lane) : row_cur;
+      // Q landed (cp.async), and with RoPE the K producer rotated it
+      const uint32_t qbar = RP ? q_rot(qi) : q_full(qi);
       if (!PKV_TW(0, mbar_wait(qbar, ring_parity(qi, kQSlots), abort_flag, kTimeoutNs))) break;
       const uint32_t qbuf = sbase + L::kOffQ + (qi % kQSlots) * L::kQBytes;
       fence_proxy_async_smem();  // Q written through the generic proxy; the MMA reads it
       for (int j = 0; j < pc.ntiles; ++j) {
         const uint32_t b = gt & 1u;
         const bool patch = tp.k_new != nullptr && pc.t1 == pc.len && j + 1 == pc.ntiles;
-        const uint4 xk = patch ? append_chunk<T, D>(tp, row_cur, true, lane) : row_cur.x;
+        const uint4 xk = patch ? append_chunk<T, D, RP>(row_cur, true, lane) : row_cur.x;
         for (int sub = 0; sub < D2; ++sub) {  // S sums the sub-rows' products
           if (!PKV_TW(1, mbar_wait(kfull(kst), kph, abort_flag, kTimeoutNs))) { ok = false; break; }
           if (sub == 0 && !PKV_TW(2, mbar_wait(bar2(1, b), ((gt >> 1) & 1u) ^ 1u, abort_flag, kTimeoutNs))) {
@@ -1009,11 +1009,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     bool have = walk.next(tp, pc);
     // The new V row of the current piece's segment (fused append), loaded
     // one piece ahead.
-    NewRow row_cur = append_fetch<T, H, D, D2>(tp, have ? pc : Piece{}, nch, false, lane);
+    NewRow row_cur = append_fetch<T, H, D, D2, RP>(tp, have ? pc : Piece{}, nch, false, lane);
     while (ok && have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
-      const NewRow row_nxt = have_nx ? append_fetch<T, H, D, D2>(tp, nx, nch, false, lane) : row_cur;
+      const NewRow row_nxt = have_nx ? append_fetch<T, H, D, D2, RP>(tp, nx, nch, false, lane) : row_cur;
       for (int j = 0; j < pc.ntiles; ++j) {
         const uint32_t b = gt & 1u;
         const uint32_t bph = (gt >> 1) & 1u;
@@ -1250,21 +1250,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 
     Piece pc;
     bool have = walk.next(tp, pc);
-    // With RoPE the four correction warps rotate each piece's landed Q in
-    // place (q_rot tells the S issuer): the first piece's now, each next
-    // piece's after the current piece's first tile is folded, its cos / sin
-    // loaded at the top of the current piece.
-    const bool rope_q = tp.cos != nullptr;
-    uint32_t qr = 0;
-    auto rotate_piece_q = [&](const Piece &q, const QRope<D, D2> &rr) {
-      if (mbar_wait(q_full(qr), ring_parity(qr, kQSlots), abort_flag, kTimeoutNs)) {
-        rotate_q<T, H, GP, N, D, D2>(tp, q, nch, sbase + L::kOffQ + (qr % kQSlots) * L::kQBytes, rr, lane, warp - 7);
-        fence_proxy_async_smem();
-        mbar_arrive(q_rot(qr));
-      }
-      ++qr;
-    };
-    if (rope_q && have) rotate_piece_q(pc, q_rope_fetch<T, D, D2>(tp, pc, lane));
 
     // Sequences of length 0 own no tiles: CTA (seq % grid) writes their zeros.
     for (int s = blockIdx.x; s < p.num_seqs; s += gridDim.x) {
@@ -1280,7 +1265,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     while (have) {
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
-      const QRope<D, D2> rope_nx = rope_q && have_nx ? q_rope_fetch<T, D, D2>(tp, nx, lane) : QRope<D, D2>{};
       float acc[D2][GP], msel[GP];  // acc[sub]: dims sub * 128 + dim
 #pragma unroll
       for (int g = 0; g < GP; ++g) {
@@ -1321,9 +1305,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           }
         }
         ++gt;
-        // the next piece's Q, once this piece's first tile is folded (its
-        // cos / sin have landed meanwhile)
-        if (j == 0 && rope_q && have_nx) rotate_piece_q(nx, rope_nx);
       }
       // Denominators of this thread's query columns: the four warp partials.
       float lsum[GP];
@@ -1552,12 +1533,12 @@ bool make_map(CUtensorMap *map, const void *base, int dtype, uint64_t row_elems,
   return true;
 }
 
-template <typename T, int H, int GP, int N, int SK, int SV, bool CH = false, int D2 = 1>
+template <typename T, bool RP, int H, int GP, int N, int SK, int SV, bool CH = false, int D2 = 1>
 cudaError_t launch_tc(const CUtensorMap &mk, const CUtensorMap &mv, const TcParams &tp, int grid,
                       cudaStream_t stream) {
-  using L = SmemLayout<N, SK, SV, D2>;
+  using L = SmemLayout<N, SK, SV, D2, RP>;
   static_assert(L::kAlloc <= 227 * 1024, "dynamic shared memory above the sm_100 per-block limit");
-  auto kern = decode_tc_kernel<T, H, GP, N, SK, SV, CH, D2>;
+  auto kern = decode_tc_kernel<T, H, GP, N, SK, SV, CH, D2, RP>;
   // The shared-memory opt-in is a per-device function attribute: set it once
   // per device (outside any stream capture that follows the first call).
   static std::atomic<uint64_t> attr_done{0};
@@ -1585,28 +1566,30 @@ cudaError_t launch_tc(const CUtensorMap &mk, const CUtensorMap &mv, const TcPara
   return cudaLaunchKernelEx(&cfg, kern, mk, mv, tp);
 }
 
-template <typename T>
+// RP: RoPE fused (cos / sin given), a separate instantiation so that the
+// plain kernel carries none of the rotation code.
+template <typename T, bool RP>
 cudaError_t dispatch_tc(const TcPlan &pl, const CUtensorMap &mk, const CUtensorMap &mv, const TcParams &tp,
                         cudaStream_t stream) {
   if (pl.D2 == 2) {
     // head_dim 256: 3 K + 2 V ring stages of half a tile each (shared memory)
-    if (pl.chunks > 1) return launch_tc<T, 1, 16, 16, 3, 2, true, 2>(mk, mv, tp, pl.grid, stream);
-    if (pl.GP == 8) return launch_tc<T, 1, 8, 16, 3, 2, false, 2>(mk, mv, tp, pl.grid, stream);
-    if (pl.GP == 16) return launch_tc<T, 1, 16, 16, 3, 2, false, 2>(mk, mv, tp, pl.grid, stream);
+    if (pl.chunks > 1) return launch_tc<T, RP, 1, 16, 16, 3, 2, true, 2>(mk, mv, tp, pl.grid, stream);
+    if (pl.GP == 8) return launch_tc<T, RP, 1, 8, 16, 3, 2, false, 2>(mk, mv, tp, pl.grid, stream);
+    if (pl.GP == 16) return launch_tc<T, RP, 1, 16, 16, 3, 2, false, 2>(mk, mv, tp, pl.grid, stream);
     return cudaErrorInvalidValue;
   }
   if (pl.chunks > 1) {
-    if (pl.H == 1 && pl.GP == 32) return launch_tc<T, 1, 32, 32, 2, 2, true>(mk, mv, tp, pl.grid, stream);
-    if (pl.H == 2 && pl.GP == 16) return launch_tc<T, 2, 16, 32, 2, 2, true>(mk, mv, tp, pl.grid, stream);
-    if (pl.H == 4 && pl.GP == 8) return launch_tc<T, 4, 8, 32, 2, 2, true>(mk, mv, tp, pl.grid, stream);
+    if (pl.H == 1 && pl.GP == 32) return launch_tc<T, RP, 1, 32, 32, 2, 2, true>(mk, mv, tp, pl.grid, stream);
+    if (pl.H == 2 && pl.GP == 16) return launch_tc<T, RP, 2, 16, 32, 2, 2, true>(mk, mv, tp, pl.grid, stream);
+    if (pl.H == 4 && pl.GP == 8) return launch_tc<T, RP, 4, 8, 32, 2, 2, true>(mk, mv, tp, pl.grid, stream);
     return cudaErrorInvalidValue;
   }
-  if (pl.H == 2 && pl.GP == 8) return launch_tc<T, 2, 8, 16, 3, 3>(mk, mv, tp, pl.grid, stream);
-  if (pl.H == 2 && pl.GP == 16) return launch_tc<T, 2, 16, 32, 2, 2>(mk, mv, tp, pl.grid, stream);
-  if (pl.H == 1 && pl.GP == 8) return launch_tc<T, 1, 8, 16, 3, 3>(mk, mv, tp, pl.grid, stream);
-  if (pl.H == 1 && pl.GP == 16) return launch_tc<T, 1, 16, 16, 3, 3>(mk, mv, tp, pl.grid, stream);
-  if (pl.H == 1 && pl.GP == 32) return launch_tc<T, 1, 32, 32, 2, 2>(mk, mv, tp, pl.grid, stream);
-  if (pl.H == 4 && pl.GP == 8) return launch_tc<T, 4, 8, 32, 2, 2>(mk, mv, tp, pl.grid, stream);
+  if (pl.H == 2 && pl.GP == 8) return launch_tc<T, RP, 2, 8, 16, 3, 3>(mk, mv, tp, pl.grid, stream);
+  if (pl.H == 2 && pl.GP == 16) return launch_tc<T, RP, 2, 16, 32, 2, 2>(mk, mv, tp, pl.grid, stream);
+  if (pl.H == 1 && pl.GP == 8) return launch_tc<T, RP, 1, 8, 16, 3, 3>(mk, mv, tp, pl.grid, stream);
+  if (pl.H == 1 && pl.GP == 16) return launch_tc<T, RP, 1, 16, 16, 3, 3>(mk, mv, tp, pl.grid, stream);
+  if (pl.H == 1 && pl.GP == 32) return launch_tc<T, RP, 1, 32, 32, 2, 2>(mk, mv, tp, pl.grid, stream);
+  if (pl.H == 4 && pl.GP == 8) return launch_tc<T, RP, 4, 8, 32, 2, 2>(mk, mv, tp, pl.grid, stream);
   return cudaErrorInvalidValue;
 }
 
@@ -1696,8 +1679,13 @@ int tc_launch(DecodeParams &p, int dtype, void *workspace, size_t workspace_byte
     tp.cs_st = append->cs_st;
   }
   tp.p = p;
-  cudaError_t e = dtype == PAGEDKV_DTYPE_BF16 ? dispatch_tc<__nv_bfloat16>(pl, mk, mv, tp, stream)
-                                  : dispatch_tc<__half>(pl, mk, mv, tp, stream);
+  const bool rope = tp.cos != nullptr;
+  cudaError_t e;
+  if (dtype == PAGEDKV_DTYPE_BF16)
+    e = rope ? dispatch_tc<__nv_bfloat16, true>(pl, mk, mv, tp, stream)
+             : dispatch_tc<__nv_bfloat16, false>(pl, mk, mv, tp, stream);
+  else
+    e = rope ? dispatch_tc<__half, true>(pl, mk, mv, tp, stream) : dispatch_tc<__half, false>(pl, mk, mv, tp, stream);
   if (e != cudaSuccess) {
     *error = std::string("tensor-core decode launch: ") + cudaGetErrorString(e);
     return PAGEDKV_ERR_CUDA;
