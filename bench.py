@@ -703,16 +703,21 @@ def _sum_over_ranks(dist, value: float, device=None) -> float:
     return float(t.item())
 
 
-def _read_traffic(kernel: str, workload: str) -> int | None:
+def _read_traffic(kernel: str, workload: str, rope: bool = False) -> int | None:
     """ncu DRAM bytes per launch of ``kernel`` on ``workload`` from
     profiles/traffic.json (keys "kernel" for config 2, "kernel:workload" for
-    the others), or None where no capture exists."""
+    the others; the RoPE instantiation under "kernel:rope" for config 2 and
+    "kernel:workload_rope" for the others), or None where no capture exists."""
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
         return None
     try:
         data = json.loads(p.read_text())
-        entry = data.get(kernel if workload == "cfg2" else f"{kernel}:{workload}")
+        if rope:
+            key = f"{kernel}:rope" if workload == "cfg2" else f"{kernel}:{workload}_rope"
+        else:
+            key = kernel if workload == "cfg2" else f"{kernel}:{workload}"
+        entry = data.get(key)
         return int(entry["bytes_per_launch"]) if entry else None
     except (ValueError, KeyError, TypeError):
         return None
@@ -990,7 +995,7 @@ def run_ours(args) -> None:
     roof_bytes = (wl.attention_unique_bytes() if shared_prefix else a_bytes) + append_b
     achieved = roof_bytes / (per_launch_ms * 1e-3) / 1e9
     kernel_name = f"decode_{family}"
-    traffic = _read_traffic(kernel_name, wl.name)
+    traffic = _read_traffic(kernel_name, wl.name, args.rope)
     launches_per_step = L * launches_attn + (1 if pairs is not None else 0)
     if dist:
         dist.barrier()
