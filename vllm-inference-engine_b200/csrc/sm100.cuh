@@ -57,9 +57,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Bounded wait on the phase with the given parity. Gives up after timeout_ns
 // (or as soon as *abort is set by another role), sets *abort and returns
 // false; the caller then unwinds to the kernel's teardown instead of hanging.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort,
-                                          uint64_t timeout_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Only the first try is inlined: the polling loop with its timer and abort
+// checks is one out-of-line function shared by every wait site, which keeps
+// the warp roles' loops small (the decode kernel has dozens of wait sites;
+// inlined, their loops made up a large share of its code and slowed the
+// short-context and head_dim-128 launches by 10-13 %).
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int *abort,
+                                           uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
   while (true) {
@@ -72,6 +76,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort,
+                                          uint64_t timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, abort, timeout_ns);
 }
 
 // ---- cp.async (4-byte global -> shared copies, completion per thread) -------------
