@@ -90,9 +90,17 @@ __device__ unsigned long long g_trace[kTraceCtas][7][kTraceSlots];
 // Timeline of the last kTraceRecs CTA runs, indexed by a ticket every CTA
 // takes at entry (launch = ticket / grid: a launch's CTAs all start before
 // the next launch may): ticket, %smid, entry, after the dependency wait,
-// first S tile ready, exit (globaltimer ns).
+// first S tile ready, exit, then the start-up steps: range prologue done,
+// K producer's first block-table window landed, its first TMA issued, S
+// issuer's first Q ready, its first K tile landed, the K producer's role
+// entry, its first two windows issued, its first Q issued, and within the
+// role entry: descriptor prefetch and policy done, first window piece walked,
+// first window issued, then a walker probe: the same walker step twice from
+// one call site, then once from another. Columns 6 on are SM clock64 cycles,
+// column 20 the clock64 cycle right after the dependency wait.
 constexpr int kTraceRecs = 160 * 48;
-__device__ unsigned long long g_tl[kTraceRecs][6];
+constexpr int kTraceCols = 21;  // columns 17-19 unused
+__device__ unsigned long long g_tl[kTraceRecs][kTraceCols];
 __device__ unsigned long long g_tl_ctr;
 #define PKV_TW(slot, expr)             \
   ([&]() {                              \
@@ -109,11 +117,13 @@ __device__ unsigned long long g_tl_ctr;
   } while (0)
 #define PKV_TADD(slot, v) (tw[slot] += (v))
 #define PKV_STAMP(var) const uint64_t var = clock64()
+#define PKV_TL(col) (g_tl[misc->tl_ticket % kTraceRecs][col] = clock64())
 #else
 #define PKV_TW(slot, expr) (expr)
 #define PKV_TV(slot, stmt) stmt
 #define PKV_TADD(slot, v) ((void)0)
 #define PKV_STAMP(var) ((void)0)
+#define PKV_TL(col) ((void)0)
 #endif
 
 struct TcParams {
@@ -651,12 +661,12 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     mbar_init(mma_done, 2);  // one commit from each MMA issuer
     for (int s = 0; s < kRescaleSlots; ++s) mbar_init(a_full(s), 1);  // one softmax thread
     for (int s = 0; s < kQSlots; ++s) {
-      mbar_init(q_full(s), 32);  // every K-producer lane, when its Q copies land
+      mbar_init(q_full(s), 32);  // every lane of the staging warp, when its Q copies land
       mbar_init(q_empty(s), 1);  // MMA commit after the piece's last S
     }
     for (int s = 0; s < kLSlots; ++s) mbar_init(l_full(s), 4);  // lane 0 of each softmax warp
     if (RP)
-      for (int s = 0; s < kQSlots; ++s) mbar_init(q_rot(s), 32);  // every K-producer lane, once rotated
+      for (int s = 0; s < kQSlots; ++s) mbar_init(q_rot(s), 32);  // every lane of the rotating warp
     misc->abort = 0;
     fence_mbarrier_init();
   }
@@ -665,12 +675,51 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     tmem_relinquish();
   }
 
-  // Everything above touched only shared memory and TMEM, so it overlaps the
-  // tail of the preceding kernel; global inputs are read only after it ends.
+  // The launch's small inputs are pulled into L2 while the preceding kernel
+  // finishes, spread over the CTAs: the sequence lengths (every CTA scans
+  // them), the block tables (the first tiles' ids are read right after the
+  // scan) and q. A prefetch reads nothing into the SM, and every write of the
+  // preceding kernel has reached L2 before the wait below returns, so no
+  // value read after it can be stale. Each range ends at its last valid
+  // element, so every line prefetched holds some of the buffer.
+  {
+    const int64_t nthr = (int64_t)gridDim.x * kThreads;
+    const int64_t t = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+    auto lines = [](const void *base, int64_t bytes) -> int64_t {
+      const uint64_t a0 = reinterpret_cast<uint64_t>(base);
+      return bytes > 0 ? (int64_t)(((a0 + bytes - 1) >> 7) - (a0 >> 7) + 1) : 0;
+    };
+    auto line_addr = [](const void *base, int64_t i) {
+      return reinterpret_cast<const void *>(((reinterpret_cast<uint64_t>(base) >> 7) + i) << 7);
+    };
+    const int64_t ns = p.num_seqs;
+    const int64_t l_lens = p.lens ? lines(p.lens, ns * 4) : 0;
+    const int64_t bt_bytes = ns > 0 ? ((ns - 1) * p.bt_s + p.max_blocks) * 4 : 0;
+    const int64_t l_bt = lines(p.bt, bt_bytes);
+    const int64_t q_bytes = ns > 0 ? ((ns - 1) * p.q_ss + (int64_t)(p.hq - 1) * p.q_sh + D) * (int64_t)sizeof(T) : 0;
+    const int64_t l_q = lines(p.q, q_bytes);
+    if (l_lens + l_bt + l_q <= (int64_t)1 << 16) {  // at most 8 MB
+      for (int64_t i = t; i < l_lens + l_bt + l_q; i += nthr) {
+        if (i < l_lens)
+          prefetch_l2(line_addr(p.lens, i));
+        else if (i < l_lens + l_bt)
+          prefetch_l2(line_addr(p.bt, i - l_lens));
+        else
+          prefetch_l2(line_addr(p.q, i - l_lens - l_bt));
+      }
+    }
+  }
+
+  // Everything above touched only shared memory and TMEM (and issued L2
+  // prefetches), so it overlaps the tail of the preceding kernel; global
+  // inputs are read only after it ends.
   grid_dependency_wait();
   grid_launch_dependents();
 #ifdef PAGEDKV_TRACE
-  if (threadIdx.x == 0) g_tl[misc->tl_ticket % kTraceRecs][3] = globaltimer_ns();
+  if (threadIdx.x == 0) {
+    g_tl[misc->tl_ticket % kTraceRecs][3] = globaltimer_ns();
+    PKV_TL(20);
+  }
 #endif
 
   // ---- prologue: total cost units and the start of this CTA's range ----------
@@ -757,6 +806,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (threadIdx.x == 0) PKV_TL(6);
   const uint32_t tmem = misc->tmem;
   const int64_t U_total = misc->total;
   const int64_t G = misc->grid;
@@ -772,6 +822,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     // piece ahead (cp.async, completing on the slot's q_full barrier). A
     // stage freed by the consumer is refilled without a round trip to L2.
     const bool is_k = warp == 0;
+    if (is_k && lane == 0) PKV_TL(11);
     const CUtensorMap *tmap = is_k ? &tmap_k : &tmap_v;
     const int nst = is_k ? SK : SV;
     const uint32_t ring = sbase + (is_k ? L::kOffK : L::kOffV);
@@ -779,6 +830,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     // K/V rows are read once (evict first), or once per query-head chunk when
     // the group is split, where the next chunk's segment re-reads them from L2.
     const uint64_t policy = CH ? l2_policy_evict_normal() : l2_policy_evict_first();
+    if (is_k && lane == 0) PKV_TL(14);
     const int bpt = kTile / p.block_size;  // blocks per tile: 1..16, divides 32
     constexpr int kQChunks = 16 * N * D2 / 32;  // Q 16-byte chunks per lane
     int stage = 0;
@@ -787,43 +839,14 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     int issued = 0;
     bool ok = true;
 
-    // Window k (k = 0, 1, ... over this CTA's pieces in order; window w of a
-    // piece q covers its logical blocks q.t0 / block_size + 32 w + [0, 32))
-    // lands in slot k % 3; lanes past the piece's last block copy nothing.
-    const uint32_t win_base = sbase + L::kOffBtWin + (is_k ? 0u : 3u * 32u * 4u);
-    const int32_t *win = reinterpret_cast<const int32_t *>(smem + L::kOffBtWin) + (is_k ? 0 : 3 * 32);
-    Walker gwalk = walk;  // generator of the window sequence
-    Piece gp;
-    bool gvalid = gwalk.next(tp, gp);
-    int gw = 0;
-    uint32_t gk = 0;  // windows issued
-    auto issue_window = [&]() {
-      if (gvalid) {
-        const int lb = gp.t0 / p.block_size + 32 * gw + lane;
-        const int need = (gp.t1 + p.block_size - 1) / p.block_size;
-        const bool in = lb < need;
-        const int32_t *src = in ? p.bt + (int64_t)gp.seq * p.bt_s + lb : p.bt;
-        cp_async_4(win_base + ((gk % 3u) * 32u + lane) * 4u, src, in ? 4u : 0u);
-        if (++gw == (gp.ntiles * bpt + 31) / 32) {
-          gw = 0;
-          gvalid = gwalk.next(tp, gp);
-        }
-      }
-      cp_async_commit();  // possibly empty: one group per window slot, always
-      ++gk;
-    };
-    issue_window();
-    issue_window();
-    uint32_t wk = 0;  // windows consumed
-
     // Q of piece q into ring slot i as the block-diagonal B operand
     // [N rows x 128], K-major SW128; padding rows and halves are zero-filled.
     // Q of each piece goes into a Q ring slot one piece ahead by cp.async,
     // completing on the slot's q_full barrier. With RoPE the cos / sin rows
     // come along (same barrier), and this warp rotates the landed Q in place
-    // once the piece's first tile is issued (the whole first ring fill for
-    // the CTA's first piece), where it would otherwise wait for a free stage;
-    // q_rot then hands it to the S issuer.
+    // once the piece's first tile is issued, where it would otherwise wait
+    // for a free stage; q_rot then hands it to the S issuer. (The CTA's first
+    // piece's Q is staged and rotated by correction warp 7.)
     auto q_issue = [&](const Piece &q, uint32_t i) -> bool {
       if (!PKV_TW(0, mbar_wait(q_empty(i), ring_parity(i, kQSlots) ^ 1u, abort_flag, kTimeoutNs))) return false;
       stage_q<T, H, GP, N, D, D2>(tp, q, nch, sbase + L::kOffQ + (i % kQSlots) * L::kQBytes, lane);
@@ -842,10 +865,110 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       return true;
     };
 
+
+    // First ring fill of the CTA's first piece, issued straight from the range
+    // prologue's results (its sequence, head group, first tile, length and the
+    // range end) with every lane computing its own loads: no walker step and
+    // no block-table window stand between the dependency release and the first
+    // tiles in flight (the piece's Q is staged by correction warp 7). The loop
+    // below starts the first piece at tile `pre`.
+    int pre = 0;
+    {
+      const int s0 = misc->seq0, len0 = misc->len0, off0 = misc->off0, hg0 = misc->hg0;
+      int lim = 0;  // the first piece is tiles [off0, lim) of its segment
+      if (s0 < p.num_seqs) {
+        // the first step of Walker::next from the range start
+        const int64_t room = misc->hi - misc->u0 - kSegUnits;
+        const int64_t fit = room < kTileUnits ? 0 : room / kTileUnits;
+        const int nt0 = tiles_of(len0);
+        lim = fit < nt0 ? (int)fit : nt0;
+        pre = min(lim - off0, nst / D2);
+        if (pre < 0) pre = 0;
+      }
+      if (pre > 0) {
+        const int t1 = min(len0, lim * kTile);  // the piece's token end, as Walker::next sets it
+        const int need = (t1 + p.block_size - 1) / p.block_size;
+        const int lb0 = off0 * bpt;  // the piece's first logical block
+        // block ids of the pre-issued tiles: entry e = j * bpt + b (< 48) is
+        // loaded by lane e % 32 into blk[e / 32]
+        int32_t blk[2] = {-1, -1};
+#pragma unroll
+        for (int k2 = 0; k2 < 2; ++k2) {
+          const int e = lane + 32 * k2;
+          if (e < pre * bpt && lb0 + e < need) blk[k2] = __ldg(p.bt + (int64_t)s0 * p.bt_s + lb0 + e);
+        }
+        const int x0 = hg0 / nch * 128 * D2;  // this tile row's first element
+        for (int st = 0; st < pre * D2; ++st) {  // first use of each stage: nothing to wait for
+          const int j = st / D2, sub = st - j * D2;
+          const uint32_t full = is_k ? kfull(st) : vfull(st);
+          if (lane == 0) mbar_arrive_expect_tx(full, kOperandBytes);
+          __syncwarp();
+          const int h = lane >= bpt ? 1 : 0;
+          const int b = lane - h * bpt;
+          const int e = j * bpt + (lane < 2 * bpt ? b : 0);
+          const int32_t v0 = __shfl_sync(0xffffffffu, blk[0], e & 31);
+          const int32_t v1 = __shfl_sync(0xffffffffu, blk[1], e & 31);
+          if (lane < 2 * bpt) {
+            const int32_t id = e < 32 ? v0 : v1;
+            int32_t y = tp.oob_row;  // out of range: TMA fills zeros, reads nothing
+            if (lb0 + e < need) {
+              if (id >= 0 && id < p.num_blocks) {
+                y = id * p.block_size;
+              } else if (is_k && h == 0 && sub == 0) {
+                set_error(p.err, PAGEDKV_EFLAG_BLOCK_ID_RANGE);
+              }
+            }
+            const uint32_t dst = ring + st * kOperandBytes + h * kHalfBytes + b * p.block_size * 128;
+            tma_load_2d(dst, tmap, x0 + sub * 128 + h * 64, y, full, policy);
+          }
+        }
+        if (is_k && lane == 0) PKV_TL(8);
+        issued = pre * D2;
+        stage = issued;
+        if (stage == nst) {
+          stage = 0;
+          sphase ^= 1u;
+        }
+      }
+    }
+
+    // Window k (k = 0, 1, ... over this CTA's pieces in order; window w of a
+    // piece q covers its logical blocks q.t0 / block_size + 32 w + [0, 32))
+    // lands in slot k % 3; lanes past the piece's last block copy nothing.
+    const uint32_t win_base = sbase + L::kOffBtWin + (is_k ? 0u : 3u * 32u * 4u);
+    const int32_t *win = reinterpret_cast<const int32_t *>(smem + L::kOffBtWin) + (is_k ? 0 : 3 * 32);
+    Walker gwalk = walk;  // generator of the window sequence
+    Piece gp;
+    bool gvalid = gwalk.next(tp, gp);
+    if (is_k && lane == 0) PKV_TL(15);
+    int gw = 0;
+    uint32_t gk = 0;  // windows issued
+    auto issue_window = [&]() {
+      if (gvalid) {
+        const int lb = gp.t0 / p.block_size + 32 * gw + lane;
+        const int need = (gp.t1 + p.block_size - 1) / p.block_size;
+        const bool in = lb < need;
+        const int32_t *src = in ? p.bt + (int64_t)gp.seq * p.bt_s + lb : p.bt;
+        cp_async_4(win_base + ((gk % 3u) * 32u + lane) * 4u, src, in ? 4u : 0u);
+        if (++gw == (gp.ntiles * bpt + 31) / 32) {
+          gw = 0;
+          gvalid = gwalk.next(tp, gp);
+        }
+      }
+      cp_async_commit();  // possibly empty: one group per window slot, always
+      ++gk;
+    };
+    issue_window();
+    if (is_k && lane == 0) PKV_TL(16);
+    issue_window();
+    if (is_k && lane == 0) PKV_TL(12);
+    uint32_t wk = 0;  // windows consumed
+
     Piece pc;
     bool have = walk.next(tp, pc);
-    uint32_t qcur = qi;  // Q slot index of pc
-    if (have && is_k) ok = q_issue(pc, qi++);
+    uint32_t qcur = 0;  // Q slot index of pc
+    qi = 1;             // the first piece's Q (slot 0) is correction warp 7's
+    if (is_k && lane == 0) PKV_TL(13);
     bool first_piece = true;
     while (ok && have) {
       Piece nx;
@@ -853,8 +976,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       // The next piece's Q, landing while this piece's tiles stream.
       const uint32_t qnx = qi;
       if (is_k && have_nx && !q_issue(nx, qi++)) break;
-      // RoPE: tiles of this piece issued before its Q is rotated
-      const int rot_at = RP && is_k ? min(pc.ntiles, first_piece ? nst / D2 : 1) : 0;
+      // tiles of this piece issued by the first ring fill above
+      const int skip = first_piece ? pre : 0;
+      // RoPE: tiles of this piece issued before its Q is rotated (the first
+      // piece's Q is rotated by correction warp 7)
+      const int rot_at = RP && is_k && !first_piece ? 1 : 0;
       first_piece = false;
       const int lb0 = pc.t0 / p.block_size;
       const int need = (pc.t1 + p.block_size - 1) / p.block_size;
@@ -868,10 +994,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           issue_window();
           cp_async_wait<2>();
           __syncwarp();
+          if (is_k && issued == 0 && lane == 0) PKV_TL(7);
         }
         const uint32_t slot = wk % 3u;
         if (wofs + bpt >= 32 || j + 1 == pc.ntiles) ++wk;  // last tile of this window
-        for (int sub = 0; sub < D2; ++sub) {  // one ring stage per 128-element sub-row
+        for (int sub = 0; sub < D2 && j >= skip; ++sub) {  // one ring stage per 128-element sub-row
           if (!PKV_TW(1, mbar_wait(is_k ? kempty(stage) : vempty(stage), sphase ^ 1u, abort_flag, kTimeoutNs))) {
             ok = false;
             break;
@@ -896,6 +1023,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
             const uint32_t dst = ring + stage * kOperandBytes + h * kHalfBytes + b * p.block_size * 128;
             tma_load_2d(dst, tmap, x0 + sub * 128 + h * 64, y, full, policy);
           }
+          if (is_k && issued == 0 && lane == 0) PKV_TL(8);
           ++issued;
           if (++stage == nst) {
             stage = 0;
@@ -946,6 +1074,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       // Q landed (cp.async), and with RoPE the K producer rotated it
       const uint32_t qbar = RP ? q_rot(qi) : q_full(qi);
       if (!PKV_TW(0, mbar_wait(qbar, ring_parity(qi, kQSlots), abort_flag, kTimeoutNs))) break;
+      if (qi == 0 && lane == 0) PKV_TL(9);
       const uint32_t qbuf = sbase + L::kOffQ + (qi % kQSlots) * L::kQBytes;
       fence_proxy_async_smem();  // Q written through the generic proxy; the MMA reads it
       for (int j = 0; j < pc.ntiles; ++j) {
@@ -954,6 +1083,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         const uint4 xk = patch ? append_chunk<T, D, RP>(row_cur, true, lane) : row_cur.x;
         for (int sub = 0; sub < D2; ++sub) {  // S sums the sub-rows' products
           if (!PKV_TW(1, mbar_wait(kfull(kst), kph, abort_flag, kTimeoutNs))) { ok = false; break; }
+          if (gt == 0 && sub == 0 && lane == 0) PKV_TL(10);
           if (sub == 0 && !PKV_TW(2, mbar_wait(bar2(1, b), ((gt >> 1) & 1u) ^ 1u, abort_flag, kTimeoutNs))) {
             ok = false;
             break;
@@ -1250,6 +1380,24 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 
     Piece pc;
     bool have = walk.next(tp, pc);
+    // The CTA's first Q (with RoPE, its cos / sin rows too) into Q slot 0 by
+    // correction warp 7, idle until the first tile is folded, while the
+    // producers issue the first ring fill; with RoPE it also rotates it once
+    // landed. (The slot's first use: nothing to wait for.)
+    if (warp == 7 && have) {
+      stage_q<T, H, GP, N, D, D2>(tp, pc, nch, sbase + L::kOffQ, lane);
+      if constexpr (RP) stage_cs<T, D, D2>(tp, pc, sbase + L::kOffCS, lane);
+      cp_async_mbar_arrive(q_full(0));
+      if constexpr (RP) {
+        // every lane takes part in the rotation's shuffles, or none does
+        const bool landed = mbar_wait(q_full(0), 0u, abort_flag, kTimeoutNs);
+        if (__all_sync(0xffffffffu, landed)) {
+          rotate_q<T, H, GP, N, D, D2>(p, pc, nch, sbase + L::kOffQ, sbase + L::kOffCS, lane);
+          fence_proxy_async_smem();  // the MMA reads the rotated operand through the async proxy
+          mbar_arrive(q_rot(0));
+        }
+      }
+    }
 
     // Sequences of length 0 own no tiles: CTA (seq % grid) writes their zeros.
     for (int s = blockIdx.x; s < p.num_seqs; s += gridDim.x) {
@@ -1381,6 +1529,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
       pc = nx;
       have = have_nx;
     }
+    if (warp == 7) cp_async_wait<0>();  // the first Q's copies (landed on the normal path)
   }
 
   // ---------------------------------------------------------------- teardown

@@ -106,6 +106,12 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // ---- TMA -------------------------------------------------------------------------
+// L2 prefetch of the 128-byte line holding addr: the line is brought into
+// L2, nothing is read into the SM.
+__device__ __forceinline__ void prefetch_l2(const void *addr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(addr)) : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
