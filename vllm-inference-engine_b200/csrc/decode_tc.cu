@@ -99,7 +99,7 @@ __device__ unsigned long long g_trace[kTraceCtas][7][kTraceSlots];
 // one call site, then once from another. Columns 6 on are SM clock64 cycles,
 // column 20 the clock64 cycle right after the dependency wait.
 constexpr int kTraceRecs = 160 * 48;
-constexpr int kTraceCols = 21;  // columns 17-19 unused
+constexpr int kTraceCols = 21;  // columns 17-19: first ring fill sized, its block ids landed, its first stage issued
 __device__ unsigned long long g_tl[kTraceRecs][kTraceCols];
 __device__ unsigned long long g_tl_ctr;
 #define PKV_TW(slot, expr)             \
@@ -885,6 +885,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         pre = min(lim - off0, nst / D2);
         if (pre < 0) pre = 0;
       }
+      if (is_k && lane == 0) PKV_TL(17);
       if (pre > 0) {
         const int t1 = min(len0, lim * kTile);  // the piece's token end, as Walker::next sets it
         const int need = (t1 + p.block_size - 1) / p.block_size;
@@ -908,6 +909,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           const int e = j * bpt + (lane < 2 * bpt ? b : 0);
           const int32_t v0 = __shfl_sync(0xffffffffu, blk[0], e & 31);
           const int32_t v1 = __shfl_sync(0xffffffffu, blk[1], e & 31);
+          if (is_k && st == 0 && lane == 0 && (v0 | v1) != 0x7fffffff) PKV_TL(18);
           if (lane < 2 * bpt) {
             const int32_t id = e < 32 ? v0 : v1;
             int32_t y = tp.oob_row;  // out of range: TMA fills zeros, reads nothing
@@ -921,6 +923,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
             const uint32_t dst = ring + st * kOperandBytes + h * kHalfBytes + b * p.block_size * 128;
             tma_load_2d(dst, tmap, x0 + sub * 128 + h * 64, y, full, policy);
           }
+          if (is_k && st == 0 && lane == 0) PKV_TL(19);
         }
         if (is_k && lane == 0) PKV_TL(8);
         issued = pre * D2;
@@ -971,11 +974,13 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     if (is_k && lane == 0) PKV_TL(13);
     bool first_piece = true;
     while (ok && have) {
+      PKV_STAMP(t_top0);
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
       // The next piece's Q, landing while this piece's tiles stream.
       const uint32_t qnx = qi;
       if (is_k && have_nx && !q_issue(nx, qi++)) break;
+      PKV_TADD(4, clock64() - t_top0);
       // tiles of this piece issued by the first ring fill above
       const int skip = first_piece ? pre : 0;
       // RoPE: tiles of this piece issued before its Q is rotated (the first
@@ -990,10 +995,12 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
         if (wofs == 0) {
           // Entering a window: stage the one two ahead (into the slot of the
           // window just finished), then wait for this one.
+          PKV_STAMP(t_win0);
           __syncwarp();
           issue_window();
           cp_async_wait<2>();
           __syncwarp();
+          PKV_TADD(2, clock64() - t_win0);
           if (is_k && issued == 0 && lane == 0) PKV_TL(7);
         }
         const uint32_t slot = wk % 3u;
@@ -1003,6 +1010,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
             ok = false;
             break;
           }
+          PKV_STAMP(t_iss0);
           const uint32_t full = is_k ? kfull(stage) : vfull(stage);
           if (lane == 0) mbar_arrive_expect_tx(full, kOperandBytes);
           __syncwarp();
@@ -1023,6 +1031,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
             const uint32_t dst = ring + stage * kOperandBytes + h * kHalfBytes + b * p.block_size * 128;
             tma_load_2d(dst, tmap, x0 + sub * 128 + h * 64, y, full, policy);
           }
+          PKV_TADD(3, clock64() - t_iss0);
           if (is_k && issued == 0 && lane == 0) PKV_TL(8);
           ++issued;
           if (++stage == nst) {
