@@ -42,7 +42,7 @@
 //     lower-numbered blocks, so a combining CTA only ever waits on CTAs
 //     dispatched before it — no second launch, equal tiles per SM.
 //   * Warp roles (12 warps): 0 K-tile TMA producer (also copies each piece's
-//     Q; with RoPE it rotates the landed Q in place), 6 V-tile TMA producer,
+//     Q; with RoPE the V producer rotates it in place), 6 V-tile TMA producer,
 //     1 S-MMA issuer (TMEM owner), 11 O-MMA issuer, 2-5 softmax, 7-10
 //     correction / epilogue. With the fused decode append, the two MMA
 //     issuers patch the new K / V row into the landed tile (and the pool).
@@ -843,10 +843,10 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
     // [N rows x 128], K-major SW128; padding rows and halves are zero-filled.
     // Q of each piece goes into a Q ring slot one piece ahead by cp.async,
     // completing on the slot's q_full barrier. With RoPE the cos / sin rows
-    // come along (same barrier), and this warp rotates the landed Q in place
-    // once the piece's first tile is issued, where it would otherwise wait
-    // for a free stage; q_rot then hands it to the S issuer. (The CTA's first
-    // piece's Q is staged and rotated by correction warp 7.)
+    // come along (same barrier), and the V producer rotates the landed Q in
+    // place at the top of the piece before; q_rot then hands it to the S
+    // issuer. (The CTA's first piece's Q is staged and rotated by correction
+    // warp 7.)
     auto q_issue = [&](const Piece &q, uint32_t i) -> bool {
       if (!PKV_TW(0, mbar_wait(q_empty(i), ring_parity(i, kQSlots) ^ 1u, abort_flag, kTimeoutNs))) return false;
       stage_q<T, H, GP, N, D, D2>(tp, q, nch, sbase + L::kOffQ + (i % kQSlots) * L::kQBytes, lane);
@@ -969,23 +969,28 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
 
     Piece pc;
     bool have = walk.next(tp, pc);
-    uint32_t qcur = 0;  // Q slot index of pc
-    qi = 1;             // the first piece's Q (slot 0) is correction warp 7's
+    qi = 1;           // the first piece's Q (slot 0) is correction warp 7's
     if (is_k && lane == 0) PKV_TL(13);
     bool first_piece = true;
+    uint32_t vq = 1;  // Q slot of the next piece (V producer, RoPE)
     while (ok && have) {
       PKV_STAMP(t_top0);
       Piece nx;
       const bool have_nx = walk.next(tp, nx);
       // The next piece's Q, landing while this piece's tiles stream.
-      const uint32_t qnx = qi;
       if (is_k && have_nx && !q_issue(nx, qi++)) break;
       PKV_TADD(4, clock64() - t_top0);
       // tiles of this piece issued by the first ring fill above
       const int skip = first_piece ? pre : 0;
-      // RoPE: tiles of this piece issued before its Q is rotated (the first
-      // piece's Q is rotated by correction warp 7)
-      const int rot_at = RP && is_k && !first_piece ? 1 : 0;
+      // RoPE: the V producer rotates the next piece's Q, which the K producer
+      // staged one piece ahead, at the top of each piece: it runs about two
+      // tiles ahead of the S issuer and is less loaded than the K producer,
+      // whose TMA issue paces short pieces. (The first piece's Q is staged and
+      // rotated by correction warp 7.)
+      if constexpr (RP) {
+        if (!is_k && have_nx && !q_rotate(nx, vq)) break;
+      }
+      ++vq;
       first_piece = false;
       const int lb0 = pc.t0 / p.block_size;
       const int need = (pc.t1 + p.block_size - 1) / p.block_size;
@@ -1040,15 +1045,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tmap_k,
           }
         }
         if (!ok) break;
-        if constexpr (RP) {
-          if (j + 1 == rot_at && !q_rotate(pc, qcur)) {
-            ok = false;
-            break;
-          }
-        }
       }
       pc = nx;
-      qcur = qnx;
       have = have_nx;
     }
     cp_async_wait<0>();  // no copy into shared memory outlives this role
