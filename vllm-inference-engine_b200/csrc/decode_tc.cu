@@ -397,6 +397,10 @@ __device__ __forceinline__ void rotate_q(const DecodeParams &p, const Piece &q, 
   constexpr uint32_t kSinOff = 128u * D2 * 2u;
 #pragma unroll
   for (int g = 0; g < kQChunks / kG; ++g) {
+    // Chunk g (and its partner g + kp) holds query columns 4 g mod N to
+    // 4 g mod N + 3 in every lane: when those are padding columns (past the
+    // H x GP real ones, zero-filled when staged), there is nothing to rotate.
+    if ((4 * g) % N >= H * GP) continue;
     uint4 xs[kG];
     bool in[kG];
     int dd[kG];
