@@ -100,3 +100,32 @@ def test_append_rope_in_place_unaligned_and_bad_slot(cuda_ready):
     pagedkv.kv_append_rope(q.to(cuda_ready), k.to(cuda_ready), v.to(cuda_ready), cos.to(cuda_ready),
                            sin.to(cuda_ready), dk, dv, bad.to(cuda_ready))
     assert pagedkv.read_error_flags(cuda_ready, clear=True) & _native.EFLAG_SLOT_RANGE
+
+
+@pytest.mark.parametrize("hq,hkv,d,n,fused,dtype", [
+    (14, 2, 64, 42_100, False, torch.float16),   # 5 rows per thread: groups of 5, 5, 5, 3
+    (14, 2, 64, 160_000, True, torch.bfloat16),  # a whole token per thread (18 rows)
+    (4, 2, 256, 40_000, False, torch.float16),   # a whole token per thread (8 rows)
+    (56, 8, 128, 5_300, True, torch.float16),    # 5 rows per thread, 72 rows: last group of 2
+])
+def test_append_rope_bulk_row_groups_vs_oracle(cuda_ready, hq, hkv, d, n, fused, dtype):
+    """Launches large enough that each thread takes several head rows of one
+    token (the rows-per-thread split of the bulk path), with padding and
+    ragged last groups: still bit-identical to the oracle."""
+    bs = 16
+    nb = (n + bs - 1) // bs + 4
+    q, k, v, cos, sin, kc, vc, slots = _case(cuda_ready, dtype, hq, hkv, d, nb=nb, bs=bs, n=n, fused=fused,
+                                             seed=n % 97)
+    slots[::1000] = -1  # padding tokens spread over the launch
+    qe = paged_ref.rope_ref(q, cos, sin)
+    ke = paged_ref.rope_ref(k, cos, sin)
+    live = slots >= 0
+    kce, vce = kc.clone(), vc.clone()
+    kce.view(-1, hkv, d)[slots[live]] = ke[live]
+    vce.view(-1, hkv, d)[slots[live]] = v[live]
+    dk, dv = kc.to(cuda_ready), vc.to(cuda_ready)
+    qo = pagedkv.kv_append_rope(q.to(cuda_ready), k.to(cuda_ready), v.to(cuda_ready), cos.to(cuda_ready),
+                                sin.to(cuda_ready), dk, dv, slots.to(cuda_ready))
+    assert torch.equal(_bits(qo), _bits(qe))
+    assert torch.equal(_bits(dk), _bits(kce)) and torch.equal(_bits(dv), _bits(vce))
+    assert pagedkv.read_error_flags(cuda_ready) == 0

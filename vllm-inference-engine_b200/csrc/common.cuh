@@ -82,27 +82,18 @@ template <> struct Elem<__nv_bfloat16> {
   __device__ __forceinline__ static __nv_bfloat16 from_float(float x) { return __float2bfloat16_rn(x); }
 };
 
-// One element of transformers' apply_rotary_pos_emb, x * cos + rotate_half(x)
-// * sin, rounded exactly as its 16-bit tensor ops: r(r(a * c) + r(b * s)),
-// where b is the rotation partner (negated for the first half of the head).
-// The fp32 products of 16-bit inputs are exact; each is rounded to T, the sum
-// is formed in fp32 and rounded to T by the caller's store. Shared by every
-// kernel that rotates, so their results are bit-identical.
-template <typename T>
-__device__ __forceinline__ float rope_elem(float a, float c, float b, float s) {
-  const float p1 = Elem<T>::to_float(Elem<T>::from_float(a * c));
-  const float p2 = Elem<T>::to_float(Elem<T>::from_float(b * s));
-  return p1 + p2;
-}
-
-// Eight elements of the same rotation on packed 16-bit pairs: r(r(x * c) +
-// r(xp' * s)) with xp' = xp negated when `lo` (the first half of the head).
-// Each op is one correctly rounded f16x2 / bf16x2 instruction (explicit .rn,
-// so nothing is contracted into an fma), which equals rope_elem: the product
-// of two 16-bit values is exact in fp32 (for bf16 products below fp32's
-// normal range the significand product has under 16 bits, so rounding it to
-// fp32 first changes no bf16 rounding), and an fp32 sum rounded to 16 bits is
-// the correctly rounded 16-bit sum (24 >= 2 * 11 + 2).
+// transformers' apply_rotary_pos_emb, x * cos + rotate_half(x) * sin, on
+// packed 16-bit pairs, rounded exactly as its 16-bit tensor ops:
+// r(r(x * c) + r(xp' * s)), with xp' the rotation partner xp, negated when
+// `lo` (the first half of the head). Each op is one correctly rounded f16x2 /
+// bf16x2 instruction (explicit .rn, so nothing is contracted into an fma),
+// which equals the fp32 form of the tensor ops (products rounded to T, summed
+// in fp32, the sum rounded to T): the product of two 16-bit values is exact
+// in fp32 (for bf16 products below fp32's normal range the significand
+// product has under 16 bits, so rounding it to fp32 first changes no bf16
+// rounding), and an fp32 sum rounded to 16 bits is the correctly rounded
+// 16-bit sum (24 >= 2 * 11 + 2). Shared by every kernel that rotates, so their
+// results are bit-identical.
 template <typename T>
 __device__ __forceinline__ uint32_t mul2_rn(uint32_t a, uint32_t b) {
   uint32_t r;
