@@ -131,6 +131,33 @@ def test_copy_blocks_out_of_range_flagged(cuda_ready):
     assert pagedkv.read_error_flags(cuda_ready, clear=True) & _native.EFLAG_COPY_RANGE
 
 
+def test_copy_blocks_out_of_range_pairs_between_valid_ones(cuda_ready):
+    """Out-of-range pairs in the middle of a launch are skipped and flagged;
+    every valid pair around them, on every layer, is still copied bit for bit."""
+    layers, nb, bs, hkv, d, pairs = 3, 600, 16, 2, 64, 250
+    g = torch.Generator().manual_seed(11)
+    ks = [torch.randn(nb, bs, hkv, d, generator=g).half() for _ in range(layers)]
+    vs = [torch.randn(nb, bs, hkv, d, generator=g).half() for _ in range(layers)]
+    perm = torch.randperm(nb, generator=g)
+    mapping = torch.stack([perm[:pairs], perm[pairs : 2 * pairs]], dim=1).contiguous()
+    bad = [7, 100, 101, 249]
+    mapping[7, 0] = nb + 3
+    mapping[100, 1] = -2
+    mapping[101, 0] = -1
+    mapping[249, 1] = nb
+    kd = [t.to(cuda_ready) for t in ks]
+    vd = [t.to(cuda_ready) for t in vs]
+    pagedkv.read_error_flags(cuda_ready, clear=True)
+    pagedkv.copy_blocks(kd, vd, mapping.to(cuda_ready))
+    assert pagedkv.read_error_flags(cuda_ready, clear=True) & _native.EFLAG_COPY_RANGE
+    good = np.array([i for i in range(pairs) if i not in bad])
+    kr = [_bits(t).copy() for t in ks]
+    vr = [_bits(t).copy() for t in vs]
+    paged_ref.copy_blocks_ref(kr, vr, mapping.numpy()[good])
+    for a, b in zip(kd + vd, kr + vr):
+        assert np.array_equal(_bits(a), b)
+
+
 def test_pool_larger_than_2gib_uses_64bit_offsets(cuda_ready):
     """A per-layer tensor above 2^31 bytes (config 5 pools are ~1.25 GB per
     tensor; this one is 2.3 GB): append, copy and attend at the far end."""
