@@ -129,6 +129,20 @@ def test_block_sizes_vs_oracle(cuda_ready, bs):
     _check_vs_oracle(cuda_ready, q, k, v, tables, lists, lens_t, 0.125)
 
 
+@pytest.mark.parametrize("d", [32, 64, 128, 256])
+@pytest.mark.parametrize("g,bs", [(1, 4), (2, 5), (4, 4), (7, 4), (12, 3)])
+def test_cuda_core_kernel_shapes_vs_oracle(cuda_ready, d, g, bs):
+    """Block sizes the tensor-core kernel does not take (below 8, not powers of
+    two) run on the CUDA-core kernel: every (head_dim, group width) variant of
+    it, contexts from one token to several splits, against the oracle."""
+    hkv = 2
+    lens = [1, bs, 3 * bs + 1, 130, 777, 2500]
+    q, k, v, tables, lists, lens_t = _random_case(7000 + 10 * d + g, len(lens), g * hkv, hkv, d, bs, lens)
+    _check_vs_oracle(cuda_ready, q, k, v, tables, lists, lens_t, 1 / math.sqrt(d))
+    assert pagedkv.last_decode_launch_info()[1] == "simt"
+    assert pagedkv.read_error_flags(cuda_ready) == 0
+
+
 def test_bf16_pool_vs_oracle(cuda_ready):
     lens = [5, 64, 300, 2048]
     q, k, v, tables, lists, lens_t = _random_case(77, 4, 14, 2, 64, 16, lens, dtype=torch.bfloat16)

@@ -12,6 +12,11 @@
 //   * q.k partial sums are reduced inside the lane group with xor shuffles,
 //   * every lane group keeps a private online softmax (m, l, acc) in base-2
 //     (scores are pre-multiplied by scale*log2(e)), updated once per U tokens,
+//   * each thread's K / V chunks reach it through a ring of S steps in shared
+//     memory, copied by cp.async S - 1 steps ahead: the loads of later steps
+//     stay in flight while this one is computed (the registers of wide groups
+//     leave two CTAs per SM, too few loads in flight to cover HBM latency
+//     otherwise); each thread reads back only its own copies,
 //   * lane groups, then warps, are merged with the usual (m, l) rescaling,
 //   * with more than one split the unnormalised partial (m, l, acc) goes to the
 //     workspace and decode_combine_kernel forms the final output.
@@ -19,6 +24,33 @@
 #include "launch.h"
 
 namespace pagedkv {
+
+namespace {
+
+// 16-byte cp.async that bypasses L1; src_bytes 0 writes zeros and reads nothing.
+__device__ __forceinline__ void stage16(void *dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void stage_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int Pending>
+__device__ __forceinline__ void stage_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(Pending) : "memory");
+}
+
+}  // namespace
+
+// Steps of K / V rows staged ahead through shared memory: as many as keep the
+// kernel's static shared memory (this ring plus the merge buffers,
+// 16 * GMAX * (D + 2) bytes) within 48 KiB, between 2 and 4.
+template <int D, int GMAX, int U>
+constexpr int simt_stages() {
+  constexpr int free_bytes = 48 * 1024 - 16 * GMAX * (D + 2) - 512;
+  constexpr int s = free_bytes / (U * 2 * 128 * 16);
+  return s < 2 ? 2 : s > 4 ? 4 : s;
+}
 
 template <typename T, int D, int GMAX, int U>
 __global__ void __launch_bounds__(128)
@@ -82,26 +114,87 @@ decode_simt_kernel(const DecodeParams p) {
   const int32_t *bt = p.bt + (int64_t)seq * p.bt_s;
   const int my = warp * TPW + lg;
 
-  for (int base = t0; base < t1; base += STRIDE * U) {
+  // Groups of two or more query heads hold enough registers that only two
+  // CTAs fit per SM: their K / V rows come through the shared-memory ring.
+  // Single-head groups keep eight CTAs per SM on registers alone, which the
+  // ring's registers and shared memory would cut (measured slower), so they
+  // load straight into registers, one step at a time.
+  constexpr bool kStaged = GMAX >= 2;
+  constexpr int S = kStaged ? simt_stages<D, GMAX, U>() : 2;
+  __shared__ __align__(16) uint4 ring[S][2 * U][NW * 32];  // [step % S][K u | V u][thread]
+  uint32_t vmask = 0;  // bit (step % S) * U + u: token u of that step is in range
+  const int nsteps = t1 > t0 ? (t1 - t0 + STRIDE * U - 1) / (STRIDE * U) : 0;
+  // Element offset of token t's row in the pool; false past the context or
+  // for a block id out of range (flagged).
+  auto locate = [&](int t, int64_t &o) -> bool {
+    o = 0;
+    if (t >= t1) return false;
+    const int lb = t / p.block_size;
+    const int off = t - lb * p.block_size;
+    const int blk = __ldg(bt + lb);
+    if (blk < 0 || (int64_t)blk >= p.num_blocks) {
+      set_error(p.err, PAGEDKV_EFLAG_BLOCK_ID_RANGE);
+      return false;
+    }
+    o = ((int64_t)blk * p.block_size + off) * row_elems;
+    return true;
+  };
+  // Copies of step i into ring slot i % S; one commit group per step, empty
+  // past the last step, so that the group count stays uniform.
+  auto issue = [&](int i) {
+    if (i < nsteps) {
+      const int st = i % S;
+      const int base = t0 + i * STRIDE * U;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        int64_t o;
+        const bool ok = locate(base + u * STRIDE + my, o);
+        stage16(&ring[st][u][threadIdx.x], kb + o, ok ? 16u : 0u);
+        stage16(&ring[st][U + u][threadIdx.x], vb + o, ok ? 16u : 0u);
+        const uint32_t bit = 1u << (st * U + u);
+        vmask = ok ? (vmask | bit) : (vmask & ~bit);
+      }
+    }
+    stage_commit();
+  };
+  if constexpr (kStaged) {
+#pragma unroll
+    for (int i = 0; i < S - 1; ++i) issue(i);
+  }
+
+  for (int step = 0; step < nsteps; ++step) {
     uint4 kr[U], vr[U];
     bool valid[U];
+    if constexpr (kStaged) {
+      stage_wait<S - 2>();  // the group of this step has landed
+      const int st = step % S;
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int t = base + u * STRIDE + my;
-      valid[u] = t < t1;
-      kr[u] = make_uint4(0u, 0u, 0u, 0u);
-      vr[u] = kr[u];
-      if (valid[u]) {
-        const int lb = t / p.block_size;
-        const int off = t - lb * p.block_size;
-        const int blk = __ldg(bt + lb);
-        if (blk < 0 || (int64_t)blk >= p.num_blocks) {
-          set_error(p.err, PAGEDKV_EFLAG_BLOCK_ID_RANGE);
-          valid[u] = false;
-        } else {
-          const int64_t o = ((int64_t)blk * p.block_size + off) * row_elems;
-          kr[u] = ldg_stream16(kb + o);
-          vr[u] = ldg_stream16(vb + o);
+      for (int u = 0; u < U; ++u) {
+        kr[u] = ring[st][u][threadIdx.x];
+        vr[u] = ring[st][U + u][threadIdx.x];
+        valid[u] = (vmask >> (st * U + u)) & 1u;
+      }
+      issue(step + S - 1);  // into the slot the previous step read
+    } else {
+      const int base = t0 + step * STRIDE * U;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int t = base + u * STRIDE + my;
+        valid[u] = t < t1;
+        kr[u] = make_uint4(0u, 0u, 0u, 0u);
+        vr[u] = kr[u];
+        if (valid[u]) {
+          const int lb = t / p.block_size;
+          const int off = t - lb * p.block_size;
+          const int blk = __ldg(bt + lb);
+          if (blk < 0 || (int64_t)blk >= p.num_blocks) {
+            set_error(p.err, PAGEDKV_EFLAG_BLOCK_ID_RANGE);
+            valid[u] = false;
+          } else {
+            const int64_t o = ((int64_t)blk * p.block_size + off) * row_elems;
+            kr[u] = ldg_stream16(kb + o);
+            vr[u] = ldg_stream16(vb + o);
+          }
         }
       }
     }
@@ -155,6 +248,8 @@ decode_simt_kernel(const DecodeParams p) {
       m[g] = mx;
     }
   }
+
+  if constexpr (kStaged) stage_wait<0>();  // the trailing groups are empty; nothing stays in flight
 
   // Merge the lane groups of each warp (lanes with equal li hold equal dims).
 #pragma unroll
