@@ -1,7 +1,7 @@
 // Paged GQA decode attention on CUDA cores (sm_100a), split-K over the context.
 //
-// Serves the shapes the tcgen05 kernel is not built for: head_dim 32 or 256,
-// block_size below 8 or not a power of two, GQA groups above 16.
+// Serves the shapes the tcgen05 kernel is not built for: block sizes below 8,
+// above 128 or not a power of two (head_dim 32, 64, 128 or 256, any group).
 //
 // Algorithm (restates engine/kernels/paged_attention.py:508-631, the batched
 // online-softmax kernel, with its grid changed from one program per QUERY head
