@@ -13,7 +13,7 @@ the whole random-init model (BASELINE config 5's architecture) over a short
 saturated trace per GPU.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload cfg1|cfg2|cfg3|cfg4|cfg4-cow|cfg5|ops|d256] [--gqa G]
+                  [--workload cfg1|cfg2|cfg3|cfg4|cfg4-cow|cfg5|ops|d256|cuda-core] [--gqa G]
                   [--layers L] [--model-requests R]
 
 Extra workloads (not the headline): ``cfg1`` = BASELINE config 1 (the
@@ -26,7 +26,9 @@ same with each sequence's last block shared by its group when the step
 starts and copied to the sequence's private block (all layers) before its
 append; ``cfg5`` = config 5 alone (``--requests`` at ``--rate`` per GPU);
 ``ops`` = the pool-write kernels alone; ``d256`` = the head_dim-256 mode
-(64 x 2048 tokens, 8 query / 4 kv heads; not a BASELINE config).
+(64 x 2048 tokens, 8 query / 4 kv heads; not a BASELINE config);
+``cuda-core`` = the CUDA-core decode kernel alone, which serves the block
+sizes the tensor-core kernel does not take (here block_size 4).
 
 N > 1 runs under torchrun, one process per GPU; sequences are sharded
 data-parallel (each rank owns its own pools, weak scaling) and nothing
@@ -1411,13 +1413,68 @@ def run_ops(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_cuda_core(args) -> None:
+    """The CUDA-core decode kernel (block sizes below 8 or not a power of two)
+    on five shapes at block_size 4, 2048-token contexts, pools larger than L2.
+    Eager calls of the public batched entry point, K calls between CUDA
+    events; algorithmic bytes = the K and V rows read."""
+    import pagedkv
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("--workload cuda-core runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pp = ROOT / "MEASURED_PEAKS.json"
+    peak = float(json.loads(pp.read_text()).get("hbm_gbs", 6650.0)) if pp.exists() else 6650.0
+    steps = min(args.steps, 50)
+    results = {}
+    for n, ctx, hkv, g, d, bs in ((128, 2048, 8, 7, 128, 4), (128, 2048, 8, 2, 128, 4), (128, 2048, 8, 1, 128, 4),
+                                  (256, 2048, 2, 7, 64, 4), (64, 2048, 4, 4, 256, 4)):
+        nbk = n * ctx // bs
+        gen = torch.Generator(device=dev).manual_seed(0)
+        k = torch.randn(nbk, bs, hkv, d, generator=gen, device=dev, dtype=torch.float16)
+        v = torch.randn(nbk, bs, hkv, d, generator=gen, device=dev, dtype=torch.float16)
+        q = torch.randn(n, hkv * g, d, generator=gen, device=dev, dtype=torch.float16)
+        tables = torch.randperm(nbk, generator=gen, device=dev).to(torch.int32).view(n, ctx // bs)
+        lens = torch.full((n,), ctx, dtype=torch.int32, device=dev)
+
+        def call():
+            return pagedkv.paged_attention_decode_batched(q, k, v, tables, lens, d ** -0.5)
+
+        for _ in range(max(3, args.warmup)):
+            call()
+        if pagedkv.last_decode_launch_info()[1] != "simt":
+            raise SystemExit("--workload cuda-core: the shape did not run on the CUDA-core kernel")
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            call()
+        b.record()
+        torch.cuda.synchronize(dev)
+        us = a.elapsed_time(b) / steps * 1e3
+        nbytes = n * ctx * hkv * d * 2 * 2
+        gbs = nbytes / (us * 1e-6) / 1e9
+        results[f"d{d}_hkv{hkv}_gqa{g}_bs{bs}"] = {
+            "us": round(us, 1), "bytes": nbytes, "GB/s": round(gbs, 1),
+            "frac_of_measured_hbm": round(gbs / peak, 4), "shape": f"{n} seqs x {ctx} tokens"}
+        del k, v, q, tables
+        torch.cuda.empty_cache()
+    print(json.dumps({
+        "metric": "CUDA-core decode kernel: us per call and GB/s", "workload": "cuda-core", "n_gpus": 1,
+        "steps": steps, "warmup": args.warmup, "peak_hbm_gbs": peak,
+        "timing": "eager calls of paged_attention_decode_batched (decode + split combine), CUDA events; "
+                  "pools exceed L2", "data": "synthetic", "shapes": results}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg4-cow", "cfg5", "cfg5l", "ops", "d256"],
+    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg4-cow", "cfg5", "cfg5l", "ops", "d256",
+                                           "cuda-core"],
                     default="cfg2")
     ap.add_argument("--requests", type=int, default=2000, help="cfg5: requests per GPU")
     ap.add_argument("--rate", type=float, default=32.0, help="cfg5: Poisson arrival rate per GPU (req/s)")
@@ -1447,6 +1504,8 @@ def main() -> None:
         run_model(args)
     elif args.workload == "ops":
         run_ops(args)
+    elif args.workload == "cuda-core":
+        run_cuda_core(args)
     else:
         run_ours(args)
 
