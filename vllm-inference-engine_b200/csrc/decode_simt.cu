@@ -124,35 +124,45 @@ decode_simt_kernel(const DecodeParams p) {
   __shared__ __align__(16) uint4 ring[S][2 * U][NW * 32];  // [step % S][K u | V u][thread]
   uint32_t vmask = 0;  // bit (step % S) * U + u: token u of that step is in range
   const int nsteps = t1 > t0 ? (t1 - t0 + STRIDE * U - 1) / (STRIDE * U) : 0;
-  // Element offset of token t's row in the pool; false past the context or
-  // for a block id out of range (flagged).
-  auto locate = [&](int t, int64_t &o) -> bool {
-    o = 0;
-    if (t >= t1) return false;
-    const int lb = t / p.block_size;
-    const int off = t - lb * p.block_size;
-    const int blk = __ldg(bt + lb);
-    if (blk < 0 || (int64_t)blk >= p.num_blocks) {
-      set_error(p.err, PAGEDKV_EFLAG_BLOCK_ID_RANGE);
-      return false;
-    }
-    o = ((int64_t)blk * p.block_size + off) * row_elems;
-    return true;
-  };
   // Copies of step i into ring slot i % S; one commit group per step, empty
-  // past the last step, so that the group count stays uniform.
+  // past the last step, so that the group count stays uniform. issue() is
+  // called for i = 0, 1, 2, ... in order, so each token's logical block and
+  // offset advance by a fixed amount per call instead of a division.
+  int nt[U], nlb[U], noff[U];  // the next step's token, block and offset per u
+  const int adv_b = (STRIDE * U) / p.block_size, adv_o = (STRIDE * U) - adv_b * p.block_size;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    nt[u] = t0 + u * STRIDE + my;
+    nlb[u] = nt[u] / p.block_size;
+    noff[u] = nt[u] - nlb[u] * p.block_size;
+  }
   auto issue = [&](int i) {
     if (i < nsteps) {
       const int st = i % S;
-      const int base = t0 + i * STRIDE * U;
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        int64_t o;
-        const bool ok = locate(base + u * STRIDE + my, o);
+        bool ok = nt[u] < t1;
+        int64_t o = 0;
+        if (ok) {
+          const int blk = __ldg(bt + nlb[u]);
+          if (blk < 0 || (int64_t)blk >= p.num_blocks) {
+            set_error(p.err, PAGEDKV_EFLAG_BLOCK_ID_RANGE);
+            ok = false;
+          } else {
+            o = ((int64_t)blk * p.block_size + noff[u]) * row_elems;
+          }
+        }
         stage16(&ring[st][u][threadIdx.x], kb + o, ok ? 16u : 0u);
         stage16(&ring[st][U + u][threadIdx.x], vb + o, ok ? 16u : 0u);
         const uint32_t bit = 1u << (st * U + u);
         vmask = ok ? (vmask | bit) : (vmask & ~bit);
+        nt[u] += STRIDE * U;
+        nlb[u] += adv_b;
+        noff[u] += adv_o;
+        if (noff[u] >= p.block_size) {
+          noff[u] -= p.block_size;
+          ++nlb[u];
+        }
       }
     }
     stage_commit();
@@ -234,10 +244,13 @@ decode_simt_kernel(const DecodeParams p) {
         mx = fmaxf(mx, s[u][g]);
       }
       if (mx == kNegInf) continue;  // no valid token seen yet by this lane group
-      const float alpha = exp2f(m[g] - mx);
-      l[g] *= alpha;
+      // Rescale only when the max moved: otherwise the factor is exp2(0) = 1.
+      if (mx > m[g]) {
+        const float alpha = exp2f(m[g] - mx);
+        l[g] *= alpha;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[g][e] *= alpha;
+        for (int e = 0; e < 8; ++e) acc[g][e] *= alpha;
+      }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const float pr = exp2f(s[u][g] - mx);
